@@ -1,0 +1,277 @@
+// extern "C" entry points of libcarekv_b200.so: argument validation, buffer
+// layout and launch.  See include/carekv_b200.h for the contract of each.
+#include <cmath>
+#include <cstring>
+
+#include "common.cuh"
+#include "internal.h"
+
+using namespace carekv;
+
+namespace {
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+int validate_config(const carekv_config_t* c) {
+  if (c == nullptr) return CAREKV_ERR_INVALID_ARG;
+  if (c->num_layers < 1 || c->num_kv_heads < 1 || c->num_heads < 1) return CAREKV_ERR_INVALID_ARG;
+  if (c->num_heads % c->num_kv_heads != 0) return CAREKV_ERR_INVALID_ARG;
+  const int qn = c->num_heads / c->num_kv_heads;
+  if (qn != 1 && qn != 2 && qn != 4 && qn != 8) return CAREKV_ERR_UNSUPPORTED;
+  if (c->head_dim != 64 && c->head_dim != 128) return CAREKV_ERR_UNSUPPORTED;
+  if (c->page_size != kPage) return CAREKV_ERR_UNSUPPORTED;
+  if (c->max_pages < 8 || c->max_pages % 8 != 0) return CAREKV_ERR_INVALID_ARG;
+  if (c->base_bits < 2 || c->base_bits > 4) return CAREKV_ERR_INVALID_ARG;
+  if (c->group_size <= 0 || c->head_dim % c->group_size != 0 || c->group_size % 8 != 0) return CAREKV_ERR_INVALID_ARG;
+  if (c->head_dim / c->group_size > 4) return CAREKV_ERR_UNSUPPORTED;
+  if (c->k_channel_group != 32) return CAREKV_ERR_UNSUPPORTED;
+  if (c->v_token_block <= 0 || kPage % c->v_token_block != 0) return CAREKV_ERR_INVALID_ARG;
+  const int C = c->head_dim / c->k_channel_group, NV = kPage / c->v_token_block;
+  if (C + NV > 8 || c->v_token_block * c->head_dim / 2 > 256) return CAREKV_ERR_UNSUPPORTED;
+  if (c->residual_bits != 4) return CAREKV_ERR_UNSUPPORTED;
+  if (c->sketch_dim < 0 || c->sketch_dim > 64) return CAREKV_ERR_INVALID_ARG;
+  if (c->scale_mode < CAREKV_SCALE_INT8 || c->scale_mode > CAREKV_SCALE_F32) return CAREKV_ERR_INVALID_ARG;
+  if (c->k_slots_per_page < 0 || c->k_slots_per_page > C) return CAREKV_ERR_INVALID_ARG;
+  if (c->v_slots_per_page < 0 || c->v_slots_per_page > NV) return CAREKV_ERR_INVALID_ARG;
+  return CAREKV_OK;
+}
+
+int validate_cache(const carekv_config_t* c, const carekv_cache_t* k) {
+  if (k == nullptr || k->batch < 1) return CAREKV_ERR_INVALID_ARG;
+  if (!k->k_codes || !k->v_codes || !k->k_scale || !k->v_scale || !k->valid || !k->num_pages || !k->v_norm2 ||
+      !k->k_err || !k->v_err || !k->slot_counter || !k->error_flag)
+    return CAREKV_ERR_INVALID_ARG;
+  if (c->scale_mode == CAREKV_SCALE_INT8 && (!k->k_master || !k->v_master)) return CAREKV_ERR_INVALID_ARG;
+  if (c->k_slots_per_page > 0 && (!k->k_slot_group || !k->k_slot_data || !k->k_slot_scale || !k->k_slot_id))
+    return CAREKV_ERR_INVALID_ARG;
+  if (c->v_slots_per_page > 0 && (!k->v_slot_block || !k->v_slot_data || !k->v_slot_scale || !k->v_slot_id))
+    return CAREKV_ERR_INVALID_ARG;
+  return CAREKV_OK;
+}
+
+int validate_range(const carekv_cache_t* k, int32_t layer, int32_t seq_begin, int32_t seq_count,
+                   const carekv_config_t* c) {
+  if (layer < 0 || layer >= c->num_layers) return CAREKV_ERR_INVALID_ARG;
+  if (seq_begin < 0 || seq_count < 0 || seq_begin + seq_count > k->batch) return CAREKV_ERR_INVALID_ARG;
+  return CAREKV_OK;
+}
+
+int validate_dtype(int32_t dt) {
+  return (dt == CAREKV_F32 || dt == CAREKV_F16 || dt == CAREKV_BF16) ? CAREKV_OK : CAREKV_ERR_INVALID_ARG;
+}
+
+int cuda_status(cudaError_t e) { return e == cudaSuccess ? CAREKV_OK : CAREKV_ERR_CUDA; }
+
+#define CHECK(x)                      \
+  do {                                \
+    const int _s = (x);               \
+    if (_s != CAREKV_OK) return _s;   \
+  } while (0)
+
+}  // namespace
+
+extern "C" {
+
+int carekv_abi_version(void) { return CAREKV_ABI_VERSION; }
+
+const char* carekv_status_string(int status) {
+  switch (status) {
+    case CAREKV_OK: return "ok";
+    case CAREKV_ERR_INVALID_ARG: return "invalid argument";
+    case CAREKV_ERR_UNSUPPORTED: return "unsupported configuration";
+    case CAREKV_ERR_CACHE_FULL: return "KV cache is full";
+    case CAREKV_ERR_CUDA: return "CUDA error";
+    case CAREKV_ERR_WORKSPACE: return "workspace too small";
+    case CAREKV_ERR_DEVICE_CHECK: return "device-side check failed";
+    default: return "unknown status";
+  }
+}
+
+int carekv_cache_layout(const carekv_config_t* cfg, int32_t batch, size_t sizes[CAREKV_NUM_BUFFERS]) {
+  CHECK(validate_config(cfg));
+  if (batch < 1 || sizes == nullptr) return CAREKV_ERR_INVALID_ARG;
+  const Dims d = make_dims(*cfg);
+  const size_t pages = static_cast<size_t>(batch) * d.L * d.H * d.P;
+  const size_t rows = pages * kPage;
+  size_t i = 0;
+  sizes[i++] = rows * d.R;                                   // k_codes
+  sizes[i++] = rows * d.R;                                   // v_codes
+  sizes[i++] = rows * d.G * d.scale_elem;                    // k_scale
+  sizes[i++] = rows * d.G * d.scale_elem;                    // v_scale
+  sizes[i++] = cfg->scale_mode == CAREKV_SCALE_INT8 ? pages * 2 : 0;  // k_master
+  sizes[i++] = cfg->scale_mode == CAREKV_SCALE_INT8 ? pages * 2 : 0;  // v_master
+  sizes[i++] = pages * 4;                                    // valid
+  sizes[i++] = static_cast<size_t>(batch) * d.L * d.H * 4;   // num_pages
+  sizes[i++] = pages * 4;                                    // v_norm2
+  sizes[i++] = pages * d.SK;                                 // k_slot_group
+  sizes[i++] = pages * d.SK * d.kslot_bytes;                 // k_slot_data
+  sizes[i++] = pages * d.SK * 2;                             // k_slot_scale
+  sizes[i++] = pages * d.SK * 4;                             // k_slot_id
+  sizes[i++] = pages * d.SV;                                 // v_slot_block
+  sizes[i++] = pages * d.SV * d.vslot_bytes;                 // v_slot_data
+  sizes[i++] = pages * d.SV * 2;                             // v_slot_scale
+  sizes[i++] = pages * d.SV * 4;                             // v_slot_id
+  sizes[i++] = pages * d.C * 2;                              // k_err
+  sizes[i++] = pages * d.NV * 2;                             // v_err
+  sizes[i++] = pages * d.C * d.sketch * 2;                   // k_sketch
+  sizes[i++] = static_cast<size_t>(batch) * 2 * 4;           // slot_counter
+  sizes[i++] = static_cast<size_t>(d.L) * d.H * 2 * 8;       // read_counter
+  sizes[i++] = 4;                                            // error_flag
+  return CAREKV_OK;
+}
+
+int carekv_cache_init(const carekv_config_t* cfg, const carekv_cache_t* cache, void* stream) {
+  CHECK(validate_config(cfg));
+  CHECK(validate_cache(cfg, cache));
+  size_t sz[CAREKV_NUM_BUFFERS];
+  CHECK(carekv_cache_layout(cfg, cache->batch, sz));
+  void* ptrs[CAREKV_NUM_BUFFERS] = {
+      cache->k_codes,      cache->v_codes,      cache->k_scale,      cache->v_scale,     cache->k_master,
+      cache->v_master,     cache->valid,        cache->num_pages,    cache->v_norm2,     cache->k_slot_group,
+      cache->k_slot_data,  cache->k_slot_scale, cache->k_slot_id,    cache->v_slot_block, cache->v_slot_data,
+      cache->v_slot_scale, cache->v_slot_id,    cache->k_err,        cache->v_err,       cache->k_sketch,
+      cache->slot_counter, cache->read_counter, cache->error_flag};
+  // slot tables start empty (-1); everything else starts at zero
+  const bool minus_one[CAREKV_NUM_BUFFERS] = {false, false, false, false, false, false, false, false,
+                                              false, true,  false, false, true,  true,  false, false,
+                                              true,  false, false, false, false, false, false};
+  cudaStream_t st = as_stream(stream);
+  for (int i = 0; i < CAREKV_NUM_BUFFERS; ++i) {
+    if (ptrs[i] == nullptr || sz[i] == 0) continue;
+    CHECK(cuda_status(cudaMemsetAsync(ptrs[i], minus_one[i] ? 0xFF : 0, sz[i], st)));
+  }
+  return CAREKV_OK;
+}
+
+int carekv_quantize(const void* x, int8_t* codes, void* scale, int64_t rows, int32_t D, int32_t bits,
+                    int32_t group_size, int32_t dtype, void* stream) {
+  if (!x || !codes || !scale || rows < 0 || D <= 0 || group_size <= 0 || D % group_size) return CAREKV_ERR_INVALID_ARG;
+  if (bits < 2 || bits > 4) return CAREKV_ERR_INVALID_ARG;
+  CHECK(validate_dtype(dtype));
+  return cuda_status(launch_quantize(x, codes, scale, rows, D, bits, group_size, dtype, as_stream(stream)));
+}
+
+int carekv_dequantize(const int8_t* codes, const void* scale, void* out, int64_t rows, int32_t D,
+                      int32_t group_size, int32_t dtype, void* stream) {
+  if (!codes || !scale || !out || rows < 0 || D <= 0 || group_size <= 0 || D % group_size) return CAREKV_ERR_INVALID_ARG;
+  CHECK(validate_dtype(dtype));
+  return cuda_status(launch_dequantize(codes, scale, out, rows, D, group_size, dtype, as_stream(stream)));
+}
+
+int carekv_pack_codes(const int8_t* codes, uint8_t* packed, int64_t rows, int32_t D, int32_t bits, void* stream) {
+  if (!codes || !packed || rows < 0 || bits < 2 || bits > 4) return CAREKV_ERR_INVALID_ARG;
+  if (D <= 0 || (bits == 3 && D % 8) || (bits == 2 && D % 4) || (bits == 4 && D % 2)) return CAREKV_ERR_INVALID_ARG;
+  return cuda_status(launch_pack(codes, packed, rows, D, bits, as_stream(stream)));
+}
+
+int carekv_unpack_codes(const uint8_t* packed, int8_t* codes, int64_t rows, int32_t D, int32_t bits, void* stream) {
+  if (!codes || !packed || rows < 0 || bits < 2 || bits > 4) return CAREKV_ERR_INVALID_ARG;
+  if (D <= 0 || (bits == 3 && D % 8) || (bits == 2 && D % 4) || (bits == 4 && D % 2)) return CAREKV_ERR_INVALID_ARG;
+  return cuda_status(launch_unpack(packed, codes, rows, D, bits, as_stream(stream)));
+}
+
+int carekv_pack_4bit(const float* x, uint8_t* packed, uint16_t* scale_f16, int64_t n, int32_t numel, void* stream) {
+  if (!x || !packed || !scale_f16 || n < 0 || numel <= 0 || numel % 2) return CAREKV_ERR_INVALID_ARG;
+  return cuda_status(launch_pack4(x, packed, scale_f16, n, numel, as_stream(stream)));
+}
+
+int carekv_unpack_4bit(const uint8_t* packed, const uint16_t* scale_f16, float* out, int64_t n, int32_t numel,
+                       void* stream) {
+  if (!out || !packed || !scale_f16 || n < 0 || numel <= 0 || numel % 2) return CAREKV_ERR_INVALID_ARG;
+  return cuda_status(launch_unpack4(packed, scale_f16, out, n, numel, as_stream(stream)));
+}
+
+static int validate_store_params(const carekv_config_t* cfg, const carekv_store_params_t* p) {
+  if (p == nullptr) return CAREKV_ERR_INVALID_ARG;
+  CHECK(validate_dtype(p->input_dtype));
+  const int C = cfg->head_dim / cfg->k_channel_group, NV = kPage / cfg->v_token_block;
+  if (p->k_budget < 0 || p->v_budget < 0) return CAREKV_ERR_INVALID_ARG;
+  if (p->joint_budget > 0) {
+    if (cfg->k_slots_per_page < std::min(p->joint_budget, C) || cfg->v_slots_per_page < std::min(p->joint_budget, NV))
+      return CAREKV_ERR_INVALID_ARG;
+  } else if (std::min(p->k_budget, C) > cfg->k_slots_per_page || std::min(p->v_budget, NV) > cfg->v_slots_per_page) {
+    return CAREKV_ERR_INVALID_ARG;
+  }
+  return CAREKV_OK;
+}
+
+int carekv_prefill_store(const carekv_config_t* cfg, const carekv_cache_t* cache, int32_t layer, const void* K,
+                         const void* V, int32_t T, int32_t seq_begin, int32_t seq_count,
+                         const carekv_store_params_t* params, const float* sketch_proj, void* stream) {
+  CHECK(validate_config(cfg));
+  CHECK(validate_cache(cfg, cache));
+  CHECK(validate_range(cache, layer, seq_begin, seq_count, cfg));
+  CHECK(validate_store_params(cfg, params));
+  if (T < 0 || (T > 0 && (!K || !V))) return CAREKV_ERR_INVALID_ARG;
+  if ((T + kPage - 1) / kPage > cfg->max_pages) return CAREKV_ERR_CACHE_FULL;
+  if (cfg->sketch_dim > 0 && cache->k_sketch && !sketch_proj) return CAREKV_ERR_INVALID_ARG;
+  return cuda_status(launch_prefill_store(*cfg, *cache, layer, K, V, T, seq_begin, seq_count, *params, sketch_proj,
+                                          as_stream(stream)));
+}
+
+int carekv_append(const carekv_config_t* cfg, const carekv_cache_t* cache, int32_t layer, const void* k,
+                  const void* v, int32_t seq_begin, int32_t seq_count, const carekv_store_params_t* params,
+                  const float* sketch_proj, int32_t may_fill_page, void* stream) {
+  CHECK(validate_config(cfg));
+  CHECK(validate_cache(cfg, cache));
+  CHECK(validate_range(cache, layer, seq_begin, seq_count, cfg));
+  CHECK(validate_store_params(cfg, params));
+  if (seq_count > 0 && (!k || !v)) return CAREKV_ERR_INVALID_ARG;
+  if (cfg->sketch_dim > 0 && cache->k_sketch && !sketch_proj) return CAREKV_ERR_INVALID_ARG;
+  return cuda_status(launch_append(*cfg, *cache, layer, k, v, seq_begin, seq_count, *params, sketch_proj,
+                                   may_fill_page != 0, as_stream(stream)));
+}
+
+int carekv_decode_workspace_bytes(const carekv_config_t* cfg, int32_t seq_count, int32_t max_pages_used,
+                                  size_t* bytes) {
+  CHECK(validate_config(cfg));
+  if (!bytes || seq_count < 0 || max_pages_used < 0 || max_pages_used > cfg->max_pages) return CAREKV_ERR_INVALID_ARG;
+  *bytes = workspace_bytes(*cfg, seq_count, max_pages_used);
+  return CAREKV_OK;
+}
+
+int carekv_decode_attention(const carekv_config_t* cfg, const carekv_cache_t* cache, int32_t layer, const void* q,
+                            void* out, int32_t dtype, int32_t seq_begin, int32_t seq_count, int32_t max_pages_used,
+                            const carekv_route_params_t* params, const float* sketch_proj, void* workspace,
+                            size_t workspace_bytes_, void* stream) {
+  CHECK(validate_config(cfg));
+  CHECK(validate_cache(cfg, cache));
+  CHECK(validate_range(cache, layer, seq_begin, seq_count, cfg));
+  CHECK(validate_dtype(dtype));
+  if (!params || !q || !out || !workspace) return CAREKV_ERR_INVALID_ARG;
+  if (max_pages_used < 0 || max_pages_used > cfg->max_pages) return CAREKV_ERR_INVALID_ARG;
+  if (params->kind < CAREKV_KIND_BOTH || params->kind > CAREKV_KIND_NONE) return CAREKV_ERR_INVALID_ARG;
+  if (params->kind != CAREKV_KIND_NONE) {
+    if (params->budget_mode == 0) {
+      if (params->read_k < 0 || params->read_v < 0 || params->read_k + params->read_v > kMaxSelHost)
+        return CAREKV_ERR_UNSUPPORTED;
+    } else {
+      const double nk = static_cast<double>(max_pages_used) * cfg->k_slots_per_page;
+      const double nv = static_cast<double>(max_pages_used) * cfg->v_slots_per_page;
+      const int bk = params->ratio_k > 0 ? std::max(1, static_cast<int>(nk * params->ratio_k)) : 0;
+      const int bv = params->ratio_v > 0 ? std::max(1, static_cast<int>(nv * params->ratio_v)) : 0;
+      if (bk + bv > kMaxSelHost) return CAREKV_ERR_UNSUPPORTED;
+    }
+    if (!params->kscore_live && (!cache->k_sketch || cfg->sketch_dim <= 0 || !sketch_proj))
+      return CAREKV_ERR_INVALID_ARG;
+  }
+  if (seq_count == 0 || max_pages_used == 0) {
+    if (seq_count == 0) return CAREKV_OK;
+  }
+  return decode_attention(*cfg, *cache, layer, q, out, dtype, seq_begin, seq_count, std::max(1, max_pages_used),
+                          *params, workspace, workspace_bytes_, sketch_proj, as_stream(stream));
+}
+
+int carekv_check_device_errors(const carekv_cache_t* cache, int32_t* flags_out, void* stream) {
+  if (!cache || !cache->error_flag) return CAREKV_ERR_INVALID_ARG;
+  int32_t h = 0;
+  cudaStream_t st = as_stream(stream);
+  CHECK(cuda_status(cudaMemcpyAsync(&h, cache->error_flag, sizeof(int32_t), cudaMemcpyDeviceToHost, st)));
+  CHECK(cuda_status(cudaStreamSynchronize(st)));
+  if (h != 0) CHECK(cuda_status(cudaMemsetAsync(cache->error_flag, 0, sizeof(int32_t), st)));
+  if (flags_out) *flags_out = h;
+  if (h & kErrPageOverflow) return CAREKV_ERR_CACHE_FULL;
+  return h ? CAREKV_ERR_DEVICE_CHECK : CAREKV_OK;
+}
+
+}  // extern "C"

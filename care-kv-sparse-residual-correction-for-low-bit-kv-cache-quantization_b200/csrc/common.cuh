@@ -1,0 +1,216 @@
+// Device helpers shared by the CARE-KV kernels.
+//
+// Numerics follow torch CPU semantics of the reference exactly where the
+// reference's results are integers or bytes (codes, scales, packed rows,
+// slot payloads): every op on an fp16 / bf16 value is computed in fp32 with
+// IEEE division / multiplication (explicit __f*_rn intrinsics, so nvcc
+// never contracts them into an FMA) and rounded back to the storage dtype
+// with round-to-nearest-even.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/carekv_b200.h"
+
+namespace carekv {
+
+constexpr int kPage = 16;            // tokens per page (the only size built)
+constexpr int kErrPageOverflow = 1;  // error_flag bit: page beyond max_pages
+constexpr int kErrBadState = 2;      // error_flag bit: inconsistent page state
+
+// ───────────────────────── dtype conversions ─────────────────────────
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t b) {
+  return __half2float(__ushort_as_half(b));
+}
+__device__ __forceinline__ uint16_t f32_to_f16_bits(float x) {
+  return __half_as_ushort(__float2half_rn(x));
+}
+__device__ __forceinline__ float f16r(float x) { return __half2float(__float2half_rn(x)); }
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Round an fp32 value to activation dtype `dt`, returned as fp32.
+__device__ __forceinline__ float rnd(float x, int dt) {
+  if (dt == CAREKV_F16) return f16r(x);
+  if (dt == CAREKV_BF16) return bf16r(x);
+  return x;
+}
+
+// clamp(min=1e-8) lower bound as torch converts the scalar to the tensor dtype.
+__device__ __forceinline__ float clamp_lo(int dt) {
+  if (dt == CAREKV_F16) return 0.0f;  // 1e-8 underflows to +0 in fp16
+  if (dt == CAREKV_BF16) return bf16r(1e-8f);
+  return 1e-8f;
+}
+
+__device__ __forceinline__ float load_act(const void* p, int64_t i, int dt) {
+  if (dt == CAREKV_F16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  if (dt == CAREKV_BF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void store_act(void* p, int64_t i, float v, int dt) {
+  if (dt == CAREKV_F16) reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  else if (dt == CAREKV_BF16) reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  else reinterpret_cast<float*>(p)[i] = v;
+}
+
+// float -> int8 code the way torch casts after round().clamp(): NaN -> 0.
+__device__ __forceinline__ int8_t to_code(float v) {
+  if (v != v) return 0;
+  return static_cast<int8_t>(static_cast<int>(v));
+}
+
+// ───────────────────────── base quantizer ─────────────────────────
+// One group of `g` values (exact in dtype dt): scale and codes
+// (quantizer.py:31-64).  qmax = 2^(bits-1)-1.
+__device__ __forceinline__ float group_scale(float max_abs, int qmax, int dt) {
+  float m = fmaxf(max_abs, clamp_lo(dt));
+  return rnd(__fdiv_rn(m, static_cast<float>(qmax)), dt);
+}
+__device__ __forceinline__ int8_t quant_code(float x, float scale, int qmax, int dt) {
+  float t = rnd(__fdiv_rn(x, scale), dt);
+  t = rintf(t);
+  t = fminf(fmaxf(t, static_cast<float>(-qmax - 1)), static_cast<float>(qmax));
+  return to_code(t);
+}
+// dequantize: code * scale in fp32, rounded to the scale dtype.
+__device__ __forceinline__ float dequant(int code, float scale, int dt) {
+  return rnd(__fmul_rn(static_cast<float>(code), scale), dt);
+}
+
+// ───────────────────────── packed rows ─────────────────────────
+__host__ __device__ __forceinline__ int row_bytes(int D, int bits) {
+  return bits == 2 ? D / 4 : (bits == 3 ? D * 3 / 8 : D / 2);
+}
+
+// code at channel c of a packed row (quantizer.py:267-301, 327-343)
+__device__ __forceinline__ int unpack_code(const uint8_t* row, int c, int bits) {
+  if (bits == 3) {
+    const uint8_t* w = row + 3 * (c >> 3);
+    uint32_t word = w[0] | (uint32_t(w[1]) << 8) | (uint32_t(w[2]) << 16);
+    int v = (word >> (3 * (c & 7))) & 7;
+    return v >= 4 ? v - 8 : v;
+  } else if (bits == 2) {
+    int v = (row[c >> 2] >> (2 * (c & 3))) & 3;
+    return v >= 2 ? v - 4 : v;
+  } else {
+    int v = (row[c >> 1] >> (4 * (c & 1))) & 15;
+    return v >= 8 ? v - 16 : v;
+  }
+}
+
+// byte j of a packed row from its codes (quantizer.py:257-324)
+__device__ __forceinline__ uint8_t pack_byte(const int8_t* codes, int j, int bits) {
+  if (bits == 3) {
+    int w = j / 3, b = j % 3;
+    uint32_t word = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) word |= (uint32_t(codes[8 * w + i]) & 7u) << (3 * i);
+    return static_cast<uint8_t>((word >> (8 * b)) & 0xFF);
+  } else if (bits == 2) {
+    uint32_t v = 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v |= (uint32_t(codes[4 * j + i]) & 3u) << (2 * i);
+    return static_cast<uint8_t>(v);
+  } else {
+    return static_cast<uint8_t>((uint32_t(codes[2 * j]) & 15u) | ((uint32_t(codes[2 * j + 1]) & 15u) << 4));
+  }
+}
+
+// ───────────────────────── base scales ─────────────────────────
+// Read one stored base scale as the fp16 value the reference dequantizes
+// with (cache.py:713-718): int8 mode fp16(code*master), otherwise the stored
+// scale cast to fp16.
+__device__ __forceinline__ float read_scale(const void* base, int64_t i, int mode, float master) {
+  switch (mode) {
+    case CAREKV_SCALE_INT8:
+      return f16r(__fmul_rn(static_cast<float>(reinterpret_cast<const int8_t*>(base)[i]), master));
+    case CAREKV_SCALE_F16:
+      return __half2float(reinterpret_cast<const __half*>(base)[i]);
+    case CAREKV_SCALE_BF16:
+      return f16r(__bfloat162float(reinterpret_cast<const __nv_bfloat16*>(base)[i]));
+    default:
+      return f16r(reinterpret_cast<const float*>(base)[i]);
+  }
+}
+
+// Store a raw (non-int8) scale in the scale dtype (cache.py:605-606).
+__device__ __forceinline__ void write_raw_scale(void* base, int64_t i, int mode, float s) {
+  if (mode == CAREKV_SCALE_F16) reinterpret_cast<__half*>(base)[i] = __float2half_rn(s);
+  else if (mode == CAREKV_SCALE_BF16) reinterpret_cast<__nv_bfloat16*>(base)[i] = __float2bfloat16_rn(s);
+  else reinterpret_cast<float*>(base)[i] = s;
+}
+
+// int8 scale code against a master (cache.py:601-602, 692-693)
+__device__ __forceinline__ int8_t int8_scale_code(float s, float master) {
+  float t = rintf(__fdiv_rn(s, master));
+  t = fminf(fmaxf(t, -128.0f), 127.0f);
+  return to_code(t);
+}
+
+// ───────────────────────── 4-bit residual slots ─────────────────────────
+__device__ __forceinline__ int nibble_code(float x, float s) {
+  float t = rintf(__fdiv_rn(x, s));
+  t = fminf(fmaxf(t, -8.0f), 7.0f);
+  return static_cast<int>(t);
+}
+__device__ __forceinline__ float unpack_nibble(const uint8_t* payload, int i, float scale) {
+  int v = (payload[i >> 1] >> (4 * (i & 1))) & 15;
+  if (v > 7) v -= 16;
+  return __fmul_rn(static_cast<float>(v), scale);
+}
+
+// ───────────────────────── reductions ─────────────────────────
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// ───────────────────────── arena indexing ─────────────────────────
+struct Dims {
+  int L, H, P, D, R, G, C, NV, SK, SV, kslot_bytes, vslot_bytes, sketch;
+  int bits, gsize, kcg, vtb, scale_mode;
+  int scale_elem;  // bytes per stored base scale
+
+  __host__ __device__ int64_t lhp(int b, int l, int h) const {
+    return (static_cast<int64_t>(b) * L + l) * H + h;
+  }
+  __host__ __device__ int64_t page(int b, int l, int h, int p) const {
+    return lhp(b, l, h) * P + p;
+  }
+};
+
+__host__ __device__ inline Dims make_dims(const carekv_config_t& c) {
+  Dims d;
+  d.L = c.num_layers;
+  d.H = c.num_kv_heads;
+  d.P = c.max_pages;
+  d.D = c.head_dim;
+  d.bits = c.base_bits;
+  d.R = row_bytes(c.head_dim, c.base_bits);
+  d.gsize = c.group_size;
+  d.G = c.head_dim / c.group_size;
+  d.kcg = c.k_channel_group;
+  d.C = c.head_dim / c.k_channel_group;
+  d.vtb = c.v_token_block;
+  d.NV = kPage / c.v_token_block;
+  d.SK = c.k_slots_per_page;
+  d.SV = c.v_slots_per_page;
+  d.kslot_bytes = kPage * c.k_channel_group / 2;
+  d.vslot_bytes = c.v_token_block * c.head_dim / 2;
+  d.sketch = c.sketch_dim;
+  d.scale_mode = c.scale_mode;
+  d.scale_elem = c.scale_mode == CAREKV_SCALE_INT8 ? 1 : (c.scale_mode == CAREKV_SCALE_F32 ? 4 : 2);
+  return d;
+}
+
+}  // namespace carekv

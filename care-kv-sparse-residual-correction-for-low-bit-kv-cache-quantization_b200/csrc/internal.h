@@ -1,0 +1,28 @@
+// Host-side launch functions shared between the translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include "../../include/carekv_b200.h"
+
+namespace carekv {
+cudaError_t launch_quantize(const void* x, int8_t* codes, void* scale, int64_t rows, int D, int bits, int gs, int dt,
+                            cudaStream_t st);
+cudaError_t launch_dequantize(const int8_t* codes, const void* scale, void* out, int64_t rows, int D, int gs, int dt,
+                              cudaStream_t st);
+cudaError_t launch_pack(const int8_t* codes, uint8_t* packed, int64_t rows, int D, int bits, cudaStream_t st);
+cudaError_t launch_unpack(const uint8_t* packed, int8_t* codes, int64_t rows, int D, int bits, cudaStream_t st);
+cudaError_t launch_pack4(const float* x, uint8_t* packed, uint16_t* sc, int64_t n, int numel, cudaStream_t st);
+cudaError_t launch_unpack4(const uint8_t* packed, const uint16_t* sc, float* out, int64_t n, int numel,
+                           cudaStream_t st);
+cudaError_t launch_prefill_store(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* K,
+                                 const void* V, int T, int seq_begin, int seq_count,
+                                 const carekv_store_params_t& prm, const float* sketch_proj, cudaStream_t st);
+cudaError_t launch_append(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* k,
+                          const void* v, int seq_begin, int seq_count, const carekv_store_params_t& prm,
+                          const float* sketch_proj, int may_fill, cudaStream_t st);
+int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* q,
+                     void* out, int dtype, int seq_begin, int seq_count, int p_used,
+                     const carekv_route_params_t& rp, void* ws, size_t ws_bytes, const float* sketch_proj,
+                     cudaStream_t st);
+size_t workspace_bytes(const carekv_config_t& c, int seq_count, int p_used);
+constexpr int kMaxSelHost = 32;
+}  // namespace carekv

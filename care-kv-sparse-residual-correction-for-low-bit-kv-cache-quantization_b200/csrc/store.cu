@@ -1,0 +1,566 @@
+// Quantize-and-pack on append plus per-page residual enumeration and slot
+// storage (kernel K1).
+//
+// Replaces, for the uniform per-group base:
+//   layer.py:204-334      _write_pages_for_kv_head (prefill pages)
+//   layer.py:1028-1146    decode append and the page-full re-store
+//   cache.py:592-701      write_base / append_to_page / int8 page scales
+//   residual_store.py:239-464  ResidualStoreManager.process_page
+//
+// One CTA processes one 16-row page of one (sequence, kv head): rows are
+// staged in shared memory, quantized per group, packed into the reference's
+// row format, the page's int8 scale codes and fp16 master are written, the
+// residual R = X - X_hat is formed in place, and one warp per candidate
+// (K channel group or V token block) computes its error norm, sketch and
+// 4-bit payload.  Thread 0 then ranks the candidates and writes the kept
+// slots in ascending group order.  Slot ids that reproduce the reference's
+// sequential arena allocation are assigned afterwards by a per-sequence scan
+// in (kv head, page) order.
+#include "common.cuh"
+#include "internal.h"
+
+namespace carekv {
+
+struct StoreSmem {
+  // sized for head_dim <= 128, page 16, slot capacity <= 8, 8 candidates
+  float x[2][kPage][128];        // K, V rows, then residuals in place
+  int8_t code[2][kPage][128];
+  float sc[2][kPage][4];         // unquantized group scales (dtype values)
+  float rscale[2][kPage][4];     // scales as read back (fp16 values)
+  float err[8];
+  float s4[8];                   // fp32 4-bit slot scale per candidate
+  uint8_t payload[8][256];
+  float red[2][32];
+  float master[2];
+};
+
+// Page store.  mode 0: rows come from K/V inputs (prefill).  mode 1: rows are
+// rebuilt from the cache's last page (decode page-full store, layer.py:1087-1146).
+template <int MODE>
+__global__ void __launch_bounds__(256) page_store_kernel(
+    carekv_config_t cfg, carekv_cache_t cache, int layer, const void* __restrict__ Kin,
+    const void* __restrict__ Vin, int T, int seq_begin, carekv_store_params_t prm,
+    const float* __restrict__ sketch_proj) {
+  __shared__ StoreSmem sm;
+  const Dims d = make_dims(cfg);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int h = blockIdx.y;
+  const int s = blockIdx.z;
+  const int b = seq_begin + s;
+  const int dt = prm.input_dtype;
+  const int D = d.D;
+  const int64_t lhp = d.lhp(b, layer, h);
+
+  int p, nv;
+  if (MODE == 0) {
+    const int np0 = cache.num_pages[lhp];
+    p = np0 + blockIdx.x;
+    const int t0 = blockIdx.x * kPage;
+    nv = min(kPage, T - t0);
+    if (p >= d.P) {
+      if (tid == 0) atomicOr(cache.error_flag, kErrPageOverflow);
+      return;
+    }
+    // stage rows; padded rows are zero (layer.py:262-271)
+    const int64_t base = ((static_cast<int64_t>(s) * d.H + h) * T + t0) * D;
+    for (int i = tid; i < kPage * D; i += blockDim.x) {
+      const int r = i / D, c = i % D;
+      float kv = 0.f, vv = 0.f;
+      if (r < nv) {
+        kv = load_act(Kin, base + static_cast<int64_t>(r) * D + c, dt);
+        vv = load_act(Vin, base + static_cast<int64_t>(r) * D + c, dt);
+      }
+      sm.x[0][r][c] = kv;
+      sm.x[1][r][c] = vv;
+    }
+  } else {
+    p = cache.num_pages[lhp] - 1;
+    if (p < 0) return;
+    const int64_t pg = lhp * d.P + p;
+    if (cache.valid[pg] != kPage) return;  // only the page this step filled
+    nv = kPage;
+    const float mk = cfg.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(cache.k_master[pg]) : 0.f;
+    const float mv = cfg.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(cache.v_master[pg]) : 0.f;
+    for (int i = tid; i < kPage * D; i += blockDim.x) {
+      const int r = i / D, c = i % D;
+      const int64_t srow = (pg * kPage + r) * d.G + c / d.gsize;
+      const float sk = read_scale(cache.k_scale, srow, d.scale_mode, mk);
+      const float sv = read_scale(cache.v_scale, srow, d.scale_mode, mv);
+      const int ck = unpack_code(cache.k_codes + (pg * kPage + r) * d.R, c, d.bits);
+      const int cv = unpack_code(cache.v_codes + (pg * kPage + r) * d.R, c, d.bits);
+      // K_hat in fp16 (scales are read back as fp16), K_orig := K_hat cast to
+      // the model dtype; R = K_orig - K_hat in the promoted dtype.
+      const float kh = f16r(__fmul_rn(static_cast<float>(ck), sk));
+      const float vh = f16r(__fmul_rn(static_cast<float>(cv), sv));
+      sm.x[0][r][c] = rnd(kh, dt) - kh;  // exact: both fp32-representable
+      sm.x[1][r][c] = rnd(vh, dt) - vh;
+      // fp16 model dtype: promoted dtype is fp16 and rnd() is exact -> 0
+    }
+  }
+  __syncthreads();
+
+  const int64_t pg = lhp * d.P + p;
+  const int qmax = (1 << (d.bits - 1)) - 1;
+
+  if (MODE == 0) {
+    // ── per-group quantization (quantizer.py:31-64) ──
+    for (int task = tid; task < 2 * kPage * d.G; task += blockDim.x) {
+      const int kind = task / (kPage * d.G);
+      const int r = (task / d.G) % kPage;
+      const int g = task % d.G;
+      float mx = 0.f;
+      for (int c = g * d.gsize; c < (g + 1) * d.gsize; ++c) mx = fmaxf(mx, fabsf(sm.x[kind][r][c]));
+      const float scale = group_scale(mx, qmax, dt);
+      sm.sc[kind][r][g] = scale;
+      for (int c = g * d.gsize; c < (g + 1) * d.gsize; ++c)
+        sm.code[kind][r][c] = quant_code(sm.x[kind][r][c], scale, qmax, dt);
+    }
+    __syncthreads();
+    // ── packed rows, all 16 rows (cache.py:636-640) ──
+    for (int i = tid; i < 2 * kPage * d.R; i += blockDim.x) {
+      const int kind = i / (kPage * d.R);
+      const int r = (i / d.R) % kPage;
+      const int j = i % d.R;
+      uint8_t* dst = (kind == 0 ? cache.k_codes : cache.v_codes) + (pg * kPage + r) * d.R + j;
+      *dst = pack_byte(&sm.code[kind][r][0], j, d.bits);
+    }
+    // ── page scales (cache.py:592-606) ──
+    if (d.scale_mode == CAREKV_SCALE_INT8) {
+      for (int kind = 0; kind < 2; ++kind) {
+        float mx = 0.f;
+        for (int i = tid; i < kPage * d.G; i += blockDim.x) mx = fmaxf(mx, fabsf(sm.sc[kind][i / d.G][i % d.G]));
+        mx = warp_max(mx);
+        if (lane == 0) sm.red[kind][warp] = mx;
+      }
+      __syncthreads();
+      if (tid < 2) {
+        float mx = 0.f;
+        for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) mx = fmaxf(mx, sm.red[tid][w]);
+        mx = fmaxf(mx, clamp_lo(dt));
+        const uint16_t mb = f32_to_f16_bits(__fdiv_rn(mx, 127.0f));
+        (tid == 0 ? cache.k_master : cache.v_master)[pg] = mb;
+        sm.master[tid] = f16_bits_to_f32(mb);
+      }
+      __syncthreads();
+      for (int i = tid; i < 2 * kPage * d.G; i += blockDim.x) {
+        const int kind = i / (kPage * d.G);
+        const int r = (i / d.G) % kPage, g = i % d.G;
+        const int8_t c8 = int8_scale_code(sm.sc[kind][r][g], sm.master[kind]);
+        reinterpret_cast<int8_t*>(kind == 0 ? cache.k_scale : cache.v_scale)[(pg * kPage + r) * d.G + g] = c8;
+        sm.rscale[kind][r][g] = f16r(__fmul_rn(static_cast<float>(c8), sm.master[kind]));
+      }
+    } else {
+      for (int i = tid; i < 2 * kPage * d.G; i += blockDim.x) {
+        const int kind = i / (kPage * d.G);
+        const int r = (i / d.G) % kPage, g = i % d.G;
+        void* dst = kind == 0 ? cache.k_scale : cache.v_scale;
+        const int64_t idx = (pg * kPage + r) * d.G + g;
+        write_raw_scale(dst, idx, d.scale_mode, sm.sc[kind][r][g]);
+        sm.rscale[kind][r][g] = read_scale(dst, idx, d.scale_mode, 0.f);
+      }
+    }
+    if (tid == 0) cache.valid[pg] = nv;
+    __syncthreads();
+    // ── residual in place (residual_store.py:271-285) + V_hat norm ──
+    float vn = 0.f;
+    for (int i = tid; i < kPage * D; i += blockDim.x) {
+      const int r = i / D, c = i % D, g = c / d.gsize;
+      if (r < nv) {
+        const float kh = dequant(sm.code[0][r][c], sm.sc[0][r][g], dt);
+        const float vh = dequant(sm.code[1][r][c], sm.sc[1][r][g], dt);
+        sm.x[0][r][c] = rnd(__fsub_rn(sm.x[0][r][c], kh), dt);
+        sm.x[1][r][c] = rnd(__fsub_rn(sm.x[1][r][c], vh), dt);
+        const float vr = f16r(__fmul_rn(static_cast<float>(sm.code[1][r][c]), sm.rscale[1][r][g]));
+        vn = fmaf(vr, vr, vn);
+      } else {
+        sm.x[0][r][c] = 0.f;
+        sm.x[1][r][c] = 0.f;
+      }
+    }
+    vn = warp_sum(vn);
+    if (lane == 0) sm.red[0][warp] = vn;
+    __syncthreads();
+    if (tid == 0) {
+      float t = 0.f;
+      for (int w = 0; w < static_cast<int>(blockDim.x / 32); ++w) t += sm.red[0][w];
+      cache.v_norm2[pg] = t;
+    }
+  }
+  __syncthreads();
+
+  // ── candidates: warp w < C -> K channel group, then V token blocks ──
+  const int ncand = d.C + d.NV;
+  for (int cand = warp; cand < ncand; cand += blockDim.x / 32) {
+    if (cand < d.C) {
+      const int c0 = cand * d.kcg;  // kcg == 32: lane = channel
+      float err = 0.f, colsum = 0.f, mx = 0.f;
+      for (int r = 0; r < kPage; ++r) {
+        const float v = sm.x[0][r][c0 + lane];
+        mx = fmaxf(mx, fabsf(v));
+        if (r < nv) {
+          const float n = sqrtf(warp_sum(v * v));
+          err += n;
+          colsum += v;
+        }
+      }
+      mx = warp_max(mx);
+      if (lane == 0) sm.err[cand] = nv > 0 ? __fdiv_rn(err, static_cast<float>(nv)) : 0.f;
+      const float sc4 = __fdiv_rn(fmaxf(mx, 1e-8f), 7.0f);
+      if (lane == 0) sm.s4[cand] = sc4;
+      // payload: value index i = t*32 + c, byte i/2 (residual_store.py:127-136)
+      for (int j = lane; j < d.kslot_bytes; j += 32) {
+        const int i0 = 2 * j;
+        const int t = i0 / d.kcg, c = i0 % d.kcg;
+        const int lo = nibble_code(sm.x[0][t][c0 + c], sc4);
+        const int hi = nibble_code(sm.x[0][t][c0 + c + 1], sc4);
+        sm.payload[cand][j] = static_cast<uint8_t>((lo & 15) | ((hi & 15) << 4));
+      }
+      // sketch = fp16(mean_t R @ P) (residual_store.py:302-312)
+      if (cache.k_sketch != nullptr && d.sketch > 0) {
+        const float mean = nv > 0 ? __fdiv_rn(colsum, static_cast<float>(nv)) : 0.f;
+        for (int jj = 0; jj < d.sketch; jj += 32) {
+          const int j = jj + lane;
+          float acc = 0.f;
+          for (int c = 0; c < d.kcg; ++c) {
+            const float mc = __shfl_sync(0xffffffffu, mean, c);
+            if (j < d.sketch) acc = fmaf(mc, sketch_proj[c * d.sketch + j], acc);
+          }
+          if (j < d.sketch)
+            cache.k_sketch[(pg * d.C + cand) * d.sketch + j] = f32_to_f16_bits(acc);
+        }
+      }
+    } else {
+      const int vb = cand - d.C;
+      const int t0 = vb * d.vtb;
+      float err = 0.f, mx = 0.f;
+      for (int r = t0; r < t0 + d.vtb; ++r) {
+        float ss = 0.f;
+        for (int c = lane; c < D; c += 32) {
+          const float v = sm.x[1][r][c];
+          ss = fmaf(v, v, ss);
+          mx = fmaxf(mx, fabsf(v));
+        }
+        if (r < nv) err += sqrtf(warp_sum(ss));
+      }
+      mx = warp_max(mx);
+      const int t1 = min(t0 + d.vtb, nv);
+      if (lane == 0) sm.err[cand] = t1 > t0 ? __fdiv_rn(err, static_cast<float>(t1 - t0)) : 0.f;
+      const float sc4 = __fdiv_rn(fmaxf(mx, 1e-8f), 7.0f);
+      if (lane == 0) sm.s4[cand] = sc4;
+      for (int j = lane; j < d.vslot_bytes; j += 32) {
+        const int i0 = 2 * j;
+        const int t = t0 + i0 / D, c = i0 % D;
+        const int lo = nibble_code(sm.x[1][t][c], sc4);
+        const int hi = nibble_code(sm.x[1][t][c + 1], sc4);
+        sm.payload[cand][j] = static_cast<uint8_t>((lo & 15) | ((hi & 15) << 4));
+      }
+    }
+  }
+  __syncthreads();
+
+  // ── selection (residual_store.py:370-423) and slot tables ──
+  if (tid == 0) {
+    int order[8], n_k = 0, n_v = 0, korder[8], vorder[8];
+    const bool pos = prm.sensitivity > 0.f && !prm.store_nothing;
+    // stable descending by error, positive errors only
+    for (int i = 0; i < d.C; ++i)
+      if (pos && sm.err[i] > 0.f) korder[n_k++] = i;
+    for (int i = 0; i < d.NV; ++i)
+      if (pos && sm.err[d.C + i] > 0.f) vorder[n_v++] = d.C + i;
+    for (int a = 1; a < n_k; ++a)
+      for (int q = a; q > 0 && sm.err[korder[q]] > sm.err[korder[q - 1]]; --q) {
+        int t = korder[q]; korder[q] = korder[q - 1]; korder[q - 1] = t;
+      }
+    for (int a = 1; a < n_v; ++a)
+      for (int q = a; q > 0 && sm.err[vorder[q]] > sm.err[vorder[q - 1]]; --q) {
+        int t = vorder[q]; vorder[q] = vorder[q - 1]; vorder[q - 1] = t;
+      }
+    int keep_k = 0, keep_v = 0;
+    if (prm.joint_budget > 0) {
+      // merge K then V stably by error, take joint_budget (residual_store.py:416-418)
+      int ik = 0, iv = 0, n = 0;
+      while (n < prm.joint_budget && (ik < n_k || iv < n_v)) {
+        if (iv >= n_v || (ik < n_k && !(sm.err[vorder[iv]] > sm.err[korder[ik]]))) { ++ik; ++keep_k; }
+        else { ++iv; ++keep_v; }
+        ++n;
+      }
+    } else {
+      keep_k = min(n_k, prm.k_budget);
+      keep_v = min(n_v, prm.v_budget);
+    }
+    keep_k = min(keep_k, d.SK);
+    keep_v = min(keep_v, d.SV);
+    // kept candidates in ascending group order, with their score rank
+    int kr[8], nk = 0;
+    for (int i = 0; i < keep_k; ++i) order[i] = korder[i];
+    for (int cg = 0; cg < d.C; ++cg)
+      for (int i = 0; i < keep_k; ++i)
+        if (order[i] == cg) kr[nk++] = cg | (i << 8);
+    for (int j = 0; j < d.SK; ++j) {
+      const int64_t e = pg * d.SK + j;
+      if (j < nk) {
+        cache.k_slot_group[e] = static_cast<int8_t>(kr[j] & 0xFF);
+        cache.k_slot_scale[e] = f32_to_f16_bits(sm.s4[kr[j] & 0xFF]);
+        cache.k_slot_id[e] = kr[j] >> 8;  // local rank; the scan adds the arena base
+      } else {
+        cache.k_slot_group[e] = -1;
+        cache.k_slot_id[e] = -1;
+      }
+    }
+    int vr[8], nvk = 0;
+    for (int i = 0; i < keep_v; ++i) order[i] = vorder[i];
+    for (int vb = 0; vb < d.NV; ++vb)
+      for (int i = 0; i < keep_v; ++i)
+        if (order[i] == d.C + vb) vr[nvk++] = vb | (i << 8);
+    for (int j = 0; j < d.SV; ++j) {
+      const int64_t e = pg * d.SV + j;
+      if (j < nvk) {
+        cache.v_slot_block[e] = static_cast<int8_t>(vr[j] & 0xFF);
+        cache.v_slot_scale[e] = f32_to_f16_bits(sm.s4[d.C + (vr[j] & 0xFF)]);
+        cache.v_slot_id[e] = vr[j] >> 8;
+      } else {
+        cache.v_slot_block[e] = -1;
+        cache.v_slot_id[e] = -1;
+      }
+    }
+    for (int cg = 0; cg < d.C; ++cg) cache.k_err[pg * d.C + cg] = f32_to_f16_bits(sm.err[cg]);
+    for (int vb = 0; vb < d.NV; ++vb) cache.v_err[pg * d.NV + vb] = f32_to_f16_bits(sm.err[d.C + vb]);
+    sm.red[1][0] = __int_as_float(nk);
+    sm.red[1][1] = __int_as_float(nvk);
+  }
+  __syncthreads();
+  // payload copies of the kept slots
+  const int nk = __float_as_int(sm.red[1][0]);
+  const int nvk = __float_as_int(sm.red[1][1]);
+  for (int j = 0; j < nk; ++j) {
+    const int cg = cache.k_slot_group[pg * d.SK + j];
+    uint8_t* dst = cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes;
+    for (int i = tid; i < d.kslot_bytes; i += blockDim.x) dst[i] = sm.payload[cg][i];
+  }
+  for (int j = 0; j < nvk; ++j) {
+    const int vb = cache.v_slot_block[pg * d.SV + j];
+    uint8_t* dst = cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes;
+    for (int i = tid; i < d.vslot_bytes; i += blockDim.x) dst[i] = sm.payload[d.C + vb][i];
+  }
+}
+
+// Assign reference arena ids: pages of this call in (kv head, page) order,
+// K and V counted separately; then advance the per-sequence counters and,
+// for prefill, the page counts.  One CTA per sequence.
+// MODE 0: pages [np0, np0+n_new) per head (prefill).  MODE 1: the last page
+// of each head when it is full (decode page-full store).
+template <int MODE>
+__global__ void __launch_bounds__(1024) slot_id_scan_kernel(carekv_config_t cfg, carekv_cache_t cache,
+                                                            int layer, int seq_begin, int n_new) {
+  const Dims d = make_dims(cfg);
+  const int b = seq_begin + blockIdx.x;
+  const int tid = threadIdx.x;
+  const int npg = (MODE == 0) ? n_new : 1;
+  const int total = d.H * npg;
+  __shared__ int sk[1024], sv[1024];
+  __shared__ int basek, basev;
+  if (tid == 0) {
+    basek = cache.slot_counter[2 * b];
+    basev = cache.slot_counter[2 * b + 1];
+  }
+  __syncthreads();
+  // each thread owns a contiguous chunk of (head, page) entries
+  const int per = (total + blockDim.x - 1) / blockDim.x;
+  const int lo = tid * per, hi = min(total, lo + per);
+  auto page_of = [&](int e, int64_t& pg) -> bool {
+    const int h = e / npg, i = e % npg;
+    const int64_t lhp = d.lhp(b, layer, h);
+    int p;
+    if (MODE == 0) {
+      p = cache.num_pages[lhp] + i;
+      if (p >= d.P) return false;
+    } else {
+      p = cache.num_pages[lhp] - 1;
+      if (p < 0 || cache.valid[lhp * d.P + p] != kPage) return false;
+    }
+    pg = lhp * d.P + p;
+    return true;
+  };
+  int ck = 0, cv = 0;
+  for (int e = lo; e < hi; ++e) {
+    int64_t pg;
+    if (!page_of(e, pg)) continue;
+    for (int j = 0; j < d.SK; ++j) ck += cache.k_slot_group[pg * d.SK + j] >= 0;
+    for (int j = 0; j < d.SV; ++j) cv += cache.v_slot_block[pg * d.SV + j] >= 0;
+  }
+  sk[tid] = ck;
+  sv[tid] = cv;
+  __syncthreads();
+  // inclusive Hillis-Steele scan
+  for (int off = 1; off < static_cast<int>(blockDim.x); off <<= 1) {
+    const int ak = tid >= off ? sk[tid - off] : 0;
+    const int av = tid >= off ? sv[tid - off] : 0;
+    __syncthreads();
+    sk[tid] += ak;
+    sv[tid] += av;
+    __syncthreads();
+  }
+  int ok = basek + sk[tid] - ck, ov = basev + sv[tid] - cv;
+  for (int e = lo; e < hi; ++e) {
+    int64_t pg;
+    if (!page_of(e, pg)) continue;
+    int nk = 0, nvv = 0;
+    for (int j = 0; j < d.SK; ++j) {
+      if (cache.k_slot_group[pg * d.SK + j] >= 0) {
+        cache.k_slot_id[pg * d.SK + j] += ok;
+        ++nk;
+      }
+    }
+    for (int j = 0; j < d.SV; ++j) {
+      if (cache.v_slot_block[pg * d.SV + j] >= 0) {
+        cache.v_slot_id[pg * d.SV + j] += ov;
+        ++nvv;
+      }
+    }
+    ok += nk;
+    ov += nvv;
+  }
+  __syncthreads();
+  if (tid == blockDim.x - 1) {
+    cache.slot_counter[2 * b] = basek + sk[tid];
+    cache.slot_counter[2 * b + 1] = basev + sv[tid];
+  }
+  if (MODE == 0) {
+    __syncthreads();
+    for (int h = tid; h < d.H; h += blockDim.x) {
+      const int64_t lhp = d.lhp(b, layer, h);
+      cache.num_pages[lhp] = min(d.P, cache.num_pages[lhp] + n_new);
+    }
+  }
+}
+
+// Decode append of one row per (sequence, kv head) (layer.py:1028-1085,
+// cache.py:656-701).  One warp per (sequence, kv head).
+__global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_cache_t cache, int layer,
+                                                    const void* __restrict__ kin,
+                                                    const void* __restrict__ vin, int seq_begin,
+                                                    carekv_store_params_t prm) {
+  const Dims d = make_dims(cfg);
+  const int lane = threadIdx.x;
+  const int h = blockIdx.x, s = blockIdx.y, b = seq_begin + s;
+  const int dt = prm.input_dtype;
+  const int D = d.D;
+  const int64_t lhp = d.lhp(b, layer, h);
+  __shared__ float xs[2][128];
+  __shared__ int8_t cs[2][128];
+  __shared__ float scs[2][4];
+  __shared__ int sh_p, sh_off;
+
+  if (lane == 0) {
+    int np = cache.num_pages[lhp];
+    int p = np - 1;
+    if (p < 0 || cache.valid[lhp * d.P + p] >= kPage) {
+      p = np;
+      if (p >= d.P) {
+        atomicOr(cache.error_flag, kErrPageOverflow);
+        p = -1;
+      } else {
+        cache.num_pages[lhp] = np + 1;
+        const int64_t pg = lhp * d.P + p;
+        cache.valid[pg] = 0;
+        cache.v_norm2[pg] = 0.f;
+        if (cfg.scale_mode == CAREKV_SCALE_INT8) {
+          cache.k_master[pg] = 0;  // a decode-opened page keeps master 0 (cache.py:689-695)
+          cache.v_master[pg] = 0;
+        }
+        for (int j = 0; j < d.SK; ++j) { cache.k_slot_group[pg * d.SK + j] = -1; cache.k_slot_id[pg * d.SK + j] = -1; }
+        for (int j = 0; j < d.SV; ++j) { cache.v_slot_block[pg * d.SV + j] = -1; cache.v_slot_id[pg * d.SV + j] = -1; }
+      }
+    }
+    sh_p = p;
+    sh_off = p >= 0 ? cache.valid[lhp * d.P + p] : 0;
+  }
+  __syncwarp();
+  const int p = sh_p;
+  if (p < 0) return;
+  const int off = sh_off;
+  const int64_t pg = lhp * d.P + p;
+  const int64_t src = (static_cast<int64_t>(s) * d.H + h) * D;
+  for (int c = lane; c < D; c += 32) {
+    xs[0][c] = load_act(kin, src + c, dt);
+    xs[1][c] = load_act(vin, src + c, dt);
+  }
+  __syncwarp();
+  const int qmax = (1 << (d.bits - 1)) - 1;
+  if (lane < 2 * d.G) {
+    const int kind = lane / d.G, g = lane % d.G;
+    float mx = 0.f;
+    for (int c = g * d.gsize; c < (g + 1) * d.gsize; ++c) mx = fmaxf(mx, fabsf(xs[kind][c]));
+    const float sc = group_scale(mx, qmax, dt);
+    scs[kind][g] = sc;
+    for (int c = g * d.gsize; c < (g + 1) * d.gsize; ++c) cs[kind][c] = quant_code(xs[kind][c], sc, qmax, dt);
+  }
+  __syncwarp();
+  for (int j = lane; j < 2 * d.R; j += 32) {
+    const int kind = j / d.R, jj = j % d.R;
+    (kind == 0 ? cache.k_codes : cache.v_codes)[(pg * kPage + off) * d.R + jj] = pack_byte(cs[kind], jj, d.bits);
+  }
+  __shared__ float rs[2][4];
+  if (lane < 2 * d.G) {
+    const int kind = lane / d.G, g = lane % d.G;
+    void* dst = kind == 0 ? cache.k_scale : cache.v_scale;
+    const int64_t idx = (pg * kPage + off) * d.G + g;
+    if (d.scale_mode == CAREKV_SCALE_INT8) {
+      const uint16_t* mp = kind == 0 ? cache.k_master : cache.v_master;
+      const float m = f16_bits_to_f32(mp[pg]);
+      const float mc = fmaxf(m, 1e-8f);  // master.clamp(min=1e-8) in fp32
+      const int8_t c8 = int8_scale_code(scs[kind][g], mc);
+      reinterpret_cast<int8_t*>(dst)[idx] = c8;
+      rs[kind][g] = f16r(__fmul_rn(static_cast<float>(c8), m));
+    } else {
+      write_raw_scale(dst, idx, d.scale_mode, scs[kind][g]);
+      rs[kind][g] = read_scale(dst, idx, d.scale_mode, 0.f);
+    }
+  }
+  __syncwarp();
+  float vn = 0.f;
+  for (int c = lane; c < D; c += 32) {
+    const float vr = f16r(__fmul_rn(static_cast<float>(cs[1][c]), rs[1][c / d.gsize]));
+    vn = fmaf(vr, vr, vn);
+  }
+  vn = warp_sum(vn);
+  if (lane == 0) {
+    cache.v_norm2[pg] += vn;
+    cache.valid[pg] = off + 1;
+  }
+}
+
+}  // namespace carekv
+
+namespace carekv {
+
+cudaError_t launch_prefill_store(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* K,
+                                 const void* V, int T, int seq_begin, int seq_count,
+                                 const carekv_store_params_t& prm, const float* sketch_proj, cudaStream_t st) {
+  const int n_new = (T + kPage - 1) / kPage;
+  if (n_new == 0 || seq_count == 0) return cudaSuccess;
+  dim3 grid(n_new, cfg.num_kv_heads, seq_count);
+  page_store_kernel<0><<<grid, 256, 0, st>>>(cfg, cache, layer, K, V, T, seq_begin, prm, sketch_proj);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  slot_id_scan_kernel<0><<<seq_count, 1024, 0, st>>>(cfg, cache, layer, seq_begin, n_new);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_append(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* k,
+                          const void* v, int seq_begin, int seq_count, const carekv_store_params_t& prm,
+                          const float* sketch_proj, int may_fill, cudaStream_t st) {
+  if (seq_count == 0) return cudaSuccess;
+  dim3 g(cfg.num_kv_heads, seq_count);
+  append_kernel<<<g, 32, 0, st>>>(cfg, cache, layer, k, v, seq_begin, prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || !may_fill) return e;
+  dim3 g2(1, cfg.num_kv_heads, seq_count);
+  page_store_kernel<1><<<g2, 256, 0, st>>>(cfg, cache, layer, nullptr, nullptr, 0, seq_begin, prm, sketch_proj);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  slot_id_scan_kernel<1><<<seq_count, 1024, 0, st>>>(cfg, cache, layer, seq_begin, 1);
+  return cudaGetLastError();
+}
+
+}  // namespace carekv

@@ -1,0 +1,285 @@
+"""DecodeEngine: host driver of the cache path over the C ABI.
+
+It owns nothing but the decode workspace; the cache arena is a CAREKVCache.
+Per layer and step the engine issues at most three kernel launches:
+carekv_append (plus the page-full store on steps where a page completes),
+and carekv_decode_attention (split-K pass + route/correct).  Host-side token
+counts (``cache.lengths``) decide capacity, the workspace page stride and
+whether a page can complete, so no call reads device memory back.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+from .cache import CAREKVCache
+from .config import resolve_route_params, resolve_store_params
+
+_DT = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
+
+
+class DecodeEngine:
+    def __init__(self, cache: CAREKVCache):
+        self.cache = cache
+        self.cfg = cache.cfg
+        self._ws = None
+        self._ws_bytes = 0
+
+    # ── helpers ───────────────────────────────────────────────────────
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.cache.device).cuda_stream
+
+    def _check_tensor(self, t: torch.Tensor, shape, what):
+        if not t.is_cuda or t.device != self.cache.device:
+            raise RuntimeError(f"{what}: expected a tensor on {self.cache.device}, got {t.device}")
+        if tuple(t.shape) != tuple(shape):
+            raise ValueError(f"{what}: expected shape {tuple(shape)}, got {tuple(t.shape)}")
+        if t.dtype not in _DT:
+            raise ValueError(f"{what}: unsupported dtype {t.dtype}")
+        return t.contiguous()
+
+    def pages_used(self, layer: int, seq_begin: int, seq_count: int, extra_tokens: int = 0) -> int:
+        T = self.cfg.page_size
+        n = max((self.cache.lengths[b][layer] + extra_tokens for b in range(seq_begin, seq_begin + seq_count)),
+                default=0)
+        return (n + T - 1) // T
+
+    def workspace(self, nbytes: int) -> torch.Tensor:
+        if self._ws is None or self._ws_bytes < nbytes:
+            self._ws = torch.empty(nbytes, dtype=torch.uint8, device=self.cache.device)
+            self._ws_bytes = nbytes
+        return self._ws
+
+    def workspace_bytes(self, seq_count: int, pages: int) -> int:
+        n = ctypes.c_size_t(0)
+        _lib.check(_lib.lib().carekv_decode_workspace_bytes(ctypes.byref(self.cache.ccfg), seq_count, pages,
+                                                            ctypes.byref(n)), "carekv_decode_workspace_bytes")
+        return int(n.value)
+
+    def _sketch_ptr(self):
+        return self.cache.sketch_proj().data_ptr() if self.cfg.store_sketch else None
+
+    # ── prefill store ─────────────────────────────────────────────────
+    def prefill_store(self, layer: int, K: torch.Tensor, V: torch.Tensor, seq_begin: int = 0,
+                      token_start: int = 0, sink_tokens: int = 4):
+        """Write T rows per (sequence, kv head): K, V [seq_count, Hkv, T, D]."""
+        cfg = self.cfg
+        n, H, T, D = K.shape
+        K = self._check_tensor(K, (n, cfg.num_kv_heads, T, cfg.head_dim), "prefill K")
+        V = self._check_tensor(V, (n, cfg.num_kv_heads, T, cfg.head_dim), "prefill V")
+        if K.dtype != V.dtype:
+            raise ValueError("K and V must share a dtype")
+        n_new = (T + cfg.page_size - 1) // cfg.page_size
+        for b in range(seq_begin, seq_begin + n):
+            if self._pages(b, layer) + n_new > cfg.max_pages:
+                raise _lib.CacheFullError(_lib.ERR_CACHE_FULL, "prefill_store")
+        sp = resolve_store_params(cfg, layer, _DT[K.dtype], token_start, sink_tokens)
+        _lib.check(_lib.lib().carekv_prefill_store(ctypes.byref(self.cache.ccfg), ctypes.byref(self.cache.c), layer,
+                                                   K.data_ptr(), V.data_ptr(), T, seq_begin, n, ctypes.byref(sp),
+                                                   self._sketch_ptr(), self._stream()), "carekv_prefill_store")
+        if T > 0:
+            last = T % cfg.page_size or cfg.page_size
+            for b in range(seq_begin, seq_begin + n):
+                self._state()[(b, layer)] = (self._pages(b, layer) + n_new, last)
+                self.cache.lengths[b][layer] += T
+
+    # ── decode ────────────────────────────────────────────────────────
+    def append(self, layer: int, k: torch.Tensor, v: torch.Tensor, seq_begin: int = 0):
+        """Append one token per sequence: k, v [seq_count, Hkv, D]."""
+        cfg = self.cfg
+        n = k.shape[0]
+        k = self._check_tensor(k, (n, cfg.num_kv_heads, cfg.head_dim), "append k")
+        v = self._check_tensor(v, (n, cfg.num_kv_heads, cfg.head_dim), "append v")
+        T = cfg.page_size
+        may_fill = 0
+        for b in range(seq_begin, seq_begin + n):
+            pages, last = self._state().get((b, layer), (0, 0))
+            if pages == 0 or last >= T:
+                if pages + 1 > cfg.max_pages:
+                    raise _lib.CacheFullError(_lib.ERR_CACHE_FULL, "append")
+                last = 0
+            if last + 1 == T:
+                may_fill = 1       # this append completes a page: run the page store
+        sp = resolve_store_params(cfg, layer, _DT[k.dtype])
+        _lib.check(_lib.lib().carekv_append(ctypes.byref(self.cache.ccfg), ctypes.byref(self.cache.c), layer,
+                                            k.data_ptr(), v.data_ptr(), seq_begin, n, ctypes.byref(sp),
+                                            self._sketch_ptr(), may_fill, self._stream()), "carekv_append")
+        for b in range(seq_begin, seq_begin + n):
+            self._advance(b, layer)
+
+    def attend(self, layer: int, q: torch.Tensor, out: Optional[torch.Tensor] = None, seq_begin: int = 0,
+               kind: Optional[str] = None, correction: bool = True, score_normalize=None, k_corr_scale=None,
+               pages: Optional[int] = None) -> torch.Tensor:
+        """Decode attention for [seq_count, Hq, D] queries against the cache."""
+        cfg = self.cfg
+        n = q.shape[0]
+        q = self._check_tensor(q, (n, cfg.num_heads, cfg.head_dim), "decode q")
+        if out is None:
+            out = torch.empty_like(q)
+        if pages is None:
+            pages = max(1, max((self._pages(b, layer) for b in range(seq_begin, seq_begin + n)), default=1))
+        rp = resolve_route_params(cfg, layer, kind=kind, score_normalize=score_normalize,
+                                  k_corr_scale=k_corr_scale)
+        if not correction:
+            rp.kind = _lib.KIND_NONE
+        nbytes = self.workspace_bytes(n, pages)
+        ws = self.workspace(nbytes)
+        _lib.check(_lib.lib().carekv_decode_attention(
+            ctypes.byref(self.cache.ccfg), ctypes.byref(self.cache.c), layer, q.data_ptr(), out.data_ptr(),
+            _DT[q.dtype], seq_begin, n, pages, ctypes.byref(rp), self._sketch_ptr(), ws.data_ptr(), ws.numel(),
+            self._stream()), "carekv_decode_attention")
+        return out
+
+    # ── host mirror of the page state ─────────────────────────────────
+    # The device keeps num_pages / valid; the host mirrors them per
+    # (sequence, layer) as (pages, valid rows of the last page).
+    def _state(self):
+        st = getattr(self.cache, "_page_state", None)
+        if st is None:
+            st = {}
+            self.cache._page_state = st
+        return st
+
+    def _pages(self, b, layer):
+        return self._state().get((b, layer), (0, 0))[0]
+
+    def _last_page_valid(self, b, layer):
+        return self._state().get((b, layer), (0, 0))[1]
+
+    def _advance(self, b, layer):
+        T = self.cfg.page_size
+        pages, last = self._state().get((b, layer), (0, 0))
+        if pages == 0 or last >= T:
+            pages, last = pages + 1, 1
+        else:
+            last += 1
+        self._state()[(b, layer)] = (pages, last)
+        self.cache.lengths[b][layer] += 1
+
+    # ── parity readback (tests) ───────────────────────────────────────
+    MAX_SEL = 32
+
+    def last_selection(self, layer: int, seq_begin: int, seq_count: int, pages: int):
+        """Selected slots of the last attend(): {(seq, kv_head, query): [(kind, page, group), ...]}.
+
+        Reads the workspace region the route kernel publishes and maps grid
+        indices back to (\"K\", page, channel group) / (\"V\", page, token block)
+        through the cache's slot tables.  Synchronizes the device.
+        """
+        cfg = self.cache.ccfg
+        qn = cfg.num_heads // cfg.num_kv_heads
+        n_bh = seq_count * cfg.num_kv_heads
+        sel = self._ws[: n_bh * qn * (self.MAX_SEL + 1) * 4].view(torch.int32).view(n_bh, qn, self.MAX_SEL + 1)
+        sel = sel.cpu()
+        SK, SV = cfg.k_slots_per_page, cfg.v_slots_per_page
+        KG = pages * SK
+        kg = self.cache.view("k_slot_group").cpu() if SK else None
+        vb = self.cache.view("v_slot_block").cpu() if SV else None
+        out = {}
+        for bh in range(n_bh):
+            s, h = divmod(bh, cfg.num_kv_heads)
+            b = seq_begin + s
+            for i in range(qn):
+                n = int(sel[bh, i, 0])
+                items = []
+                for e in sel[bh, i, 1:1 + n].tolist():
+                    if e < KG:
+                        p, j = divmod(e, SK)
+                        items.append(("K", p, int(kg[b, layer, h, p, j])))
+                    else:
+                        p, j = divmod(e - KG, SV)
+                        items.append(("V", p, int(vb[b, layer, h, p, j])))
+                out[(b, h, i)] = items
+        return out
+
+    def last_scores(self, seq_count: int, pages: int):
+        """Normalised scores of the last attend(): [seq_count*Hkv, qn, pages*(SK+SV)] (-1 = no slot)."""
+        cfg = self.cache.ccfg
+        qn = cfg.num_heads // cfg.num_kv_heads
+        n_bh = seq_count * cfg.num_kv_heads
+        off = n_bh * qn * (self.MAX_SEL + 1) * 4
+        ng = pages * (cfg.k_slots_per_page + cfg.v_slots_per_page)
+        return self._ws[off: off + n_bh * qn * ng * 4].view(torch.float32).view(n_bh, qn, ng).clone()
+
+
+class DecodeStepGraph:
+    """One decode step over every layer, captured as CUDA graphs.
+
+    Per layer the step appends the new K/V rows and runs decode attention
+    (three kernel launches; five on steps where a page completes).  Kernels
+    read page counts from device memory, so one graph replays for every
+    step; a second graph adds the page-full store and is replayed on the
+    steps where the host page mirror says a page completes.  Step inputs
+    live in fixed device buffers (q [L,B,Hq,D], k/v [L,B,Hkv,D]) and outputs
+    land in out [L,B,Hq,D].
+    """
+
+    def __init__(self, engine: DecodeEngine, q, k, v, out, max_pages: int, correction: bool = True):
+        self.engine = engine
+        self.cache = engine.cache
+        self.cfg = engine.cfg
+        self.q, self.k, self.v, self.out = q, k, v, out
+        self.L, self.B = q.shape[0], q.shape[1]
+        self.max_pages = max_pages
+        self.correction = correction
+        lib = _lib.lib()
+        cache = self.cache
+        dt = _DT[q.dtype]
+        self.store_params = [resolve_store_params(self.cfg, l, dt) for l in range(self.L)]
+        self.route_params = []
+        for l in range(self.L):
+            rp = resolve_route_params(self.cfg, l)
+            if not correction:
+                rp.kind = _lib.KIND_NONE
+            self.route_params.append(rp)
+        nbytes = engine.workspace_bytes(self.B, max_pages)
+        self.ws = engine.workspace(nbytes)
+        self.sketch = engine._sketch_ptr()
+        self.graphs = {}
+        self.launches = {}
+        stream = torch.cuda.Stream(cache.device)
+        for fill in (0, 1):
+            # warm the launch path once outside capture (lazy module loading)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                self._issue(fill, torch.cuda.current_stream(cache.device).cuda_stream)
+            self.graphs[fill] = g
+            self.launches[fill] = self.L * ((3 if fill else 1) + 2)
+
+    def _issue(self, fill, st):
+        lib = _lib.lib()
+        cache = self.cache
+        for l in range(self.L):
+            _lib.check(lib.carekv_append(ctypes.byref(cache.ccfg), ctypes.byref(cache.c), l, self.k[l].data_ptr(),
+                                         self.v[l].data_ptr(), 0, self.B, ctypes.byref(self.store_params[l]),
+                                         self.sketch, fill, st), "carekv_append")
+            _lib.check(lib.carekv_decode_attention(
+                ctypes.byref(cache.ccfg), ctypes.byref(cache.c), l, self.q[l].data_ptr(), self.out[l].data_ptr(),
+                _DT[self.q.dtype], 0, self.B, self.max_pages, ctypes.byref(self.route_params[l]), self.sketch,
+                self.ws.data_ptr(), self.ws.numel(), st), "carekv_decode_attention")
+
+    def next_fill(self) -> int:
+        T = self.cfg.page_size
+        for b in range(self.B):
+            for l in range(self.L):
+                pages, last = self.engine._state().get((b, l), (0, 0))
+                if pages == 0 or last >= T:
+                    if pages + 1 > min(self.cfg.max_pages, self.max_pages):
+                        raise _lib.CacheFullError(_lib.ERR_CACHE_FULL, "decode step")
+                    last = 0
+                if last + 1 == T:
+                    return 1
+        return 0
+
+    def replay(self) -> int:
+        """Run one step; returns the number of kernel launches it issued."""
+        fill = self.next_fill()
+        self.graphs[fill].replay()
+        for b in range(self.B):
+            for l in range(self.L):
+                self.engine._advance(b, l)
+        return self.launches[fill]

@@ -1,0 +1,226 @@
+/*
+ * carekv_b200.h -- C ABI of the B200 CARE-KV decode hot path.
+ *
+ * Plain C: pointers, sizes and status codes; no framework types.  Every
+ * device pointer is caller-owned device memory; every entry point takes an
+ * explicit CUDA stream (cudaStream_t passed as void*) and returns
+ * CAREKV_OK or an error code.  Nothing here allocates device memory except
+ * where a comment says otherwise.
+ *
+ * Reference interfaces replaced (paths relative to the reference project):
+ *   quantizer.py:31-99, 257-383     -> carekv_quantize / carekv_dequantize /
+ *                                      carekv_pack_codes / carekv_unpack_codes
+ *   residual_store.py:121-146       -> carekv_pack_4bit / carekv_unpack_4bit
+ *   cache.py:430-536 (buffers)      -> carekv_cache_layout / carekv_cache_init
+ *   layer.py:204-334 + cache.py:617-654 + residual_store.py:239-464
+ *                                   -> carekv_prefill_store
+ *   layer.py:1028-1146 + cache.py:656-701
+ *                                   -> carekv_append
+ *   attention.py:979-1039 (base decode) + attention.py:576-957
+ *   (vectorized_joint_correction) + residual_router.py:37-76
+ *                                   -> carekv_decode_attention
+ */
+#ifndef CAREKV_B200_H
+#define CAREKV_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CAREKV_ABI_VERSION 1
+
+/* status codes */
+#define CAREKV_OK                 0
+#define CAREKV_ERR_INVALID_ARG    1   /* bad pointer, size or config value      */
+#define CAREKV_ERR_UNSUPPORTED    2   /* valid but not built (e.g. page_size!=16) */
+#define CAREKV_ERR_CACHE_FULL     3   /* a page beyond max_pages was needed      */
+#define CAREKV_ERR_CUDA           4   /* a CUDA launch or API call failed        */
+#define CAREKV_ERR_WORKSPACE      5   /* workspace smaller than required         */
+#define CAREKV_ERR_DEVICE_CHECK   6   /* a device-side bounds check tripped      */
+
+/* activation element types */
+#define CAREKV_F32   0
+#define CAREKV_F16   1
+#define CAREKV_BF16  2
+
+/* base scale storage (CacheConfig.scale_quant / scale_dtype) */
+#define CAREKV_SCALE_INT8  0   /* int8 codes + one fp16 master per page */
+#define CAREKV_SCALE_F16   1
+#define CAREKV_SCALE_BF16  2
+#define CAREKV_SCALE_F32   3
+
+/* Static shape of one cache arena (CacheConfig, cache.py:209-384). */
+typedef struct carekv_config {
+    int32_t num_layers;
+    int32_t num_heads;          /* query heads                                */
+    int32_t num_kv_heads;
+    int32_t head_dim;           /* 64 or 128                                  */
+    int32_t page_size;          /* tokens per page; 16                        */
+    int32_t max_pages;          /* per (sequence, layer, kv head), multiple of 8 */
+    int32_t base_bits;          /* 2, 3 or 4                                  */
+    int32_t group_size;         /* per-group quantization width; divides head_dim */
+    int32_t k_channel_group;    /* channels per K residual slot; 32           */
+    int32_t v_token_block;      /* tokens per V residual slot; divides page_size */
+    int32_t sketch_dim;         /* fp16 sketch length per K group, 0 = none kept */
+    int32_t residual_bits;      /* 4                                          */
+    int32_t scale_mode;         /* CAREKV_SCALE_*                             */
+    int32_t k_slots_per_page;   /* K slot capacity per page (>= store budget)  */
+    int32_t v_slots_per_page;   /* V slot capacity per page                    */
+} carekv_config_t;
+
+/* Device buffers of one arena holding `batch` sequences.  Shapes use
+ * B=batch, L=num_layers, H=num_kv_heads, P=max_pages, T=page_size,
+ * R=packed row bytes, G=head_dim/group_size, C=head_dim/k_channel_group,
+ * NV=page_size/v_token_block, SK/SV=slot capacities. */
+typedef struct carekv_cache {
+    int32_t   batch;
+    uint8_t  *k_codes;        /* [B][L][H][P][T][R] packed rows (quantizer.py row format) */
+    uint8_t  *v_codes;
+    void     *k_scale;        /* [B][L][H][P][T][G] int8 | fp16 | bf16 | fp32              */
+    void     *v_scale;
+    uint16_t *k_master;       /* [B][L][H][P] fp16 bits; int8 scale mode only              */
+    uint16_t *v_master;
+    int32_t  *valid;          /* [B][L][H][P] valid rows per page                          */
+    int32_t  *num_pages;      /* [B][L][H] allocated pages                                 */
+    float    *v_norm2;        /* [B][L][H][P] sum of squared dequantized V over valid rows */
+    int8_t   *k_slot_group;   /* [B][L][H][P][SK] channel group of each kept K slot, ascending, -1 = empty */
+    uint8_t  *k_slot_data;    /* [B][L][H][P][SK][T*k_channel_group/2] 4-bit payload        */
+    uint16_t *k_slot_scale;   /* [B][L][H][P][SK] fp16 bits                                 */
+    int32_t  *k_slot_id;      /* [B][L][H][P][SK] id the reference arena would assign       */
+    int8_t   *v_slot_block;   /* [B][L][H][P][SV] token block of each kept V slot           */
+    uint8_t  *v_slot_data;    /* [B][L][H][P][SV][v_token_block*head_dim/2]                 */
+    uint16_t *v_slot_scale;   /* [B][L][H][P][SV]                                           */
+    int32_t  *v_slot_id;      /* [B][L][H][P][SV]                                           */
+    uint16_t *k_err;          /* [B][L][H][P][C] fp16 mean residual row norm per K group    */
+    uint16_t *v_err;          /* [B][L][H][P][NV]                                           */
+    uint16_t *k_sketch;       /* [B][L][H][P][C][sketch_dim] fp16, may be NULL              */
+    int32_t  *slot_counter;   /* [B][2] next K / V arena id per sequence                    */
+    unsigned long long *read_counter; /* [L][H][2] K / V slots read, may be NULL           */
+    int32_t  *error_flag;     /* [1] bit mask set by device-side checks                    */
+} carekv_cache_t;
+
+/* Per-call store policy, resolved by the host for one layer
+ * (residual_store.py:370-423, cache.py:180-202). */
+typedef struct carekv_store_params {
+    int32_t k_budget;         /* K slots kept per page (<= k_slots_per_page)   */
+    int32_t v_budget;
+    int32_t joint_budget;     /* > 0 selects the legacy joint policy          */
+    int32_t store_nothing;    /* 1: keep no slot (ratio 0 everywhere)         */
+    int32_t sink_tokens;      /* rows with absolute position < this are sink  */
+    int32_t token_start;      /* absolute position of the first prefill row   */
+    float   sensitivity;      /* layer sensitivity                            */
+    int32_t input_dtype;      /* CAREKV_F32 / F16 / BF16 of the K and V rows   */
+} carekv_store_params_t;
+
+/* Per-call routing / correction policy (attention.py:576-957,
+ * residual_router.py:37-76), resolved by the host for one layer. */
+#define CAREKV_KIND_BOTH 0
+#define CAREKV_KIND_K    1
+#define CAREKV_KIND_V    2
+#define CAREKV_KIND_NONE 3    /* base attention only */
+typedef struct carekv_route_params {
+    int32_t kind;             /* CAREKV_KIND_*                                */
+    int32_t joint;            /* 1 joint top-k over K and V, 0 separate       */
+    int32_t score_normalize;  /* per-query mean normalisation                  */
+    int32_t kscore_live;      /* 1 combined_kvscore, 0 sketch proxy score      */
+    int32_t exact;            /* 1 exact softmax K correction, 0 linear        */
+    int32_t budget_mode;      /* 0 absolute (read_k/read_v), 1 ratio           */
+    int32_t read_k;
+    int32_t read_v;
+    double  ratio_k;          /* ratio mode; double so int(n * ratio) matches Python */
+    double  ratio_v;
+    float   k_corr_scale;     /* linear mode only                              */
+    float   sensitivity;
+    float   lambda_k;
+    float   lambda_v;
+} carekv_route_params_t;
+
+/* ABI version and a static string for a status code. */
+int carekv_abi_version(void);
+const char *carekv_status_string(int status);
+
+/* Byte sizes of the arena buffers, in the order of carekv_cache_t's pointer
+ * fields (23 entries, k_codes .. error_flag).  Replaces the sizing in
+ * cache.py:430-536. */
+#define CAREKV_NUM_BUFFERS 23
+int carekv_cache_layout(const carekv_config_t *cfg, int32_t batch, size_t sizes[CAREKV_NUM_BUFFERS]);
+
+/* Reset an arena to empty: counters, valid rows and page counts zeroed,
+ * slot tables set to -1.  Replaces CAREKVCache._init_buffers (cache.py:430-536). */
+int carekv_cache_init(const carekv_config_t *cfg, const carekv_cache_t *cache, void *stream);
+
+/* ---- standalone quantizer ops on contiguous device rows ------------------ */
+/* quantize (quantizer.py:31-64): x [rows][D] -> codes int8 [rows][D],
+ * scale [rows][D/g] in the same dtype as x. */
+int carekv_quantize(const void *x, int8_t *codes, void *scale, int64_t rows, int32_t D,
+                    int32_t bits, int32_t group_size, int32_t dtype, void *stream);
+/* dequantize (quantizer.py:67-82): codes*scale in fp32, cast to dtype. */
+int carekv_dequantize(const int8_t *codes, const void *scale, void *out, int64_t rows, int32_t D,
+                      int32_t group_size, int32_t dtype, void *stream);
+/* pack_codes_2d / unpack_codes_2d (quantizer.py:364-383). */
+int carekv_pack_codes(const int8_t *codes, uint8_t *packed, int64_t rows, int32_t D, int32_t bits,
+                      void *stream);
+int carekv_unpack_codes(const uint8_t *packed, int8_t *codes, int64_t rows, int32_t D, int32_t bits,
+                        void *stream);
+/* pack_4bit / unpack_4bit (residual_store.py:121-146) on `n` independent
+ * blocks of `numel` fp32 values each (numel even). */
+int carekv_pack_4bit(const float *x, uint8_t *packed, uint16_t *scale_f16, int64_t n, int32_t numel,
+                     void *stream);
+int carekv_unpack_4bit(const uint8_t *packed, const uint16_t *scale_f16, float *out, int64_t n,
+                       int32_t numel, void *stream);
+
+/* ---- cache path ----------------------------------------------------------- */
+/* Prefill store of `T` rows for sequences [seq_begin, seq_begin+seq_count)
+ * of layer `layer`: allocates ceil(T/page_size) pages per kv head after the
+ * pages already held, quantizes and packs rows, writes int8 page scales,
+ * enumerates and keeps residual slots.  K, V: [seq_count][H][T][D] in
+ * params->input_dtype.  sketch_proj: [k_channel_group][sketch_dim] fp32
+ * (required when cfg->sketch_dim > 0).  Replaces layer.py:204-334. */
+int carekv_prefill_store(const carekv_config_t *cfg, const carekv_cache_t *cache, int32_t layer,
+                         const void *K, const void *V, int32_t T, int32_t seq_begin,
+                         int32_t seq_count, const carekv_store_params_t *params,
+                         const float *sketch_proj, void *stream);
+
+/* Append one token per sequence to layer `layer` (decode): k, v
+ * [seq_count][H][D] in params->input_dtype.  Opens a page when needed and,
+ * when a page fills, re-runs the residual store on it as the reference does
+ * (layer.py:1087-1146).  The page-full store runs only when may_fill_page
+ * is nonzero; a caller that knows no sequence completes a page in this
+ * call may pass 0 to skip those two launches.  A page needed beyond
+ * max_pages is not written; the device sets bit 1 of cache->error_flag. */
+int carekv_append(const carekv_config_t *cfg, const carekv_cache_t *cache, int32_t layer,
+                  const void *k, const void *v, int32_t seq_begin, int32_t seq_count,
+                  const carekv_store_params_t *params, const float *sketch_proj,
+                  int32_t may_fill_page, void *stream);
+
+/* Workspace bytes carekv_decode_attention needs for `seq_count` sequences
+ * holding at most `max_pages_used` pages per (layer, kv head). */
+int carekv_decode_workspace_bytes(const carekv_config_t *cfg, int32_t seq_count,
+                                  int32_t max_pages_used, size_t *bytes);
+
+/* Decode attention for layer `layer`: base attention over the packed
+ * pages plus the routed residual correction.  q, out: [seq_count][num_heads][D]
+ * in `dtype`.  The workspace must hold carekv_decode_workspace_bytes.
+ * sketch_proj ([k_channel_group][sketch_dim] fp32) is read only by the
+ * sketch proxy score (params->kscore_live == 0).  At most 32 slots may be
+ * selected per query (absolute budgets, or the worst case of ratio budgets).
+ * Replaces CAREKVMultiHeadAttention.forward (attention.py:1042-1077) with
+ * vectorized_joint_correction applied to each kv head's query group. */
+int carekv_decode_attention(const carekv_config_t *cfg, const carekv_cache_t *cache, int32_t layer,
+                            const void *q, void *out, int32_t dtype, int32_t seq_begin,
+                            int32_t seq_count, int32_t max_pages_used,
+                            const carekv_route_params_t *params, const float *sketch_proj,
+                            void *workspace, size_t workspace_bytes, void *stream);
+
+/* Copy the device error flag to the host and clear it (synchronizes the
+ * stream).  Returns CAREKV_OK when no device check tripped. */
+int carekv_check_device_errors(const carekv_cache_t *cache, int32_t *flags_out, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CAREKV_B200_H */

@@ -1,0 +1,161 @@
+"""GPU parity: the sm_100a kernels against the reference goldens and the oracle.
+
+Bit-exact: packed codes, int8 scale codes and fp16 masters, valid counts,
+slot ids (the reference's arena order), 4-bit payloads and their scales,
+and the selected (kind, page, group) slots of every query on tie-free
+inputs.  Floating outputs: error norms within one fp16 ulp, attention
+output and dO within 1e-3 relative / 2e-3 absolute (fp32 accumulation).
+"""
+
+import json
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import GOLDEN, load_pkg
+from helpers import (PAPER_BEST_ENV, compare_cache_state, env, oracle_cache_for, oracle_selection,
+                     route_cfg_from, selection_margin)
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-3, 2e-3
+TDT = {"fp32": torch.float32, "fp16": torch.float16, "bf16": torch.bfloat16}
+
+
+@pytest.fixture(scope="module")
+def pkg():
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    return load_pkg()
+
+
+def _golden(name):
+    z = np.load(os.path.join(GOLDEN, name), allow_pickle=False)
+    return z, json.loads(str(z["meta"]))
+
+
+def _t(x, dt, dev="cuda"):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dev).to(TDT[dt])
+
+
+# ─────────────────────────── quantizer ops ───────────────────────────
+def test_quantizer_ops_match_reference_goldens(pkg):
+    z, cases = _golden("quant.npz")
+    for c in cases:
+        k, dt, bits, gs, D = c["key"], c["dt"], c["bits"], c["group_size"], c["D"]
+        x = _t(z[k + "_x"], dt)
+        qc = pkg.QuantConfig(bits=bits, group_size=gs)
+        codes, scale = pkg.quantize(x, qc)
+        assert np.array_equal(codes.cpu().numpy(), z[k + "_codes"]), (c, "codes")
+        assert np.array_equal(scale.float().cpu().numpy(), z[k + "_scale"]), (c, "scale")
+        packed = pkg.pack_codes_2d(codes, bits)
+        assert np.array_equal(packed.view(torch.uint8).cpu().numpy(), z[k + "_packed"]), (c, "packed")
+        assert torch.equal(pkg.unpack_codes_2d(packed, bits, D), codes)
+        xh = pkg.dequantize(codes, scale, x.shape, qc)
+        assert np.array_equal(xh.float().cpu().numpy(), z[k + "_xhat"]), (c, "x_hat")
+        r4, r4s = pkg.pack_4bit(torch.from_numpy(z[k + "_resid"][:, :32].copy()).cuda())
+        assert np.array_equal(r4.view(torch.uint8).cpu().numpy(), z[k + "_r4"]), (c, "4-bit payload")
+        assert float(r4s.float().item()) == float(z[k + "_r4s"]), (c, "4-bit scale")
+        back = pkg.unpack_4bit(r4, r4s, 16 * 32).cpu().numpy()
+        assert np.array_equal(back, oracle.unpack_4bit(z[k + "_r4"], z[k + "_r4s"], 512))
+
+
+# ─────────────────────── prefill store + decode append ───────────────────────
+def _store_case_cfg(pkg, c, store_sketch=True):
+    return pkg.CacheConfig(
+        num_layers=1, num_heads=c["Hq"], num_kv_heads=c["Hkv"], head_dim=c["D"], page_size=16,
+        max_pages=c["max_pages"], base_bits=c["bits"], group_size=c["group_size"], k_channel_group=32,
+        v_token_block=4, sketch_dim=32, packed_base=True, scale_quant=c["scale_quant"],
+        store_budget_mode=c["store_budget_mode"], store_abs_k=c["store_abs_k"], store_abs_v=c["store_abs_v"],
+        store_budget_ratio=c["store_budget_ratio"], read_budget_ratio=0.0, store_sketch=store_sketch)
+
+
+@pytest.mark.parametrize("ci", range(7))
+def test_store_and_append_match_reference_goldens(pkg, ci):
+    z, cases = _golden("store_decode.npz")
+    c = cases[ci]
+    key, dt = c["key"], c["dt"]
+    with env(CAREKV_STORE_POLICY=c["store_policy"], CAREKV_PREFILL_RESIDUAL_KIND=c["kind"]):
+        cfg = _store_case_cfg(pkg, c)
+        cache = pkg.CAREKVCache(cfg, torch.device("cuda"), batch=1)
+        eng = pkg.DecodeEngine(cache)
+        K, V = _t(z[key + "_K"], dt), _t(z[key + "_V"], dt)
+        eng.prefill_store(0, K[None], V[None])
+        oc = oracle_cache_for(cfg)
+        for h in range(c["Hkv"]):
+            oc.prefill_write(0, h, z[key + "_K"][h], z[key + "_V"][h], dt)
+        torch.cuda.synchronize()
+        compare_cache_state(cache, oc, 0, 0, check_sketch=True)
+        grp = c["Hq"] // c["Hkv"]
+        for s in range(c["steps"]):
+            kr, vr = _t(z[key + "_dk"][s], dt), _t(z[key + "_dv"][s], dt)
+            eng.append(0, kr[None], vr[None])
+            q = _t(z[key + "_dq"][s], dt)
+            O = eng.attend(0, q[None], correction=False)[0].float().cpu().numpy()
+            ref = z[key + "_dO"][s]
+            tol = {"fp32": 1e-4, "fp16": 2e-3, "bf16": 8e-3}[dt]
+            np.testing.assert_allclose(O, ref, rtol=tol, atol=tol, err_msg=f"decode step {s}")
+            pos = int(oc.valid[0, 0, :oc.next_page[0, 0]].sum())
+            for h in range(c["Hkv"]):
+                oc.append(0, h, z[key + "_dk"][s][h], z[key + "_dv"][s][h], dt, pos_abs=pos)
+        torch.cuda.synchronize()
+        compare_cache_state(cache, oc, 0, 0, check_sketch=True)
+        cache.check_errors()
+
+
+# ─────────────────────────── correction ───────────────────────────
+@pytest.mark.parametrize("ci", range(9))
+def test_decode_correction_matches_reference_goldens(pkg, ci):
+    """Kernel O = O_base + dO against the reference's vectorized_joint_correction."""
+    z, cases = _golden("correction.npz")
+    c = cases[ci]
+    key = c["key"]
+    D, Hq, Hkv, N = c["D"], c["Hq"], c["Hkv"], c["N"]
+    e = dict(PAPER_BEST_ENV)
+    e.update(CAREKV_KSCORE_LIVE="1" if c["kscore_live"] else "0",
+             CAREKV_K_CORRECTION_MODE=c["k_correction_mode"],
+             CAREKV_SCORE_NORMALIZE="1" if c["score_normalize"] else "0",
+             CAREKV_PREFILL_RESIDUAL_KIND=c["kind"], CAREKV_K_CORRECTION_SCALE="0.1")
+    with env(**e):
+        cfg = pkg.CacheConfig(
+            num_layers=1, num_heads=Hq, num_kv_heads=Hkv, head_dim=D, page_size=16,
+            max_pages=c["max_pages"], base_bits=3, group_size=32, k_channel_group=32, v_token_block=4,
+            sketch_dim=32, packed_base=True, scale_quant="int8", store_budget_mode="absolute",
+            store_abs_k=c["store_abs_k"], store_abs_v=c["store_abs_v"], read_budget_mode=c["read_budget_mode"],
+            read_abs_k=c["read_abs_k"], read_abs_v=c["read_abs_v"], read_budget_ratio=c["read_budget_ratio"],
+            route_policy=c["route_policy"], store_sketch=not c["kscore_live"])
+        cache = pkg.CAREKVCache(cfg, torch.device("cuda"), batch=1)
+        eng = pkg.DecodeEngine(cache)
+        with env(CAREKV_PREFILL_RESIDUAL_KIND="both"):
+            eng.prefill_store(0, _t(z[key + "_K"], "fp32")[None], _t(z[key + "_V"], "fp32")[None])
+        q = _t(z[key + "_Q"], "fp32")[None]
+        pages = eng._pages(0, 0)
+        O = eng.attend(0, q)[0].cpu().numpy()
+        sel = eng.last_selection(0, 0, 1, pages)
+        k_reads, v_reads = cache.read_counters()
+        oc = oracle_cache_for(cfg)
+        with env(CAREKV_PREFILL_RESIDUAL_KIND="both"):
+            for h in range(Hkv):
+                oc.prefill_write(0, h, z[key + "_K"][h], z[key + "_V"][h], "fp32")
+        grp = Hq // Hkv
+        tk = tv = 0
+        for h in range(Hkv):
+            ref = z[f"{key}_O_{h}"] + z[f"{key}_delta_{h}"]
+            np.testing.assert_allclose(O[h * grp:(h + 1) * grp], ref, rtol=RTOL, atol=ATOL,
+                                       err_msg=f"{c['name']} kv head {h}")
+            Kh, Vh, _ = oc.read_base_concat(0, h)
+            qh = z[key + "_Q"][h * grp:(h + 1) * grp]
+            S, A, Ob = oracle.base_attention(Kh, Vh, qh, D)
+            _, info = oracle.vectorized_joint_correction(oc, 0, h, qh, S, A, Vh, Ob, route_cfg_from(cfg))
+            want = oracle_selection(info, grp)
+            for i in range(grp):
+                got = sorted(sel[(0, h, i)])
+                if got != want[i]:
+                    assert selection_margin(info, i) < 1e-5, (c["name"], h, i, got, want[i])
+            tk += int(z[f"{key}_reads_{h}"][0])
+            tv += int(z[f"{key}_reads_{h}"][1])
+        assert (k_reads, v_reads) == (tk, tv), (c["name"], (k_reads, v_reads), (tk, tv))
