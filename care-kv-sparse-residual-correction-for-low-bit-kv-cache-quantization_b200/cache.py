@@ -55,6 +55,8 @@ class CAREKVCache:
         device = torch.device(device)
         if device.type != "cuda":
             raise RuntimeError("CAREKVCache lives in GPU memory; the B200 build has no CPU path")
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
         self.cfg = cfg
         self.device = device
         self.batch = int(batch)
@@ -164,10 +166,11 @@ class CAREKVCache:
         """The reference's PageMeta for a page, rebuilt from the device tables."""
         c = self.ccfg
         C, NV = c.head_dim // c.k_channel_group, c.page_size // c.v_token_block
-        kg = self.view("k_slot_group")[seq, layer, kv_head, page_id].tolist()
-        ki = self.view("k_slot_id")[seq, layer, kv_head, page_id].tolist()
-        vb = self.view("v_slot_block")[seq, layer, kv_head, page_id].tolist()
-        vi = self.view("v_slot_id")[seq, layer, kv_head, page_id].tolist()
+        def _row(name):
+            t = self.view(name)
+            return [] if t is None else t[seq, layer, kv_head, page_id].tolist()
+        kg, ki = _row("k_slot_group"), _row("k_slot_id")
+        vb, vi = _row("v_slot_block"), _row("v_slot_id")
         ks = [-1] * C
         vs = [-1] * NV
         for g, i in zip(kg, ki):

@@ -72,9 +72,10 @@ __device__ __forceinline__ float group_scale(float max_abs, int qmax, int dt) {
 }
 __device__ __forceinline__ int8_t quant_code(float x, float scale, int qmax, int dt) {
   float t = rnd(__fdiv_rn(x, scale), dt);
+  if (t != t) return 0;  // torch's clamp keeps NaN (0/0 on an all-zero fp16 group); int8 cast -> 0
   t = rintf(t);
   t = fminf(fmaxf(t, static_cast<float>(-qmax - 1)), static_cast<float>(qmax));
-  return to_code(t);
+  return static_cast<int8_t>(static_cast<int>(t));
 }
 // dequantize: code * scale in fp32, rounded to the scale dtype.
 __device__ __forceinline__ float dequant(int code, float scale, int dt) {
@@ -146,9 +147,11 @@ __device__ __forceinline__ void write_raw_scale(void* base, int64_t i, int mode,
 
 // int8 scale code against a master (cache.py:601-602, 692-693)
 __device__ __forceinline__ int8_t int8_scale_code(float s, float master) {
-  float t = rintf(__fdiv_rn(s, master));
+  float t = __fdiv_rn(s, master);
+  if (t != t) return 0;  // 0/0 with a zero master: NaN -> int8 0 as in torch
+  t = rintf(t);
   t = fminf(fmaxf(t, -128.0f), 127.0f);
-  return to_code(t);
+  return static_cast<int8_t>(static_cast<int>(t));
 }
 
 // ───────────────────────── 4-bit residual slots ─────────────────────────

@@ -1,0 +1,38 @@
+// Arguments shared by the decode kernels (decode.cu, decode_fast.cu).
+#pragma once
+#include "common.cuh"
+
+namespace carekv {
+
+struct DecodeArgs {
+  carekv_config_t cfg;
+  carekv_cache_t cache;
+  int layer;
+  const void* q;
+  void* out;
+  int dt;
+  int seq_begin;
+  int qn;           // query heads per kv head
+  int pps;          // pages per split
+  int n_splits;
+  int p_used;       // workspace page stride
+  float sf;         // fp32(1/sqrt(D))
+  float sqrt_d;     // fp32(sqrt(D))
+  float* S;         // [bh][qn][p_used*16] logits
+  float* pm;        // [bh][n_splits][qn]
+  float* pl;
+  float* po;        // [bh][n_splits][qn][D]
+  float* scores;    // [bh][qn][p_used*(SK+SV)]
+  int* sel_out;     // [bh][qn][1 + kMaxSel]: count, then selected grid indices
+  const float* sketch_proj;
+  carekv_route_params_t rp;
+  int force_generic;  // 1: use the generic split-K pass (tests)
+};
+
+template <int QN>
+cudaError_t launch_route(DecodeArgs& a, cudaStream_t st, int n_bh);
+
+template <int QN, int D>
+cudaError_t launch_decode_partial_int3(DecodeArgs& a, cudaStream_t st, int n_bh);
+
+}  // namespace carekv

@@ -1,0 +1,595 @@
+// Route + correct (kernels K4 + K2): one CTA of 8 warps per (sequence, kv head).
+//
+//  1. merge the split-K partials into O_base, M and L;
+//  2. score every stored residual slot: K slots with combined_kvscore
+//     (attention.py:167-184) or the sketch proxy (attention.py:718-725), one
+//     half-warp per slot (lane = token, 16-byte payload row per lane, all
+//     loads issued before use); V slots with block attention mass x error
+//     norm (attention.py:787-790), one thread per slot;
+//  3. normalise per query (attention.py:830-844) and select the joint or
+//     separate top-k (attention.py:856-875) with a two-level warp argmax,
+//     ties to the lower grid index;
+//  4. apply the exact softmax renormalisation (attention.py:96-118, in the
+//     sparse form dO = (O + sum_S A(e^ds-1)V + sum_V A e^ds R_V) /
+//     (1 + sum_S A(e^ds-1)) - O) or the linear form, one selected page or slot
+//     per warp, rows staged in shared memory, and write O = O_base + dO.
+//
+// Grid index: K entries (page, slot j) at p*SK + j, then V entries at
+// KG + p*SV + j; slot tables keep groups in ascending order, so the index
+// order is the reference's (page, group) order with K before V.
+#include "common.cuh"
+#include "internal.h"
+#include "decode_args.h"
+
+namespace carekv {
+
+constexpr int kRSel = 32;     // selected slots per query (host-validated)
+constexpr float kREps = 1e-6f;
+constexpr float kRL2e = 1.4426950408889634f;
+constexpr int kRWarps = 8;
+
+__device__ __forceinline__ bool rbetter(float s1, int i1, float s2, int i2) {
+  return s1 > s2 || (s1 == s2 && i1 < i2);
+}
+
+__device__ __forceinline__ void warp_argmax(float& v, int& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (rbetter(ov, oi, v, i)) { v = ov; i = oi; }
+  }
+}
+
+struct RouteSmem {
+  float Q[8][128];
+  float O[8][128];
+  float M[8], invL[8], L[8];
+  float red[kRWarps][8], red2[kRWarps][8];
+  float nk[8], nv[8];
+  int sel[8][kRSel];
+  float selv[8][kRSel];
+  int nsel[8];
+  float cand_v[kRWarps][kRSel];
+  int cand_i[kRWarps][kRSel];
+  float ds[kRSel][kPage];         // wK (unscaled q.R_K) per selected K page and token
+  int kp_page[kRSel], kp_mask[kRSel];
+  int vsel[kRSel];
+  float acc[kRWarps][128];
+  float z[kRWarps];
+  uint32_t stage[kRWarps][16 * 64 / 4 + 8];  // one page of packed V rows (<= 64 B each) or a V slot payload
+  float stage_sc[kRWarps][16 * 4];           // the page's V scales (fp16 values)
+  float coef[kRWarps][kPage];
+  int cnt_k, cnt_v, ntot, any_k, nkp, nvs;
+  float mshift;
+};
+
+template <int QN>
+__global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in_smem) {
+  __shared__ RouteSmem sm;
+  extern __shared__ float dyn[];
+  const Dims d = make_dims(a.cfg);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int bh = blockIdx.x;
+  const int s = bh / d.H, h = bh % d.H;
+  const int b = a.seq_begin + s;
+  const int D = d.D;
+  const int Hq = d.H * QN;
+  const int64_t lhp = d.lhp(b, a.layer, h);
+  const int np = min(a.cache.num_pages[lhp], a.p_used);
+  const carekv_route_params_t& rp = a.rp;
+
+  // ── 1. queries and the merged split-K partials ──
+  for (int idx = tid; idx < QN * D; idx += blockDim.x) {
+    const int i = idx / D, c = idx % D;
+    sm.Q[i][c] = load_act(a.q, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + c, a.dt);
+  }
+  if (tid < QN) {
+    const int64_t base = static_cast<int64_t>(bh) * a.n_splits * QN + tid;
+    float M = -INFINITY;
+    for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, a.pm[base + sp * QN]);
+    float L = 0.f;
+    if (M != -INFINITY)
+      for (int sp = 0; sp < a.n_splits; ++sp) {
+        const float m = a.pm[base + sp * QN];
+        if (m != -INFINITY) L += a.pl[base + sp * QN] * exp2f((m - M) * kRL2e);
+      }
+    sm.M[tid] = M;
+    sm.L[tid] = L;
+    sm.invL[tid] = L > 0.f ? 1.0f / L : 0.f;
+  }
+  if (tid == 0) { sm.cnt_k = 0; sm.cnt_v = 0; sm.ntot = 0; sm.any_k = 0; }
+  __syncthreads();
+  for (int idx = tid; idx < QN * D; idx += blockDim.x) {
+    const int i = idx / D, c = idx % D;
+    float O = 0.f;
+    if (sm.L[i] > 0.f) {
+      const int64_t base = static_cast<int64_t>(bh) * a.n_splits * QN + i;
+      for (int sp = 0; sp < a.n_splits; ++sp) {
+        const float m = a.pm[base + sp * QN];
+        if (m != -INFINITY) O += a.po[(base + sp * QN) * D + c] * exp2f((m - sm.M[i]) * kRL2e);
+      }
+      O = __fdiv_rn(O, sm.L[i]);
+    }
+    sm.O[i][c] = O;
+  }
+  __syncthreads();
+
+  auto write_base = [&]() {
+    if (tid < QN) a.sel_out[(static_cast<int64_t>(bh) * QN + tid) * (kRSel + 1)] = 0;
+    for (int idx = tid; idx < QN * D; idx += blockDim.x) {
+      const int i = idx / D, c = idx % D;
+      store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + c, sm.O[i][c], a.dt);
+    }
+  };
+  if (np == 0 || rp.kind == CAREKV_KIND_NONE) {
+    write_base();
+    return;
+  }
+
+  const int KG = a.p_used * d.SK;
+  const int VG = a.p_used * d.SV;
+  const int NG = KG + VG;
+  float* sc = scores_in_smem ? dyn : a.scores + static_cast<int64_t>(bh) * QN * NG;
+  const float* Sb = a.S + static_cast<int64_t>(bh) * QN * a.p_used * kPage;
+  const int64_t sst = static_cast<int64_t>(a.p_used) * kPage;
+  const bool kind_k = rp.kind == CAREKV_KIND_BOTH || rp.kind == CAREKV_KIND_K;
+  const bool kind_v = rp.kind == CAREKV_KIND_BOTH || rp.kind == CAREKV_KIND_V;
+  const bool may_k = kind_k && (rp.budget_mode == 0 ? rp.read_k > 0 : rp.ratio_k > 0.0);
+  const bool may_v = kind_v && (rp.budget_mode == 0 ? rp.read_v > 0 : rp.ratio_v > 0.0);
+
+  // ── 2a. K scores: half-warp per grid entry ──
+  {
+    const int half = lane >> 4, t = lane & 15;
+    const unsigned hm = 0xFFFFu << (16 * half);   // shuffles stay inside the half-warp
+    int cnt = 0;
+    for (int e0 = 2 * warp; e0 < KG; e0 += 2 * kRWarps) {
+      const int e = e0 + half;
+      const bool in = e < KG;
+      const int p = in ? e / d.SK : 0;
+      const int j = in ? e % d.SK : 0;
+      const int64_t pg = lhp * d.P + p;
+      int grp = -1, nv = 0;
+      if (in && p < np) {
+        grp = a.cache.k_slot_group[pg * d.SK + j];
+        nv = a.cache.valid[pg];
+      }
+      const bool ok = grp >= 0 && nv > 0;
+      if (t == 0 && ok) ++cnt;
+      if (!ok || !may_k) {
+        if (in && t < QN) sc[t * NG + e] = -1.f;
+        continue;
+      }
+      const uint8_t* pay = a.cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes;
+      const uint4 raw = *reinterpret_cast<const uint4*>(pay + t * 16);
+      const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
+      float sv[QN];
+#pragma unroll
+      for (int i = 0; i < QN; ++i) sv[i] = t < nv ? Sb[i * sst + p * kPage + t] : 0.f;
+      const float vn2 = a.cache.v_norm2[pg];
+      const uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
+      float r[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        int v = (wds[c >> 3] >> (4 * (c & 7))) & 15;
+        v = v > 7 ? v - 16 : v;
+        r[c] = __fmul_rn(static_cast<float>(v), rs);
+      }
+      const float* qb = &sm.Q[0][grp * d.kcg];
+      if (rp.kscore_live) {
+        const float vc = sqrtf(vn2);
+#pragma unroll
+        for (int i = 0; i < QN; ++i) {
+          float dot = 0.f;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) dot = fmaf(qb[i * 128 + c], r[c], dot);
+          float term = 0.f;
+          if (t < nv) {
+            const float dS = __fdiv_rn(dot, a.sqrt_d);
+            const float A = exp2f((sv[i] - sm.M[i]) * kRL2e) * sm.invL[i];
+            term = dS * (A * (1.f - A));
+          }
+          float ss = term * term;
+          ss += __shfl_xor_sync(hm, ss, 8);
+          ss += __shfl_xor_sync(hm, ss, 4);
+          ss += __shfl_xor_sync(hm, ss, 2);
+          ss += __shfl_xor_sync(hm, ss, 1);
+          float ks = sqrtf(ss) * vc;
+          if (!(ks == ks) || isinf(ks)) ks = 0.f;
+          if (t == 0) sc[i * NG + e] = fmaxf(ks, 0.f) * rp.sensitivity;
+        }
+      } else {
+        // sketch proxy: mass * |q_sketch . k_sketch| * boundary * vdiff * sens
+        const float mv = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
+        for (int i = 0; i < QN; ++i) {
+          float A = 0.f, inv = 0.f, vd = 0.f;
+          if (t < nv) {
+            A = exp2f((sv[i] - sm.M[i]) * kRL2e) * sm.invL[i];
+            inv = __fdiv_rn(1.f, fmaxf(sm.M[i] - sv[i], kREps));
+            float acc = 0.f;
+            for (int c = 0; c < D; ++c) {
+              const float svv = read_scale(a.cache.v_scale, (pg * kPage + t) * d.G + c / d.gsize, d.scale_mode, mv);
+              const float vh = f16r(__fmul_rn(static_cast<float>(unpack_code(a.cache.v_codes + (pg * kPage + t) * d.R, c, d.bits)), svv));
+              const float df = vh - sm.O[i][c];
+              acc = fmaf(df, df, acc);
+            }
+            vd = sqrtf(acc);
+          }
+          float mass = A, bnd = A * inv, pvd = A * vd;
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) {
+            mass += __shfl_xor_sync(hm, mass, o);
+            bnd += __shfl_xor_sync(hm, bnd, o);
+            pvd += __shfl_xor_sync(hm, pvd, o);
+          }
+          float qd = 0.f;
+          for (int jj = t; jj < d.sketch; jj += 16) {
+            float qs = 0.f;
+            for (int c = 0; c < d.kcg; ++c) qs = fmaf(sm.Q[i][grp * d.kcg + c], a.sketch_proj[c * d.sketch + jj], qs);
+            qd += qs * f16_bits_to_f32(a.cache.k_sketch[(pg * d.C + grp) * d.sketch + jj]);
+          }
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) qd += __shfl_xor_sync(hm, qd, o);
+          if (t == 0) sc[i * NG + e] = mass * fabsf(qd) * bnd * pvd * rp.sensitivity;
+        }
+      }
+    }
+    cnt += __shfl_xor_sync(0xffffffffu, cnt, 16);
+    if (lane == 0 && cnt) atomicAdd(&sm.cnt_k, cnt);
+  }
+  // ── 2b. V scores: thread per grid entry; page token count ──
+  {
+    int cnt = 0, ntok = 0;
+    for (int e = tid; e < VG; e += blockDim.x) {
+      const int p = e / d.SV, j = e % d.SV;
+      const int64_t pg = lhp * d.P + p;
+      int vb = -1, nv = 0;
+      if (p < np) {
+        vb = a.cache.v_slot_block[pg * d.SV + j];
+        nv = a.cache.valid[pg];
+      }
+      const int t0 = vb * d.vtb, t1 = min(t0 + d.vtb, nv);
+      const bool ok = vb >= 0 && t1 > t0;
+      cnt += ok;
+      if (ok && may_v) {
+        const float err = f16_bits_to_f32(a.cache.v_err[pg * d.NV + vb]);
+        for (int i = 0; i < QN; ++i) {
+          float mass = 0.f;
+          for (int t = t0; t < t1; ++t) mass += exp2f((Sb[i * sst + p * kPage + t] - sm.M[i]) * kRL2e) * sm.invL[i];
+          sc[i * NG + KG + e] = __fmul_rn(__fmul_rn(mass, err), rp.sensitivity);
+        }
+      } else {
+        for (int i = 0; i < QN; ++i) sc[i * NG + KG + e] = -1.f;
+      }
+    }
+    for (int p = tid; p < np; p += blockDim.x) ntok += a.cache.valid[lhp * d.P + p];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+      ntok += __shfl_xor_sync(0xffffffffu, ntok, o);
+    }
+    if (lane == 0) {
+      if (cnt) atomicAdd(&sm.cnt_v, cnt);
+      if (ntok) atomicAdd(&sm.ntot, ntok);
+    }
+  }
+  __syncthreads();
+
+  // ── budgets (residual_router.py:37-76) ──
+  const int n_k = sm.cnt_k, n_v = sm.cnt_v;
+  const bool want_k = kind_k && n_k > 0, want_v = kind_v && n_v > 0;
+  int bk, bv;
+  {
+    const int tk = want_k ? n_k : 0, tv = want_v ? n_v : 0;
+    if (rp.budget_mode == 0) {
+      bk = rp.read_k;
+      bv = rp.read_v;
+    } else {
+      bk = (rp.ratio_k > 0.0 && tk > 0) ? max(1, static_cast<int>(static_cast<double>(tk) * rp.ratio_k)) : 0;
+      bv = (rp.ratio_v > 0.0 && tv > 0) ? max(1, static_cast<int>(static_cast<double>(tv) * rp.ratio_v)) : 0;
+    }
+    if (rp.kind == CAREKV_KIND_V) bk = 0;
+    if (rp.kind == CAREKV_KIND_K) bv = 0;
+    bk = min(bk, tk);
+    bv = min(bv, tv);
+  }
+  if ((!want_k && !want_v) || (bk == 0 && bv == 0)) {
+    write_base();
+    return;
+  }
+  const bool score_k = want_k && bk > 0, score_v = want_v && bv > 0;
+
+  // ── 3a. normalisation; kinds that take no part are not candidates ──
+  const bool norm = rp.score_normalize && rp.kind == CAREKV_KIND_BOTH && score_k && score_v;
+  if (norm) {
+    for (int i = 0; i < QN; ++i) {
+      float ak = 0.f, av = 0.f;
+      for (int e = tid; e < NG; e += blockDim.x) {
+        const float v = sc[i * NG + e];
+        if (v >= 0.f) { if (e < KG) ak += v; else av += v; }
+      }
+      ak = warp_sum(ak);
+      av = warp_sum(av);
+      if (lane == 0) { sm.red[warp][i] = ak; sm.red2[warp][i] = av; }
+    }
+    __syncthreads();
+    if (tid < QN) {
+      float x = 0.f, y = 0.f;
+      for (int w = 0; w < kRWarps; ++w) { x += sm.red[w][tid]; y += sm.red2[w][tid]; }
+      sm.nk[tid] = fmaxf(__fdiv_rn(x, static_cast<float>(n_k)), kREps);
+      sm.nv[tid] = fmaxf(__fdiv_rn(y, static_cast<float>(n_v)), kREps);
+    }
+    __syncthreads();
+  }
+  for (int e = tid; e < NG; e += blockDim.x) {
+    const bool part = e < KG ? score_k : score_v;
+    for (int i = 0; i < QN; ++i) {
+      float v = sc[i * NG + e];
+      if (!part) v = -1.f;
+      else if (norm && v >= 0.f) {
+        v = e < KG ? __fdiv_rn(v, sm.nk[i]) : __fdiv_rn(v, sm.nv[i]);
+        if (rp.kscore_live) v = __fmul_rn(v, e < KG ? rp.lambda_k : rp.lambda_v);
+      }
+      sc[i * NG + e] = v;
+    }
+  }
+  __syncthreads();
+
+  // ── 3b. selection: per warp top-k of its chunk, then warp 0 merges ──
+  const bool joint = rp.joint && rp.kind == CAREKV_KIND_BOTH && score_k && score_v;
+  // Iterated argmax with a moving bound: each round takes the best entry
+  // strictly worse (score desc, index asc) than the previous pick, so no
+  // score is modified.  Level 1: every warp takes the top-k of its chunk;
+  // level 2: warp 0 takes the top-k of the 8 candidate lists.
+  auto pick = [&](int i, int lo, int hi, int k) {
+    if (k <= 0 || hi <= lo) return;
+    const int chunk = (hi - lo + kRWarps - 1) / kRWarps;
+    const int clo = lo + warp * chunk, chi = min(hi, clo + chunk);
+    const float* row = sc + i * NG;
+    float lv = INFINITY;
+    int li = -1;
+    for (int r = 0; r < k; ++r) {
+      float bv_ = -1.f;
+      int bi = 0x7fffffff;
+      for (int e = clo + lane; e < chi; e += 32) {
+        const float v = row[e];
+        if (v >= 0.f && rbetter(lv, li, v, e) && rbetter(v, e, bv_, bi)) { bv_ = v; bi = e; }
+      }
+      warp_argmax(bv_, bi);
+      if (lane == 0) {
+        sm.cand_v[warp][r] = bv_;
+        sm.cand_i[warp][r] = bi;
+      }
+      lv = bv_;
+      li = bi;
+      if (bv_ < 0.f) {
+        for (int r2 = r + 1 + lane; r2 < k; r2 += 32) { sm.cand_v[warp][r2] = -1.f; sm.cand_i[warp][r2] = 0x7fffffff; }
+        break;
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      float mv_ = INFINITY;
+      int mi = -1;
+      for (int r = 0; r < k; ++r) {
+        float bv_ = -1.f;
+        int bi = 0x7fffffff;
+        for (int x = lane; x < kRWarps * k; x += 32) {
+          const float v = sm.cand_v[x / k][x % k];
+          const int ix = sm.cand_i[x / k][x % k];
+          if (v >= 0.f && rbetter(mv_, mi, v, ix) && rbetter(v, ix, bv_, bi)) { bv_ = v; bi = ix; }
+        }
+        warp_argmax(bv_, bi);
+        if (bv_ < 0.f) break;
+        if (lane == 0 && sm.nsel[i] < kRSel) {
+          sm.selv[i][sm.nsel[i]] = bv_;
+          sm.sel[i][sm.nsel[i]++] = bi;
+          if (bi < KG) sm.any_k = 1;
+        }
+        mv_ = bv_;
+        mi = bi;
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+  };
+  if (tid < QN) sm.nsel[tid] = 0;
+  __syncthreads();
+  for (int i = 0; i < QN; ++i) {
+    if (joint) {
+      const int mb = (bk > 0 && bv > 0) ? bk + bv : max(bk, bv);
+      pick(i, 0, NG, min(mb, n_k + n_v));
+    } else {
+      if (score_k) pick(i, 0, KG, bk);
+      if (score_v) pick(i, KG, NG, bv);
+    }
+  }
+  if (tid < QN) {
+    int* so = a.sel_out + (static_cast<int64_t>(bh) * QN + tid) * (kRSel + 1);
+    so[0] = sm.nsel[tid];
+    for (int k = 0; k < sm.nsel[tid]; ++k) so[1 + k] = sm.sel[tid][k];
+  }
+  if (scores_in_smem) {
+    float* g = a.scores + static_cast<int64_t>(bh) * QN * NG;
+    for (int e = tid; e < QN * NG; e += blockDim.x) g[e] = sc[e];
+  }
+  __syncthreads();
+
+  // ── 4. apply ──
+  const bool exact = rp.exact && sm.any_k;
+  const int ntot = sm.ntot;
+  int reads_k = 0, reads_v = 0;
+  const int R = d.R, G = d.G;
+  for (int i = 0; i < QN; ++i) {
+    if (tid == 0) {
+      int nkp = 0, nvs = 0;
+      for (int k = 0; k < sm.nsel[i]; ++k) {
+        const int e = sm.sel[i][k];
+        if (e >= KG) { sm.vsel[nvs++] = e - KG; ++reads_v; continue; }
+        ++reads_k;
+        const int p = e / d.SK;
+        int u = -1;
+        for (int x = 0; x < nkp; ++x) if (sm.kp_page[x] == p) u = x;
+        if (u < 0) { u = nkp++; sm.kp_page[u] = p; sm.kp_mask[u] = 0; }
+        sm.kp_mask[u] |= 1 << (e % d.SK);
+      }
+      sm.nkp = nkp;
+      sm.nvs = nvs;
+    }
+    __syncthreads();
+    const int nkp = sm.nkp, nvs = sm.nvs;
+    // wK per (selected K page, token): q . R_K summed over the page's selected groups
+    for (int x = tid; x < nkp * kPage; x += blockDim.x) {
+      const int u = x / kPage, t = x % kPage;
+      const int64_t pg = lhp * d.P + sm.kp_page[u];
+      float acc = 0.f;
+      for (int j = 0; j < d.SK; ++j) {
+        if (!((sm.kp_mask[u] >> j) & 1)) continue;
+        const int grp = a.cache.k_slot_group[pg * d.SK + j];
+        const uint4 raw = *reinterpret_cast<const uint4*>(a.cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes + t * 16);
+        const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
+        const uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
+        float dot = 0.f;
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          int v = (wds[c >> 3] >> (4 * (c & 7))) & 15;
+          v = v > 7 ? v - 16 : v;
+          dot = fmaf(sm.Q[i][grp * d.kcg + c], __fmul_rn(static_cast<float>(v), rs), dot);
+        }
+        acc += dot;
+      }
+      sm.ds[u][t] = acc;
+    }
+    __syncthreads();
+    if (exact && warp == 0) {
+      float mx = -INFINITY;
+      int covered = 0;
+      for (int u = 0; u < nkp; ++u) {
+        const int nv = a.cache.valid[lhp * d.P + sm.kp_page[u]];
+        covered += nv;
+        if (lane < nv) mx = fmaxf(mx, __fdiv_rn(sm.ds[u][lane], a.sqrt_d));
+      }
+      mx = warp_max(mx);
+      if (lane == 0) sm.mshift = (nkp == 0) ? 0.f : (covered >= ntot ? mx : fmaxf(mx, 0.f));
+    }
+    __syncthreads();
+    const float mshift = exact ? sm.mshift : 0.f;
+    const float cbase = exact ? expf(-mshift) : 1.f;
+    float num[4] = {0.f, 0.f, 0.f, 0.f};
+    float zp = 0.f;
+    for (int item = warp; item < nkp + nvs; item += kRWarps) {
+      uint8_t* stg = reinterpret_cast<uint8_t*>(sm.stage[warp]);
+      if (item < nkp) {
+        const int u = item, p = sm.kp_page[u];
+        const int64_t pg = lhp * d.P + p;
+        const int nv = a.cache.valid[pg];
+        const float mv = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
+        // stage the page's packed V rows and scales
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(a.cache.v_codes + pg * kPage * R);
+        for (int w = lane; w < kPage * R / 4; w += 32) sm.stage[warp][w] = src[w];
+        for (int x = lane; x < kPage * G; x += 32)
+          sm.stage_sc[warp][x] = read_scale(a.cache.v_scale, pg * kPage * G + x, d.scale_mode, mv);
+        if (lane < kPage) {
+          float cf = 0.f;
+          if (lane < nv) {
+            const float A = exp2f((Sb[i * sst + p * kPage + lane] - sm.M[i]) * kRL2e) * sm.invL[i];
+            const float wk = sm.ds[u][lane];
+            if (exact) {
+              const float dsv = __fdiv_rn(wk, a.sqrt_d);
+              cf = A * (dsv <= 80.f ? cbase * expm1f(dsv) : expf(dsv - mshift) - cbase);
+            } else {
+              cf = A * wk * rp.k_corr_scale;
+            }
+          }
+          sm.coef[warp][lane] = cf;
+        }
+        __syncwarp();
+        for (int t = 0; t < nv; ++t) {
+          const float cf = sm.coef[warp][t];
+          if (exact) zp += cf;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const int c = lane + 32 * jj;
+            if (c < D) {
+              const float vh = f16r(__fmul_rn(static_cast<float>(unpack_code(stg + t * R, c, d.bits)),
+                                              sm.stage_sc[warp][t * G + c / d.gsize]));
+              num[jj] = fmaf(cf, exact ? vh : (vh - sm.O[i][c]), num[jj]);
+            }
+          }
+        }
+      } else {
+        const int ev = sm.vsel[item - nkp];
+        const int p = ev / d.SV, j = ev % d.SV;
+        const int64_t pg = lhp * d.P + p;
+        const int vb = a.cache.v_slot_block[pg * d.SV + j];
+        const int nv = a.cache.valid[pg];
+        const int t0 = vb * d.vtb, t1 = min(t0 + d.vtb, nv);
+        const uint32_t* src = reinterpret_cast<const uint32_t*>(a.cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes);
+        for (int w = lane; w < d.vslot_bytes / 4; w += 32) sm.stage[warp][w] = src[w];
+        const float rs = f16_bits_to_f32(a.cache.v_slot_scale[pg * d.SV + j]);
+        int u = -1;
+        for (int x = 0; x < nkp; ++x) if (sm.kp_page[x] == p) u = x;
+        if (lane < d.vtb) {
+          const int t = t0 + lane;
+          float cf = 0.f;
+          if (t < t1) {
+            const float A = exp2f((Sb[i * sst + p * kPage + t] - sm.M[i]) * kRL2e) * sm.invL[i];
+            float w = 1.f;
+            if (exact) {
+              const float dsv = u >= 0 ? __fdiv_rn(sm.ds[u][t], a.sqrt_d) : 0.f;
+              w = dsv <= 80.f ? cbase * expf(dsv) : expf(dsv - mshift);
+            }
+            cf = A * w;
+          }
+          sm.coef[warp][lane] = cf;
+        }
+        __syncwarp();
+        for (int tt = 0; tt < t1 - t0; ++tt) {
+          const float cf = sm.coef[warp][tt];
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const int c = lane + 32 * jj;
+            if (c < D) num[jj] = fmaf(cf, unpack_nibble(stg, tt * D + c, rs), num[jj]);
+          }
+        }
+      }
+      __syncwarp();
+    }
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int c = lane + 32 * jj;
+      if (c < D) sm.acc[warp][c] = num[jj];
+    }
+    if (lane == 0) sm.z[warp] = zp;
+    __syncthreads();
+    if (tid < D) {
+      float n = 0.f, z = cbase;
+      for (int w = 0; w < kRWarps; ++w) { n += sm.acc[w][tid]; z += sm.z[w]; }
+      const float ob = sm.O[i][tid];
+      const float delta = exact ? (__fdiv_rn(fmaf(cbase, ob, n), z) - ob) : n;
+      store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + tid, ob + delta, a.dt);
+    }
+    __syncthreads();
+  }
+  if (a.cache.read_counter != nullptr && tid == 0) {
+    unsigned long long* rc = a.cache.read_counter + (static_cast<int64_t>(a.layer) * d.H + h) * 2;
+    if (sm.any_k && reads_k) atomicAdd(rc, static_cast<unsigned long long>(reads_k));
+    if (reads_v) atomicAdd(rc + 1, static_cast<unsigned long long>(reads_v));
+  }
+}
+
+template <int QN>
+cudaError_t launch_route(DecodeArgs& a, cudaStream_t st, int n_bh) {
+  const int NG = a.p_used * (a.cfg.k_slots_per_page + a.cfg.v_slots_per_page);
+  const size_t sc_bytes = static_cast<size_t>(QN) * NG * sizeof(float);
+  const int in_smem = sc_bytes + sizeof(RouteSmem) <= 46 * 1024 ? 1 : 0;
+  route_kernel2<QN><<<n_bh, kRWarps * 32, in_smem ? sc_bytes : 0, st>>>(a, in_smem);
+  return cudaGetLastError();
+}
+
+template cudaError_t launch_route<1>(DecodeArgs&, cudaStream_t, int);
+template cudaError_t launch_route<2>(DecodeArgs&, cudaStream_t, int);
+template cudaError_t launch_route<4>(DecodeArgs&, cudaStream_t, int);
+template cudaError_t launch_route<8>(DecodeArgs&, cudaStream_t, int);
+
+}  // namespace carekv

@@ -201,7 +201,7 @@ class DecodeEngine:
         cfg = self.cache.ccfg
         qn = cfg.num_heads // cfg.num_kv_heads
         n_bh = seq_count * cfg.num_kv_heads
-        off = n_bh * qn * (self.MAX_SEL + 1) * 4
+        off = (n_bh * qn * (self.MAX_SEL + 1) * 4 + 255) // 256 * 256   # regions are 256-byte aligned
         ng = pages * (cfg.k_slots_per_page + cfg.v_slots_per_page)
         return self._ws[off: off + n_bh * qn * ng * 4].view(torch.float32).view(n_bh, qn, ng).clone()
 

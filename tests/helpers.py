@@ -143,7 +143,7 @@ def compare_cache_state(gpu_cache, oc, b, layer, check_sketch=False, err_ulps=Tr
             np.testing.assert_allclose(gm.v_error_norm.float().cpu().numpy(), om["v_err"], rtol=1e-3, atol=1e-7)
             if check_sketch and gm.k_sketch is not None:
                 np.testing.assert_allclose(gm.k_sketch.float().cpu().numpy(), om["k_sketch"], rtol=2e-3, atol=1e-5)
-            if kdata is not None:
+            if kdata is not None and kgrp is not None:
                 g = kgrp[b, layer, h, p].cpu().numpy()
                 for j, cg in enumerate(g):
                     if cg < 0:
@@ -152,7 +152,7 @@ def compare_cache_state(gpu_cache, oc, b, layer, check_sketch=False, err_ulps=Tr
                     packed, sc = oc.k_slots[sid]
                     assert np.array_equal(kdata[h, p, j], packed), ("K payload", h, p, cg)
                     assert float(kscale[b, layer, h, p, j].float().item()) == float(sc), ("K slot scale", h, p)
-            if vdata is not None:
+            if vdata is not None and vblk is not None:
                 g = vblk[b, layer, h, p].cpu().numpy()
                 for j, vb in enumerate(g):
                     if vb < 0:

@@ -120,7 +120,8 @@ def test_decode_correction_matches_reference_goldens(pkg, ci):
              CAREKV_K_CORRECTION_MODE=c["k_correction_mode"],
              CAREKV_SCORE_NORMALIZE="1" if c["score_normalize"] else "0",
              CAREKV_PREFILL_RESIDUAL_KIND=c["kind"], CAREKV_K_CORRECTION_SCALE="0.1")
-    with env(**e):
+    with env(**e), env(CAREKV_PREFILL_RESIDUAL_KIND="both"):
+        # the store ran with kind=both; only the routing below uses the case's kind
         cfg = pkg.CacheConfig(
             num_layers=1, num_heads=Hq, num_kv_heads=Hkv, head_dim=D, page_size=16,
             max_pages=c["max_pages"], base_bits=3, group_size=32, k_channel_group=32, v_token_block=4,
@@ -130,15 +131,15 @@ def test_decode_correction_matches_reference_goldens(pkg, ci):
             route_policy=c["route_policy"], store_sketch=not c["kscore_live"])
         cache = pkg.CAREKVCache(cfg, torch.device("cuda"), batch=1)
         eng = pkg.DecodeEngine(cache)
-        with env(CAREKV_PREFILL_RESIDUAL_KIND="both"):
-            eng.prefill_store(0, _t(z[key + "_K"], "fp32")[None], _t(z[key + "_V"], "fp32")[None])
+        eng.prefill_store(0, _t(z[key + "_K"], "fp32")[None], _t(z[key + "_V"], "fp32")[None])
+    with env(**e):
         q = _t(z[key + "_Q"], "fp32")[None]
         pages = eng._pages(0, 0)
         O = eng.attend(0, q)[0].cpu().numpy()
         sel = eng.last_selection(0, 0, 1, pages)
         k_reads, v_reads = cache.read_counters()
-        oc = oracle_cache_for(cfg)
         with env(CAREKV_PREFILL_RESIDUAL_KIND="both"):
+            oc = oracle_cache_for(cfg)
             for h in range(Hkv):
                 oc.prefill_write(0, h, z[key + "_K"][h], z[key + "_V"][h], "fp32")
         grp = Hq // Hkv
