@@ -81,7 +81,10 @@ SIGNATURES = [
     ("carekv_decode_attention", i32, [ctypes.POINTER(Config), ctypes.POINTER(Cache), i32, vp, vp, i32, i32, i32,
                                       i32, ctypes.POINTER(RouteParams), vp, vp, ctypes.c_size_t, vp]),
     ("carekv_check_device_errors", i32, [ctypes.POINTER(Cache), ctypes.POINTER(i32), vp]),
+    ("carekv_decode_attention_noalloc", i32, [ctypes.POINTER(Config), ctypes.POINTER(Cache), i32, vp, vp, i32, i32,
+                                              i32, i32, ctypes.POINTER(RouteParams), vp, vp]),
 ]
+NOALLOC_MAX_BYTES = 32 << 20
 
 _lib = None
 _load_error = None

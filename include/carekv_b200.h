@@ -215,6 +215,33 @@ int carekv_decode_attention(const carekv_config_t *cfg, const carekv_cache_t *ca
                             const carekv_route_params_t *params, const float *sketch_proj,
                             void *workspace, size_t workspace_bytes, void *stream);
 
+/* Decode attention for callers that cannot allocate device memory.
+ *
+ * No counterpart in the reference.  Same inputs, output and result as
+ * carekv_decode_attention, but the scratch is a fixed array compiled into
+ * this library (CAREKV_NOALLOC_MAX_BYTES per device, reserved on every GPU
+ * that loads the library until the process exits) instead of a caller
+ * workspace.  It is meant for callers that have no device allocator at hand
+ * or may not use one while a step runs: a serving engine that owns all
+ * device memory through its own pool, a host runtime binding this ABI with
+ * no access to cudaMalloc, or a latency-bound loop that must avoid the
+ * device synchronisation an allocation implies.
+ *
+ * The first call made while a device is current looks up that device's
+ * array (cudaGetSymbolAddress) and caches the address; make that first call
+ * before any stream capture.  A call whose scratch need
+ * (carekv_decode_workspace_bytes) exceeds CAREKV_NOALLOC_MAX_BYTES returns
+ * CAREKV_ERR_WORKSPACE without running anything.  All calls share the one
+ * array: no part of it needs clearing between calls, but calls that may
+ * overlap on the GPU race on it, so the caller must serialise them.  The call
+ * allocates nothing. */
+#define CAREKV_NOALLOC_MAX_BYTES ((size_t)32 << 20)
+int carekv_decode_attention_noalloc(const carekv_config_t *cfg, const carekv_cache_t *cache,
+                                    int32_t layer, const void *q, void *out, int32_t dtype,
+                                    int32_t seq_begin, int32_t seq_count, int32_t max_pages_used,
+                                    const carekv_route_params_t *params, const float *sketch_proj,
+                                    void *stream);
+
 /* Copy the device error flag to the host and clear it (synchronizes the
  * stream).  Returns CAREKV_OK when no device check tripped. */
 int carekv_check_device_errors(const carekv_cache_t *cache, int32_t *flags_out, void *stream);
