@@ -41,6 +41,31 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
   }
 }
 
+__device__ __forceinline__ void rmma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t rpack_h2(float lo, float hi) {
+  __half2 r = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+// Byte k of w (two 4-bit two's-complement codes, even channel in the low
+// nibble) -> half2 of the exact codes.  The low nibble goes to mantissa bit 0
+// of the low half (value 1024 + u), the high nibble to bit 4 of the high half
+// (value 64 + u); the XOR of bit 3 turns two's complement into u = code + 8
+// and the same key read as fp16 is the offset removed by the subtraction.
+__device__ __forceinline__ uint32_t nib_pair(uint32_t w, int k) {
+  const uint32_t y = __byte_perm(w, 0u, 0x4040u | (static_cast<uint32_t>(k) * 0x0101u));
+  const uint32_t key = 0x54806408u;
+  const uint32_t x = (y & 0x00F0000Fu) ^ key;
+  __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&x), *reinterpret_cast<const __half2*>(&key));
+  return *reinterpret_cast<uint32_t*>(&r);
+}
+
 struct RouteSmem {
   float Q[8][128];
   float O[8][128];
@@ -58,6 +83,7 @@ struct RouteSmem {
   float acc[kRWarps][128];
   float z[kRWarps];
   uint32_t stage[kRWarps][16 * 64 / 4 + 8];  // one page of packed V rows (<= 64 B each) or a V slot payload
+  __align__(16) uint32_t qfrag[4][2][32][4];  // A fragments of q_hi / q_lo per channel group and k-step
   float stage_sc[kRWarps][16 * 4];           // the page's V scales (fp16 values)
   float coef[kRWarps][kPage];
   int cnt_k, cnt_v, ntot, any_k, nkp, nvs;
@@ -115,6 +141,23 @@ __global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in
   }
   __syncthreads();
 
+  // A fragments for the slot dots: rows gid = q_hi, gid+8 = q_lo of query gid;
+  // k-step ks of group g covers channels g*32 + 8*tig + 4*ks + {0..3}
+  for (int x = tid; x < d.C * 2 * 32; x += blockDim.x) {
+    const int g = x / 64, ks = (x / 32) % 2, ln = x % 32;
+    const int qg = ln >> 2, tg = ln & 3;
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (qg < QN)
+      for (int e = 0; e < 4; ++e) v[e] = sm.Q[qg][g * 32 + 8 * tg + 4 * ks + e];
+    float hi[4], lo[4];
+    for (int e = 0; e < 4; ++e) { hi[e] = __half2float(__float2half_rn(v[e])); lo[e] = v[e] - hi[e]; }
+    sm.qfrag[g][ks][ln][0] = rpack_h2(hi[0], hi[1]);
+    sm.qfrag[g][ks][ln][1] = rpack_h2(lo[0], lo[1]);
+    sm.qfrag[g][ks][ln][2] = rpack_h2(hi[2], hi[3]);
+    sm.qfrag[g][ks][ln][3] = rpack_h2(lo[2], lo[3]);
+  }
+  __syncthreads();
+
   auto write_base = [&]() {
     if (tid < QN) a.sel_out[(static_cast<int64_t>(bh) * QN + tid) * (kRSel + 1)] = 0;
     for (int idx = tid; idx < QN * D; idx += blockDim.x) {
@@ -138,7 +181,71 @@ __global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in
   const bool may_k = kind_k && (rp.budget_mode == 0 ? rp.read_k > 0 : rp.ratio_k > 0.0);
   const bool may_v = kind_v && (rp.budget_mode == 0 ? rp.read_v > 0 : rp.ratio_v > 0.0);
 
-  // ── 2a. K scores: half-warp per grid entry ──
+  // ── 2a. K scores ──
+  if (rp.kscore_live || !may_k) {
+    // combined_kvscore, one warp per stored slot: q . R_K^T on the tensor
+    // cores (codes as exact fp16 integers, slot scale applied after), then
+    // ||dS * A(1-A)|| over the page's valid tokens * ||V_page||_F * sens.
+    const int gid = lane >> 2, tig = lane & 3;
+    int cnt = 0;
+    for (int e = warp; e < KG; e += kRWarps) {
+      const int p = e / d.SK, j = e % d.SK;
+      const int64_t pg = lhp * d.P + p;
+      int grp = -1, nv = 0;
+      if (p < np) {
+        grp = a.cache.k_slot_group[pg * d.SK + j];
+        nv = a.cache.valid[pg];
+      }
+      const bool ok = grp >= 0 && nv > 0;
+      cnt += ok;
+      if (!ok || !may_k) {
+        if (lane < QN) sc[lane * NG + e] = -1.f;
+        continue;
+      }
+      const uint8_t* pay = a.cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes;
+      const uint32_t w0 = *reinterpret_cast<const uint32_t*>(pay + gid * 16 + 4 * tig);
+      const uint32_t w1 = *reinterpret_cast<const uint32_t*>(pay + (gid + 8) * 16 + 4 * tig);
+      const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
+      const float vc = sqrtf(a.cache.v_norm2[pg]);
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
+      if (gid < QN) {
+        const float* srow = Sb + gid * sst + p * kPage;
+        const float2 sa = *reinterpret_cast<const float2*>(srow + 2 * tig);
+        const float2 sb2 = *reinterpret_cast<const float2*>(srow + 8 + 2 * tig);
+        s4[0] = sa.x; s4[1] = sa.y; s4[2] = sb2.x; s4[3] = sb2.y;
+      }
+      float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int ks = 0; ks < 2; ++ks) {
+        const uint4 af = *reinterpret_cast<const uint4*>(&sm.qfrag[grp][ks][lane][0]);
+        rmma16816(c0, af.x, af.y, af.z, af.w, nib_pair(w0, 2 * ks), nib_pair(w0, 2 * ks + 1));
+        rmma16816(c1, af.x, af.y, af.z, af.w, nib_pair(w1, 2 * ks), nib_pair(w1, 2 * ks + 1));
+      }
+      // tokens 2tig, 2tig+1 (c0) and 8+2tig, 9+2tig (c1) of query gid
+      float ss = 0.f;
+      if (gid < QN) {
+        const float dots[4] = {c0[0] + c0[2], c0[1] + c0[3], c1[0] + c1[2], c1[1] + c1[3]};
+        const int toks[4] = {2 * tig, 2 * tig + 1, 8 + 2 * tig, 9 + 2 * tig};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (toks[u] < nv) {
+            const float dS = __fdiv_rn(__fmul_rn(dots[u], rs), a.sqrt_d);
+            const float A = exp2f((s4[u] - sm.M[gid]) * kRL2e) * sm.invL[gid];
+            const float term = dS * (A * (1.f - A));
+            ss = fmaf(term, term, ss);
+          }
+        }
+      }
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      if (tig == 0 && gid < QN) {
+        float ks = sqrtf(ss) * vc;
+        if (!(ks == ks) || isinf(ks)) ks = 0.f;
+        sc[gid * NG + e] = fmaxf(ks, 0.f) * rp.sensitivity;
+      }
+    }
+    if (lane == 0 && cnt) atomicAdd(&sm.cnt_k, cnt);
+  } else
   {
     const int half = lane >> 4, t = lane & 15;
     const unsigned hm = 0xFFFFu << (16 * half);   // shuffles stay inside the half-warp
