@@ -133,10 +133,10 @@ struct SplitPlan {
 };
 
 // Pages per split so the CTA count fills whole waves of the split-K pass
-// (2 CTAs per SM on 148 SMs) while every CTA keeps at least 64 pages (16 per
-// warp, enough to fill the staging pipeline); fewer splits win ties.
-inline SplitPlan split_plan(int n_bh, int p_used) {
-  const int slots = 2 * 148;
+// (`slots` resident CTAs over the 148 SMs) while every CTA keeps at least 64
+// pages (16 per warp, enough to fill the staging pipeline); fewer splits win
+// ties.
+inline SplitPlan split_plan(int n_bh, int p_used, int slots) {
   int best_ns = 1;
   double best = -1.0;
   for (int ns = 1; ns <= 32; ++ns) {
@@ -158,15 +158,30 @@ inline SplitPlan split_plan(int n_bh, int p_used) {
 
 static inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
+// Split-K pass chosen for a layout.  NARROW: INT3 / int8 scales with at most
+// 4 query heads per kv head (decode_narrow.cu, 4 CTAs per SM, also computes
+// q . R_K of the stored K slots); WIDE: the same layout with 8 query heads
+// (decode_fast.cu, 2 CTAs per SM); GENERIC: every other layout.
+enum class Pass { GENERIC, WIDE, NARROW };
+inline Pass choose_pass(const carekv_config_t& c) {
+  const int D = c.head_dim;
+  const bool int3 = c.base_bits == 3 && c.scale_mode == CAREKV_SCALE_INT8 && (D == 64 || D == 128) &&
+                    c.group_size % (D / 4) == 0 && c.group_size % (D / 8) == 0 && c.page_size == kPage;
+  if (!int3) return Pass::GENERIC;
+  return c.num_heads / c.num_kv_heads <= 4 ? Pass::NARROW : Pass::WIDE;
+}
+inline int pass_slots(Pass p) { return p == Pass::NARROW ? 4 * 148 : 2 * 148; }
+
 // Workspace regions, each 256-byte aligned: selection readback, scores,
-// logits, split partials m / l / O.
+// logits, split partials m / l / O, and (narrow pass) q . R_K per K slot.
 struct WsLayout {
-  int64_t sel, scores, S, pm, pl, po, total;
+  int64_t sel, scores, S, pm, pl, po, kw, total;
 };
 inline WsLayout ws_layout(const carekv_config_t& c, int seq_count, int p_used) {
   const int64_t qn = c.num_heads / c.num_kv_heads;
   const int64_t n_bh = static_cast<int64_t>(seq_count) * c.num_kv_heads;
-  const SplitPlan sp = split_plan(static_cast<int>(n_bh), p_used);
+  const Pass pass = choose_pass(c);
+  const SplitPlan sp = split_plan(static_cast<int>(n_bh), p_used, pass_slots(pass));
   WsLayout w;
   int64_t o = 0;
   w.sel = o;    o = align256(o + n_bh * qn * (kMaxSel + 1) * 4);
@@ -175,6 +190,8 @@ inline WsLayout ws_layout(const carekv_config_t& c, int seq_count, int p_used) {
   w.pm = o;     o = align256(o + n_bh * sp.n_splits * qn * 4);
   w.pl = o;     o = align256(o + n_bh * sp.n_splits * qn * 4);
   w.po = o;     o = align256(o + n_bh * sp.n_splits * qn * static_cast<int64_t>(c.head_dim) * 4);
+  w.kw = o;
+  if (pass == Pass::NARROW) o = align256(o + n_bh * qn * static_cast<int64_t>(p_used) * c.k_slots_per_page * kPage * 4);
   w.total = o;
   return w;
 }
@@ -183,19 +200,20 @@ size_t workspace_bytes(const carekv_config_t& c, int seq_count, int p_used) {
   return static_cast<size_t>(ws_layout(c, seq_count, p_used).total);
 }
 
-// The fast pass covers the INT3 / int8-scale layout with scale groups that
-// contain each thread's channel chunk; every other layout runs the generic pass.
-inline bool fast_path(const carekv_config_t& c) {
-  const int D = c.head_dim;
-  return c.base_bits == 3 && c.scale_mode == CAREKV_SCALE_INT8 && (D == 64 || D == 128) &&
-         c.group_size % (D / 4) == 0 && c.group_size % (D / 8) == 0 && c.page_size == kPage;
-}
-
 template <int QN>
 static cudaError_t launch_qn(DecodeArgs& a, cudaStream_t st, int n_bh) {
   dim3 g1(n_bh, a.n_splits);
   cudaError_t e;
-  if (fast_path(a.cfg) && !a.force_generic) {
+  const Pass pass = a.force_generic ? Pass::GENERIC : choose_pass(a.cfg);
+  if (pass != Pass::NARROW) a.kw = nullptr;
+  if (pass == Pass::NARROW) {
+    if constexpr (QN <= 4) {
+      e = a.cfg.head_dim == 64 ? launch_decode_narrow<QN, 64>(a, st, n_bh)
+                               : launch_decode_narrow<QN, 128>(a, st, n_bh);
+    } else {
+      return cudaErrorInvalidValue;
+    }
+  } else if (pass == Pass::WIDE) {
     e = a.cfg.head_dim == 64 ? launch_decode_partial_int3<QN, 64>(a, st, n_bh)
                              : launch_decode_partial_int3<QN, 128>(a, st, n_bh);
   } else {
@@ -222,7 +240,7 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
   a.seq_begin = seq_begin;
   a.qn = cfg.num_heads / cfg.num_kv_heads;
   const int n_bh = seq_count * cfg.num_kv_heads;
-  const SplitPlan sp = split_plan(n_bh, p_used);
+  const SplitPlan sp = split_plan(n_bh, p_used, pass_slots(choose_pass(cfg)));
   a.pps = sp.pps;
   a.n_splits = sp.n_splits;
   a.p_used = p_used;
@@ -238,6 +256,11 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
   a.pm = reinterpret_cast<float*>(w + wl.pm);
   a.pl = reinterpret_cast<float*>(w + wl.pl);
   a.po = reinterpret_cast<float*>(w + wl.po);
+  // q . R_K is precomputed by the narrow pass whenever live combined_kvscore
+  // scoring may read it: K slots stored and K residuals part of the route
+  const bool live_k = rp.kind != CAREKV_KIND_NONE && rp.kind != CAREKV_KIND_V && rp.kscore_live &&
+                      cfg.k_slots_per_page > 0;
+  a.kw = (choose_pass(cfg) == Pass::NARROW && live_k) ? reinterpret_cast<float*>(w + wl.kw) : nullptr;
   a.sketch_proj = sketch_proj;
   a.rp = rp;
   a.force_generic = 0;

@@ -24,6 +24,8 @@ struct DecodeArgs {
   float* po;        // [bh][n_splits][qn][D]
   float* scores;    // [bh][qn][p_used*(SK+SV)]
   int* sel_out;     // [bh][qn][1 + kMaxSel]: count, then selected grid indices
+  float* kw;        // [bh][qn][p_used*SK][16]: q . R_K per stored K slot and token, written by
+                    // the narrow split-K pass when live K scoring runs there; null otherwise
   const float* sketch_proj;
   carekv_route_params_t rp;
   int force_generic;  // 1: use the generic split-K pass (tests)
@@ -34,5 +36,9 @@ cudaError_t launch_route(DecodeArgs& a, cudaStream_t st, int n_bh);
 
 template <int QN, int D>
 cudaError_t launch_decode_partial_int3(DecodeArgs& a, cudaStream_t st, int n_bh);
+
+template <int QN, int D>
+cudaError_t launch_decode_narrow(DecodeArgs& a, cudaStream_t st, int n_bh);
+size_t narrow_smem_bytes(const carekv_config_t& c, bool kslot);
 
 }  // namespace carekv

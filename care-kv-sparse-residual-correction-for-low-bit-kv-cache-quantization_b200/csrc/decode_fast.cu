@@ -22,6 +22,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "decode_args.h"
+#include "ptx.cuh"
 
 namespace carekv {
 namespace fast {
@@ -30,44 +31,6 @@ constexpr int kWarps = 4;
 constexpr int kCP = 2;   // pages per stage
 constexpr int kNS = 4;   // stages per warp
 constexpr float kLog2e = 1.4426950408889634f;
-
-// ───────────────────────── PTX helpers ─────────────────────────
-__device__ __forceinline__ uint32_t smem_addr(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_addr(dst)),
-      "l"(src), "r"(bytes), "r"(smem_addr(bar))
-      : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(smem_addr(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-// Bounded wait: false after ~2^31 cycles (about a second) without completion.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-  const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > (1ll << 31)) return false;
-  }
-  return true;
-}
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
 __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -78,18 +41,6 @@ __device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], 
 }
 
 __device__ __forceinline__ uint32_t lop_and_xor(uint32_t x, uint32_t m, uint32_t k) { return (x & m) ^ k; }
-__device__ __forceinline__ uint32_t h2sub(uint32_t a, uint32_t b) {
-  __half2 r = __hsub2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-__device__ __forceinline__ uint32_t h2mul(uint32_t a, uint32_t b) {
-  __half2 r = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
-  return *reinterpret_cast<uint32_t*>(&r);
-}
-__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
-  __half2 r = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&r);
-}
 __device__ __forceinline__ uint32_t dup_h2(float v) { return pack_h2(v, v); }
 
 // 24-bit packed word w of a row (3 bytes at 3w) from two aligned 32-bit

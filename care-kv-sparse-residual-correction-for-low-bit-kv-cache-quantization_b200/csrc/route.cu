@@ -20,6 +20,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "decode_args.h"
+#include "ptx.cuh"
 
 namespace carekv {
 
@@ -41,29 +42,35 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
   }
 }
 
-__device__ __forceinline__ void rmma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                          uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};\n"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+// 24-bit packed word at byte offset o of a staged row (bits 24..31 garbage).
+__device__ __forceinline__ uint32_t rword24(const uint8_t* row, int o) {
+  const uint32_t* p = reinterpret_cast<const uint32_t*>(row + (o & ~3));
+  return prmt(p[0], p[1], 0x3210 + 0x1111 * (o & 3));
 }
-__device__ __forceinline__ uint32_t rpack_h2(float lo, float hi) {
-  __half2 r = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&r);
+// acc[j] += cf * fp16(code_j * sigma) for the 8 channels of packed INT3 word w
+// of a row (exact fp16 dequantization: field -> mantissa, HSUB2, HMUL2)
+__device__ __forceinline__ void acc_int3_word(const uint8_t* row, int w, uint32_t sig2, float cf, float (&acc)[8]) {
+  const uint32_t W = rword24(row, 3 * w);
+  const uint32_t t = prmt(W, W << 13, 0x7610);         // low W[0:16], high W[3:19]
+  const uint32_t t2 = prmt(W >> 12, W << 1, 0x7610);   // low W[12:28], high W[15:31]
+  const uint32_t h[4] = {i3_pair<0, 0>(t, sig2), i3_pair<6, 6>(t, sig2), i3_pair<0, 0>(t2, sig2),
+                         i3_pair<6, 6>(t2, sig2)};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[k]));
+    acc[2 * k] = fmaf(cf, f.x, acc[2 * k]);
+    acc[2 * k + 1] = fmaf(cf, f.y, acc[2 * k + 1]);
+  }
 }
-// Byte k of w (two 4-bit two's-complement codes, even channel in the low
-// nibble) -> half2 of the exact codes.  The low nibble goes to mantissa bit 0
-// of the low half (value 1024 + u), the high nibble to bit 4 of the high half
-// (value 64 + u); the XOR of bit 3 turns two's complement into u = code + 8
-// and the same key read as fp16 is the offset removed by the subtraction.
-__device__ __forceinline__ uint32_t nib_pair(uint32_t w, int k) {
-  const uint32_t y = __byte_perm(w, 0u, 0x4040u | (static_cast<uint32_t>(k) * 0x0101u));
-  const uint32_t key = 0x54806408u;
-  const uint32_t x = (y & 0x00F0000Fu) ^ key;
-  __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&x), *reinterpret_cast<const __half2*>(&key));
-  return *reinterpret_cast<uint32_t*>(&r);
+// acc[j] += c * code_j for the 8 nibbles of a 4-bit residual word
+__device__ __forceinline__ void acc_nib_word(uint32_t u, float c, float (&acc)[8]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t hk = nib_pair(u, k);
+    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hk));
+    acc[2 * k] = fmaf(c, f.x, acc[2 * k]);
+    acc[2 * k + 1] = fmaf(c, f.y, acc[2 * k + 1]);
+  }
 }
 
 struct RouteSmem {
@@ -75,14 +82,16 @@ struct RouteSmem {
   int sel[8][kRSel];
   float selv[8][kRSel];
   int nsel[8];
-  float cand_v[kRWarps][kRSel];
-  int cand_i[kRWarps][kRSel];
+  int cnt[2][kRWarps];
+  float gv[kRSel];
+  int gi[kRSel];
+  int gcount;
   float ds[kRSel][kPage];         // wK (unscaled q.R_K) per selected K page and token
   int kp_page[kRSel], kp_mask[kRSel];
   int vsel[kRSel];
   float acc[kRWarps][128];
   float z[kRWarps];
-  uint32_t stage[kRWarps][16 * 64 / 4 + 8];  // one page of packed V rows (<= 64 B each) or a V slot payload
+  __align__(16) uint32_t stage[kRWarps][16 * 64 / 4 + 8];  // one page of packed V rows (<= 64 B each) or a V slot payload
   __align__(16) uint32_t qfrag[4][2][32][4];  // A fragments of q_hi / q_lo per channel group and k-step
   float stage_sc[kRWarps][16 * 4];           // the page's V scales (fp16 values)
   float coef[kRWarps][kPage];
@@ -91,7 +100,7 @@ struct RouteSmem {
 };
 
 template <int QN>
-__global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in_smem) {
+__global__ void __launch_bounds__(256, 4) route_kernel2(DecodeArgs a, int scores_in_smem) {
   __shared__ RouteSmem sm;
   extern __shared__ float dyn[];
   const Dims d = make_dims(a.cfg);
@@ -151,10 +160,10 @@ __global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in
       for (int e = 0; e < 4; ++e) v[e] = sm.Q[qg][g * 32 + 8 * tg + 4 * ks + e];
     float hi[4], lo[4];
     for (int e = 0; e < 4; ++e) { hi[e] = __half2float(__float2half_rn(v[e])); lo[e] = v[e] - hi[e]; }
-    sm.qfrag[g][ks][ln][0] = rpack_h2(hi[0], hi[1]);
-    sm.qfrag[g][ks][ln][1] = rpack_h2(lo[0], lo[1]);
-    sm.qfrag[g][ks][ln][2] = rpack_h2(hi[2], hi[3]);
-    sm.qfrag[g][ks][ln][3] = rpack_h2(lo[2], lo[3]);
+    sm.qfrag[g][ks][ln][0] = pack_h2(hi[0], hi[1]);
+    sm.qfrag[g][ks][ln][1] = pack_h2(lo[0], lo[1]);
+    sm.qfrag[g][ks][ln][2] = pack_h2(hi[2], hi[3]);
+    sm.qfrag[g][ks][ln][3] = pack_h2(lo[2], lo[3]);
   }
   __syncthreads();
 
@@ -182,7 +191,52 @@ __global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in
   const bool may_v = kind_v && (rp.budget_mode == 0 ? rp.read_v > 0 : rp.ratio_v > 0.0);
 
   // ── 2a. K scores ──
-  if (rp.kscore_live || !may_k) {
+  if (a.kw != nullptr) {
+    // combined_kvscore from q . R_K precomputed by the split-K pass: one
+    // thread per (query, stored slot); ||dS * A(1-A)|| over the page's valid
+    // tokens * ||V_page||_F * sens
+    int cnt = 0;
+    for (int idx = tid; idx < QN * KG; idx += blockDim.x) {
+      const int i = idx / KG, e = idx - i * KG;
+      const int p = e / d.SK, j = e - p * d.SK;
+      const int64_t pg = lhp * d.P + p;
+      int grp = -1, nv = 0;
+      if (p < np) {
+        grp = a.cache.k_slot_group[pg * d.SK + j];
+        nv = a.cache.valid[pg];
+      }
+      const bool ok = grp >= 0 && nv > 0;
+      if (i == 0) cnt += ok;
+      if (!ok || !may_k) {
+        sc[i * NG + e] = -1.f;
+        continue;
+      }
+      const float4* wv = reinterpret_cast<const float4*>(a.kw + ((static_cast<int64_t>(bh) * QN + i) * KG + e) * kPage);
+      const float4* sv = reinterpret_cast<const float4*>(Sb + i * sst + p * kPage);
+      const float vc = sqrtf(a.cache.v_norm2[pg]);
+      float ss = 0.f;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const float4 w4 = wv[q4], s4 = sv[q4];
+        const float wa[4] = {w4.x, w4.y, w4.z, w4.w};
+        const float sa[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (4 * q4 + u < nv) {
+            const float dS = __fdiv_rn(wa[u], a.sqrt_d);
+            const float A = exp2f((sa[u] - sm.M[i]) * kRL2e) * sm.invL[i];
+            const float term = dS * (A * (1.f - A));
+            ss = fmaf(term, term, ss);
+          }
+        }
+      }
+      float ks = sqrtf(ss) * vc;
+      if (!(ks == ks) || isinf(ks)) ks = 0.f;
+      sc[i * NG + e] = fmaxf(ks, 0.f) * rp.sensitivity;
+    }
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    if (lane == 0 && cnt) atomicAdd(&sm.cnt_k, cnt);
+  } else if (rp.kscore_live || !may_k) {
     // combined_kvscore, one warp per stored slot: q . R_K^T on the tensor
     // cores (codes as exact fp16 integers, slot scale applied after), then
     // ||dS * A(1-A)|| over the page's valid tokens * ||V_page||_F * sens.
@@ -218,8 +272,8 @@ __global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks) {
         const uint4 af = *reinterpret_cast<const uint4*>(&sm.qfrag[grp][ks][lane][0]);
-        rmma16816(c0, af.x, af.y, af.z, af.w, nib_pair(w0, 2 * ks), nib_pair(w0, 2 * ks + 1));
-        rmma16816(c1, af.x, af.y, af.z, af.w, nib_pair(w1, 2 * ks), nib_pair(w1, 2 * ks + 1));
+        mma_f16(c0, af.x, af.y, af.z, af.w, nib_pair(w0, 2 * ks), nib_pair(w0, 2 * ks + 1));
+        mma_f16(c1, af.x, af.y, af.z, af.w, nib_pair(w1, 2 * ks), nib_pair(w1, 2 * ks + 1));
       }
       // tokens 2tig, 2tig+1 (c0) and 8+2tig, 9+2tig (c1) of query gid
       float ss = 0.f;
@@ -442,61 +496,98 @@ __global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in
   }
   __syncthreads();
 
-  // ── 3b. selection: per warp top-k of its chunk, then warp 0 merges ──
+  // ── 3b. selection ──
   const bool joint = rp.joint && rp.kind == CAREKV_KIND_BOTH && score_k && score_v;
-  // Iterated argmax with a moving bound: each round takes the best entry
-  // strictly worse (score desc, index asc) than the previous pick, so no
-  // score is modified.  Level 1: every warp takes the top-k of its chunk;
-  // level 2: warp 0 takes the top-k of the 8 candidate lists.
+  // Top-k of sc[i][lo:hi) by (score desc, index asc), appended to sel[i].
+  // A block-wide bisection on the score's bit pattern (non-negative floats
+  // order like their bits; excluded entries hold -1) finds the k-th score T:
+  // every entry above T is taken, and ties at T go to the lowest indices
+  // (a second bisection over the index bound, only when T is shared).  One
+  // warp then sorts the <= 32 picks.
+  int flip = 0;
+  auto skey = [](float v) -> uint32_t { return v >= 0.f ? __float_as_uint(v) + 1u : 0u; };
+  auto bcount = [&](int c) -> int {   // block-wide sum, one barrier (double-buffered slots)
+    c = __reduce_add_sync(0xffffffffu, c);
+    if (lane == 0) sm.cnt[flip][warp] = c;
+    __syncthreads();
+    int tot = 0;
+#pragma unroll
+    for (int w = 0; w < kRWarps; ++w) tot += sm.cnt[flip][w];
+    flip ^= 1;
+    return tot;
+  };
   auto pick = [&](int i, int lo, int hi, int k) {
     if (k <= 0 || hi <= lo) return;
-    const int chunk = (hi - lo + kRWarps - 1) / kRWarps;
-    const int clo = lo + warp * chunk, chi = min(hi, clo + chunk);
     const float* row = sc + i * NG;
-    float lv = INFINITY;
-    int li = -1;
-    for (int r = 0; r < k; ++r) {
-      float bv_ = -1.f;
-      int bi = 0x7fffffff;
-      for (int e = clo + lane; e < chi; e += 32) {
-        const float v = row[e];
-        if (v >= 0.f && rbetter(lv, li, v, e) && rbetter(v, e, bv_, bi)) { bv_ = v; bi = e; }
+    auto count_ge = [&](uint32_t t) {
+      int c = 0;
+      for (int e = lo + tid; e < hi; e += blockDim.x) c += skey(row[e]) >= t;
+      return bcount(c);
+    };
+    const int n_cand = count_ge(1u);
+    const int room = kRSel - sm.nsel[i];
+    int kk = min(k, n_cand);
+    if (kk > room) {   // more picks than the selection table holds
+      if (tid == 0) atomicOr(a.cache.error_flag, 8);
+      kk = room;
+    }
+    if (kk <= 0) return;
+    uint32_t T = 1u;
+    int ibound = hi;   // take key > T, and key == T at indices < ibound
+    if (n_cand > kk) {
+      uint32_t tlo = 1u, thi = 0x7F800002u;
+      int c_lo = n_cand, c_hi = 0;   // counts at tlo (>= kk) and thi (< kk)
+      while (thi - tlo > 1u) {
+        const uint32_t mid = tlo + (thi - tlo) / 2u;
+        const int c = count_ge(mid);
+        if (c >= kk) { tlo = mid; c_lo = c; } else { thi = mid; c_hi = c; }
       }
-      warp_argmax(bv_, bi);
-      if (lane == 0) {
-        sm.cand_v[warp][r] = bv_;
-        sm.cand_i[warp][r] = bi;
+      T = tlo;
+      const int need = kk - c_hi;   // ties at T to take
+      if (c_lo - c_hi > need) {
+        int ilo = lo, ihi = hi;     // smallest bound with #{key == T, e < bound} >= need
+        while (ihi - ilo > 0) {
+          const int mid = ilo + (ihi - ilo) / 2;
+          int c = 0;
+          for (int e = lo + tid; e < mid; e += blockDim.x) c += skey(row[e]) == T;
+          if (bcount(c) >= need) ihi = mid; else ilo = mid + 1;
+        }
+        ibound = ilo;
       }
-      lv = bv_;
-      li = bi;
-      if (bv_ < 0.f) {
-        for (int r2 = r + 1 + lane; r2 < k; r2 += 32) { sm.cand_v[warp][r2] = -1.f; sm.cand_i[warp][r2] = 0x7fffffff; }
-        break;
+    }
+    if (tid == 0) sm.gcount = 0;
+    __syncthreads();
+    for (int e = lo + tid; e < hi; e += blockDim.x) {
+      const uint32_t kv = skey(row[e]);
+      if (kv > T || (kv == T && e < ibound)) {
+        const int slot = atomicAdd(&sm.gcount, 1);
+        if (slot < kRSel) { sm.gv[slot] = row[e]; sm.gi[slot] = e; }
       }
     }
     __syncthreads();
     if (warp == 0) {
-      float mv_ = INFINITY;
-      int mi = -1;
-      for (int r = 0; r < k; ++r) {
-        float bv_ = -1.f;
-        int bi = 0x7fffffff;
-        for (int x = lane; x < kRWarps * k; x += 32) {
-          const float v = sm.cand_v[x / k][x % k];
-          const int ix = sm.cand_i[x / k][x % k];
-          if (v >= 0.f && rbetter(mv_, mi, v, ix) && rbetter(v, ix, bv_, bi)) { bv_ = v; bi = ix; }
+      const int n = min(sm.gcount, kk);
+      float v = lane < n ? sm.gv[lane] : -1.f;
+      int ix = lane < n ? sm.gi[lane] : 0x7fffffff;
+#pragma unroll
+      for (int size = 2; size <= 32; size <<= 1)
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, v, stride);
+          const int oi = __shfl_xor_sync(0xffffffffu, ix, stride);
+          const bool want_better = ((lane & stride) == 0) == ((lane & size) == 0 || size == 32);
+          const bool take = want_better ? rbetter(ov, oi, v, ix) : rbetter(v, ix, ov, oi);
+          if (take) { v = ov; ix = oi; }
         }
-        warp_argmax(bv_, bi);
-        if (bv_ < 0.f) break;
-        if (lane == 0 && sm.nsel[i] < kRSel) {
-          sm.selv[i][sm.nsel[i]] = bv_;
-          sm.sel[i][sm.nsel[i]++] = bi;
-          if (bi < KG) sm.any_k = 1;
-        }
-        mv_ = bv_;
-        mi = bi;
-        __syncwarp();
+      const int base = sm.nsel[i];
+      if (lane < n) {
+        sm.sel[i][base + lane] = ix;
+        sm.selv[i][base + lane] = v;
       }
+      const bool hk = lane < n && ix < KG;
+      if (__any_sync(0xffffffffu, hk) && lane == 0) sm.any_k = 1;
+      __syncwarp();
+      if (lane == 0) sm.nsel[i] = base + n;
     }
     __syncthreads();
   };
@@ -527,21 +618,44 @@ __global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in
   const int ntot = sm.ntot;
   int reads_k = 0, reads_v = 0;
   const int R = d.R, G = d.G;
+  // INT3 rows with int8 scales decode a packed word (8 channels) per lane;
+  // other layouts decode channel by channel
+  const bool fast3 = d.bits == 3 && d.scale_mode == CAREKV_SCALE_INT8 && (D == 64 || D == 128) && d.gsize % 8 == 0;
+  const int WPR = D / 8;      // packed words (8 channels) per row
+  const int RG = 32 / WPR;    // rows one warp walks side by side
+  const int wl = lane % WPR, rg = lane / WPR;
   for (int i = 0; i < QN; ++i) {
-    if (tid == 0) {
-      int nkp = 0, nvs = 0;
-      for (int k = 0; k < sm.nsel[i]; ++k) {
-        const int e = sm.sel[i][k];
-        if (e >= KG) { sm.vsel[nvs++] = e - KG; ++reads_v; continue; }
-        ++reads_k;
-        const int p = e / d.SK;
-        int u = -1;
-        for (int x = 0; x < nkp; ++x) if (sm.kp_page[x] == p) u = x;
-        if (u < 0) { u = nkp++; sm.kp_page[u] = p; sm.kp_mask[u] = 0; }
-        sm.kp_mask[u] |= 1 << (e % d.SK);
+    // selected K pages (the first selection of a page leads it) and V slots
+    if (warp == 0) {
+      const int nsel = sm.nsel[i];
+      const int e = lane < nsel ? sm.sel[i][lane] : -1;
+      const bool isk = e >= 0 && e < KG, isv = e >= KG;
+      const int p = isk ? e / d.SK : -1;
+      bool leader = isk;
+      int msk = 0;
+      for (int k = 0; k < nsel; ++k) {
+        const int ek = sm.sel[i][k];
+        if (isk && ek < KG && ek / d.SK == p) {
+          if (k < lane) leader = false;
+          msk |= 1 << (ek % d.SK);
+        }
       }
-      sm.nkp = nkp;
-      sm.nvs = nvs;
+      const unsigned lt = (1u << lane) - 1u;
+      const unsigned bl = __ballot_sync(0xffffffffu, leader);
+      const unsigned bv = __ballot_sync(0xffffffffu, isv);
+      const unsigned bk = __ballot_sync(0xffffffffu, isk);
+      if (leader) {
+        const int u = __popc(bl & lt);
+        sm.kp_page[u] = p;
+        sm.kp_mask[u] = msk;
+      }
+      if (isv) sm.vsel[__popc(bv & lt)] = e - KG;
+      if (lane == 0) {
+        sm.nkp = __popc(bl);
+        sm.nvs = __popc(bv);
+        reads_k += __popc(bk);
+        reads_v += __popc(bv);
+      }
     }
     __syncthreads();
     const int nkp = sm.nkp, nvs = sm.nvs;
@@ -552,6 +666,10 @@ __global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in
       float acc = 0.f;
       for (int j = 0; j < d.SK; ++j) {
         if (!((sm.kp_mask[u] >> j) & 1)) continue;
+        if (a.kw != nullptr) {
+          acc += a.kw[((static_cast<int64_t>(bh) * QN + i) * KG + sm.kp_page[u] * d.SK + j) * kPage + t];
+          continue;
+        }
         const int grp = a.cache.k_slot_group[pg * d.SK + j];
         const uint4 raw = *reinterpret_cast<const uint4*>(a.cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes + t * 16);
         const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
@@ -582,7 +700,10 @@ __global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in
     __syncthreads();
     const float mshift = exact ? sm.mshift : 0.f;
     const float cbase = exact ? expf(-mshift) : 1.f;
-    float num[4] = {0.f, 0.f, 0.f, 0.f};
+    // numerator sum_S cf * V_hat + sum_V cf * R_V and z = sum over K tokens of cf:
+    // exact  dO = (cbase O + num) / (cbase + z) - O,   linear  dO = num - z O
+    float num[4] = {0.f, 0.f, 0.f, 0.f};   // channel lane + 32 jj (per-channel decode)
+    float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // channels 8 wl + j (word decode)
     float zp = 0.f;
     for (int item = warp; item < nkp + nvs; item += kRWarps) {
       uint8_t* stg = reinterpret_cast<uint8_t*>(sm.stage[warp]);
@@ -592,35 +713,41 @@ __global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in
         const int nv = a.cache.valid[pg];
         const float mv = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
         // stage the page's packed V rows and scales
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(a.cache.v_codes + pg * kPage * R);
-        for (int w = lane; w < kPage * R / 4; w += 32) sm.stage[warp][w] = src[w];
+        const uint4* src = reinterpret_cast<const uint4*>(a.cache.v_codes + pg * kPage * R);
+        uint4* dst = reinterpret_cast<uint4*>(sm.stage[warp]);
+        for (int w = lane; w < kPage * R / 16; w += 32) dst[w] = src[w];
         for (int x = lane; x < kPage * G; x += 32)
           sm.stage_sc[warp][x] = read_scale(a.cache.v_scale, pg * kPage * G + x, d.scale_mode, mv);
-        if (lane < kPage) {
-          float cf = 0.f;
-          if (lane < nv) {
-            const float A = exp2f((Sb[i * sst + p * kPage + lane] - sm.M[i]) * kRL2e) * sm.invL[i];
-            const float wk = sm.ds[u][lane];
-            if (exact) {
-              const float dsv = __fdiv_rn(wk, a.sqrt_d);
-              cf = A * (dsv <= 80.f ? cbase * expm1f(dsv) : expf(dsv - mshift) - cbase);
-            } else {
-              cf = A * wk * rp.k_corr_scale;
-            }
+        float cf = 0.f;
+        if (lane < kPage && lane < nv) {
+          const float A = exp2f((Sb[i * sst + p * kPage + lane] - sm.M[i]) * kRL2e) * sm.invL[i];
+          const float wk = sm.ds[u][lane];
+          if (exact) {
+            const float dsv = __fdiv_rn(wk, a.sqrt_d);
+            cf = A * (dsv <= 80.f ? cbase * expm1f(dsv) : expf(dsv - mshift) - cbase);
+          } else {
+            cf = A * wk * rp.k_corr_scale;
           }
-          sm.coef[warp][lane] = cf;
         }
+        if (lane < kPage) sm.coef[warp][lane] = cf;
+        zp += warp_sum(cf);
         __syncwarp();
-        for (int t = 0; t < nv; ++t) {
-          const float cf = sm.coef[warp][t];
-          if (exact) zp += cf;
+        if (fast3) {
+          for (int t = rg; t < nv; t += RG) {
+            const float sg = sm.stage_sc[warp][t * G + (8 * wl) / d.gsize];
+            acc_int3_word(stg + t * R, wl, pack_h2(sg, sg), sm.coef[warp][t], acc8);
+          }
+        } else {
+          for (int t = 0; t < nv; ++t) {
+            const float c = sm.coef[warp][t];
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const int c = lane + 32 * jj;
-            if (c < D) {
-              const float vh = f16r(__fmul_rn(static_cast<float>(unpack_code(stg + t * R, c, d.bits)),
-                                              sm.stage_sc[warp][t * G + c / d.gsize]));
-              num[jj] = fmaf(cf, exact ? vh : (vh - sm.O[i][c]), num[jj]);
+            for (int jj = 0; jj < 4; ++jj) {
+              const int ch = lane + 32 * jj;
+              if (ch < D) {
+                const float vh = f16r(__fmul_rn(static_cast<float>(unpack_code(stg + t * R, ch, d.bits)),
+                                                sm.stage_sc[warp][t * G + ch / d.gsize]));
+                num[jj] = fmaf(c, vh, num[jj]);
+              }
             }
           }
         }
@@ -651,29 +778,32 @@ __global__ void __launch_bounds__(256) route_kernel2(DecodeArgs a, int scores_in
           sm.coef[warp][lane] = cf;
         }
         __syncwarp();
-        for (int tt = 0; tt < t1 - t0; ++tt) {
-          const float cf = sm.coef[warp][tt];
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const int c = lane + 32 * jj;
-            if (c < D) num[jj] = fmaf(cf, unpack_nibble(stg, tt * D + c, rs), num[jj]);
-          }
-        }
+        // row r of the payload: D/2 bytes, channel c at nibble c of the row
+        for (int r = rg; r < t1 - t0; r += RG)
+          acc_nib_word(sm.stage[warp][r * WPR + wl], sm.coef[warp][r] * rs, acc8);
       }
       __syncwarp();
     }
+    // fold the word layout's row groups onto lanes 0 .. WPR-1
+    for (int o = WPR; o < 32; o <<= 1)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc8[j] += __shfl_xor_sync(0xffffffffu, acc8[j], o);
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       const int c = lane + 32 * jj;
       if (c < D) sm.acc[warp][c] = num[jj];
     }
+    __syncwarp();
+    if (lane < WPR)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sm.acc[warp][8 * lane + j] += acc8[j];
     if (lane == 0) sm.z[warp] = zp;
     __syncthreads();
     if (tid < D) {
-      float n = 0.f, z = cbase;
+      float n = 0.f, z = 0.f;
       for (int w = 0; w < kRWarps; ++w) { n += sm.acc[w][tid]; z += sm.z[w]; }
       const float ob = sm.O[i][tid];
-      const float delta = exact ? (__fdiv_rn(fmaf(cbase, ob, n), z) - ob) : n;
+      const float delta = exact ? (__fdiv_rn(fmaf(cbase, ob, n), cbase + z) - ob) : (n - z * ob);
       store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + tid, ob + delta, a.dt);
     }
     __syncthreads();
