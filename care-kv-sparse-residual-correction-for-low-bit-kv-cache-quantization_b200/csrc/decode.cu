@@ -18,6 +18,7 @@
 #include "common.cuh"
 #include "internal.h"
 #include "decode_args.h"
+#include "ptx.cuh"
 
 namespace carekv {
 
@@ -261,6 +262,12 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
   const bool live_k = rp.kind != CAREKV_KIND_NONE && rp.kind != CAREKV_KIND_V && rp.kscore_live &&
                       cfg.k_slots_per_page > 0;
   a.kw = (choose_pass(cfg) == Pass::NARROW && live_k) ? reinterpret_cast<float*>(w + wl.kw) : nullptr;
+  a.s_perm = 0;
+  a.dq_keys[0] = i3_key2(0, 0);
+  a.dq_keys[1] = i3_key2(3, 3);
+  a.dq_keys[2] = i3_key2(6, 6);
+  a.dq_keys[3] = 0x64086408u;
+  a.dq_keys[4] = 0x54805480u;
   a.sketch_proj = sketch_proj;
   a.rp = rp;
   a.force_generic = 0;

@@ -26,10 +26,21 @@ struct DecodeArgs {
   int* sel_out;     // [bh][qn][1 + kMaxSel]: count, then selected grid indices
   float* kw;        // [bh][qn][p_used*SK][16]: q . R_K per stored K slot and token, written by
                     // the narrow split-K pass when live K scoring runs there; null otherwise
+  int s_perm;       // 1: S and kw hold a page's 16 tokens in tok_pos() order
+  // fp16 magic keys of the exact low-bit dequantization (3-bit fields at
+  // mantissa bit 0, 3, 6; 4-bit fields at bit 0, 4), passed as arguments so
+  // the kernels hold them in registers instead of re-creating them per use
+  uint32_t dq_keys[5];
   const float* sketch_proj;
   carekv_route_params_t rp;
   int force_generic;  // 1: use the generic split-K pass (tests)
 };
+
+// Position of token t (0..15) inside a page's 16 logits: the narrow pass
+// stores tokens t and t+8 (t < 8) side by side, at 2t and 2t+1.
+__device__ __forceinline__ int tok_pos(int t, int perm) { return perm ? 2 * (t & 7) + (t >> 3) : t; }
+// Token held at position j (inverse of tok_pos).
+__device__ __forceinline__ int pos_tok(int j, int perm) { return perm ? (j >> 1) + 8 * (j & 1) : j; }
 
 template <int QN>
 cudaError_t launch_route(DecodeArgs& a, cudaStream_t st, int n_bh);

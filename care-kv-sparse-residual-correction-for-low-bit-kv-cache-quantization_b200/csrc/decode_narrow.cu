@@ -8,6 +8,8 @@
 // scoring is on (attention.py:167-184), it writes w = q . R_K for every
 // stored K residual slot, query and token (R_K = code * slot scale over the
 // slot's 32-channel group), so the router never re-reads slot payloads.
+// S and w are written in the pair order of tok_pos() (decode_args.h): the
+// lane that owns tokens t and t+8 stores them side by side.
 //
 // Orientation: tokens and channels sit on the M side of the MMAs and the
 // queries on N, as 8 columns = fp16 hi and lo halves of up to 4 queries:
@@ -16,16 +18,18 @@
 //     w^T [16 tok x 8]  = R_K [16 tok x 32] . Q_g^T [32 x 8]
 // A page costs D/16 MMAs per side, each thread keeps D/4 fp32 accumulators,
 // and the hi + lo split keeps ~22 significant bits of q and p, so S and O
-// match an fp32 evaluation to accumulation-order rounding.
+// match an fp32 evaluation to accumulation-order rounding.  The two pages of
+// a stage share one online-softmax update.
 //
 // Per warp: an NS-stage ring of bulk copies (cp.async.bulk + mbarrier,
 // bounded waits) stages CP contiguous pages at a time: packed K and V rows,
 // their int8 scale codes and the pages' K slot payloads.  Per-page metadata
 // (valid rows, fp16 masters, slot groups and scales) is read 32 pages at a
 // time into shared memory.  Dequantization is exact: 3-bit fields are moved
-// into fp16 mantissas (PRMT / LOP3), the offset removed with HSUB2 and the
-// scale applied with HMUL2, i.e. fp16(code * scale) rounded once, as the
-// reference dequantizes; scale codes become fp16(int8 * master) the same way.
+// to mantissa bit 0, 3 or 6 of an fp16 half (PRMT / SHF / LOP3), the offset
+// removed with HSUB2 and the scale applied with HMUL2, i.e. fp16(code *
+// scale) rounded once, as the reference dequantizes; scale codes become
+// fp16(int8 * master) the same way.
 #include "common.cuh"
 #include "internal.h"
 #include "decode_args.h"
@@ -63,6 +67,13 @@ __host__ __device__ inline Geo geo(int D, int G, int SK, bool kslot) {
   return g;
 }
 
+// 2^x with the SFU approximation (results below 2^-126 flush to zero).
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
 // 24-bit packed word at byte offset o of a staged row (bits 24..31 garbage).
@@ -71,37 +82,57 @@ __device__ __forceinline__ uint32_t word24_at(const uint8_t* row, int o) {
   return prmt(p[0], p[1], 0x3210 + 0x1111 * (o & 3));
 }
 
-// One packed word (8 codes f0..f7, 3 bits each) of a K row -> the four half2
-// operands of two k-steps: (f0,f3) (f1,f4) | (f2,f5) (f6,f7).
-__device__ __forceinline__ void k_quads(uint32_t W, uint32_t sig2, uint32_t (&o)[4]) {
-  const uint32_t t1 = prmt(W, W, 0x2110);  // low half W[0:16], high half W[8:24]
-  const uint32_t t2 = prmt(W, W, 0x2222);  // both halves W[16:24] in their low byte
-  o[0] = i3_pair<0, 1>(t1, sig2);
-  o[1] = i3_pair<3, 4>(t1, sig2);
-  o[2] = i3_pair<6, 7>(t1, sig2);
-  o[3] = i3_pair<2, 5>(t2, sig2);
-}
-// Same word of rows a (low half) and b (high half): field f of both rows.
-__device__ __forceinline__ void v_octs(uint32_t Wa, uint32_t Wb, uint32_t sig2, uint32_t (&o)[8]) {
-  const uint32_t r1 = prmt(Wa, Wb, 0x5410);
-  const uint32_t r2 = prmt(Wa, Wb, 0x6521);
-  const uint32_t r3 = prmt(Wa, Wb, 0x7632);
-  o[0] = i3_pair<0, 0>(r1, sig2);
-  o[1] = i3_pair<3, 3>(r1, sig2);
-  o[2] = i3_pair<6, 6>(r1, sig2);
-  o[3] = i3_pair<1, 1>(r2, sig2);
-  o[4] = i3_pair<4, 4>(r2, sig2);
-  o[5] = i3_pair<7, 7>(r2, sig2);
-  o[6] = i3_pair<2, 2>(r3, sig2);
-  o[7] = i3_pair<5, 5>(r3, sig2);
+// Magic keys of the field positions used below (DecodeArgs::dq_keys), held
+// in registers: a key is both the XOR operand of the LOP3 (whose immediate
+// slot holds the mask) and the subtrahend of the HSUB2.
+struct Keys {
+  uint32_t k0, k3, k6, n0, n4;
+};
+// exact half2 (code_lo, code_hi) * sig2 of two 3-bit fields at mantissa bit S
+template <int S>
+__device__ __forceinline__ uint32_t i3p(uint32_t t, uint32_t key, uint32_t sig2) {
+  uint32_t x;  // (t & mask) ^ key in one LOP3
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(x) : "r"(t), "n"(i3_mask2(S, S)), "r"(key));
+  return h2mul(h2sub(x, key), sig2);
 }
 
-// fp16 hi / lo halves of x packed as (hi, lo)
-__device__ __forceinline__ uint32_t hilo(float x) {
-  const __half hi = __float2half_rn(x);
-  const __half lo = __float2half_rn(x - __half2float(hi));
-  __half2 r = __halves2half2(hi, lo);
-  return *reinterpret_cast<uint32_t*>(&r);
+// One packed K word (codes f0..f7, 3 bits each) -> half2 operands
+// (f0,f3) (f1,f4) (f2,f5) (f6,f7), every field at mantissa bit 0, 3 or 6.
+__device__ __forceinline__ void k_quads(uint32_t W, uint32_t sig2, const Keys& K, uint32_t (&o)[4]) {
+  const uint32_t t1 = prmt(W, W >> 9, 0x5410);         // W[0:16] | W[9:25]
+  const uint32_t t2 = prmt(W >> 12, W >> 15, 0x5410);  // W[12:28] | W[15:31]
+  o[0] = i3p<0>(t1, K.k0, sig2);
+  o[1] = i3p<3>(t1, K.k3, sig2);
+  o[2] = i3p<6>(t1, K.k6, sig2);
+  o[3] = i3p<6>(t2, K.k6, sig2);
+}
+// The same packed word of two rows a (low halves) and b (high halves):
+// fields f0..f2 in r[0], f3..f5 in r[1], f6, f7 in r[2], at bits 0, 3, 6.
+struct VSrc {
+  uint32_t r[3];
+};
+__device__ __forceinline__ VSrc v_src(uint32_t Wa, uint32_t Wb) {
+  VSrc v;
+  v.r[0] = prmt(Wa, Wb, 0x5410);
+  v.r[1] = prmt(Wa, Wb, 0x6521) >> 1;
+  v.r[2] = prmt(Wa, Wb, 0x7632) >> 2;
+  return v;
+}
+template <int F>
+__device__ __forceinline__ uint32_t v_field(const VSrc& v, const Keys& K, uint32_t sig2) {
+  constexpr int S = 3 * (F < 6 ? F % 3 : F - 6);
+  const uint32_t key = S == 0 ? K.k0 : (S == 3 ? K.k3 : K.k6);
+  return i3p<S>(v.r[F < 3 ? 0 : (F < 6 ? 1 : 2)], key, sig2);
+}
+
+// 4-bit residual word (nibbles n0..n7) -> exact half2 codes (n0,n4) (n1,n5)
+// (n2,n6) (n3,n7): nibble at mantissa bit 0 or 4, offset removed by HSUB2.
+__device__ __forceinline__ void nib_quads(uint32_t u, const Keys& K, uint32_t (&o)[4]) {
+  const uint32_t v = u >> 8;
+  o[0] = h2sub((u & 0x000F000Fu) ^ K.n0, K.n0);
+  o[1] = h2sub((u & 0x00F000F0u) ^ K.n4, K.n4);
+  o[2] = h2sub((v & 0x000F000Fu) ^ K.n0, K.n0);
+  o[3] = h2sub((v & 0x00F000F0u) ^ K.n4, K.n4);
 }
 
 template <int QN, int D>
@@ -114,6 +145,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bars[kWarps][kNS];
   __shared__ float sm_m[kWarps][4], sm_l[kWarps][4];
+  __shared__ __align__(16) float q_sm[QN][D];
 
   const Dims d = make_dims(a.cfg);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -150,90 +182,203 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   }
   __syncwarp();
 
+  // bulk copies of chunk c (pages pa + 2c, pa + 2c + 1); sources are
+  // recomputed from the arguments on every issue (one lane, once per chunk)
   const int n_chunks = (pb - pa + kCP - 1) / kCP;
   auto issue = [&](int c) {
     const int p = pa + c * kCP;
     const int n = min(kCP, pb - p);
-    uint8_t* st = wsm + (c % kNS) * g.stage;
-    uint64_t* br = &bar[c % kNS];
+    const int slot = c % kNS;
+    uint8_t* st = wsm + slot * g.stage;
+    uint64_t* br = &bar[slot];
+    const int64_t pg = page0 + p;
     const uint32_t cbytes = n * kPage * R, sbytes = n * kPage * G;
     const uint32_t slbytes = kslot ? n * SK * 256 : 0;
     mbar_expect_tx(br, 2 * cbytes + 2 * sbytes + slbytes);
-    bulk_g2s(st, a.cache.k_codes + (page0 + p) * kPage * R, cbytes, br);
-    bulk_g2s(st + g.vOff, a.cache.v_codes + (page0 + p) * kPage * R, cbytes, br);
-    bulk_g2s(st + g.ksOff, reinterpret_cast<const int8_t*>(a.cache.k_scale) + (page0 + p) * kPage * G, sbytes, br);
-    bulk_g2s(st + g.vsOff, reinterpret_cast<const int8_t*>(a.cache.v_scale) + (page0 + p) * kPage * G, sbytes, br);
-    if (slbytes) bulk_g2s(st + g.slOff, a.cache.k_slot_data + (page0 + p) * SK * 256, slbytes, br);
+    bulk_g2s(st, a.cache.k_codes + pg * (kPage * R), cbytes, br);
+    bulk_g2s(st + g.vOff, a.cache.v_codes + pg * (kPage * R), cbytes, br);
+    bulk_g2s(st + g.ksOff, reinterpret_cast<const int8_t*>(a.cache.k_scale) + pg * kPage * G, sbytes, br);
+    bulk_g2s(st + g.vsOff, reinterpret_cast<const int8_t*>(a.cache.v_scale) + pg * kPage * G, sbytes, br);
+    if (slbytes) bulk_g2s(st + g.slOff, a.cache.k_slot_data + pg * SK * 256, slbytes, br);
   };
   if (lane == 0)
     for (int c = 0; c < min(kNS, n_chunks); ++c) issue(c);
 
-  // ── Q^T operands: column n = query n/2, half n%2 (0 = hi, 1 = lo) ──
+  // ── queries (fp32) in shared memory, then the Q^T operands ──
+  for (int x = threadIdx.x; x < QN * D; x += blockDim.x)
+    q_sm[x / D][x % D] = load_act(a.q, (static_cast<int64_t>(s) * Hq + h * QN) * D + x, a.dt);
+  __syncthreads();
+  // column n = query n/2, half n%2 (0 = hi, 1 = lo)
   const int qi = gid >> 1, part = gid & 1;
-  auto qval = [&](int c) -> float {
+  auto qp = [&](int c) -> float {
     if (qi >= QN) return 0.f;
-    const float x = load_act(a.q, (static_cast<int64_t>(s) * Hq + h * QN + qi) * D + c, a.dt);
+    const float x = q_sm[qi][c];
     const float hi = __half2float(__float2half_rn(x));
     return part ? x - hi : hi;
   };
   // K side: thread tig owns channels tig*D/4 .. +D/4 (KW packed words); word
   // i feeds k-steps 2i ((f0,f3) (f1,f4)) and 2i+1 ((f2,f5) (f6,f7)).
   uint32_t qb[KS][2];
-  {
-    const int c0 = tig * (D / 4);
 #pragma unroll
-    for (int i = 0; i < KW; ++i) {
-      const int c = c0 + 8 * i;
-      qb[2 * i][0] = pack_h2(qval(c + 0), qval(c + 3));
-      qb[2 * i][1] = pack_h2(qval(c + 1), qval(c + 4));
-      qb[2 * i + 1][0] = pack_h2(qval(c + 2), qval(c + 5));
-      qb[2 * i + 1][1] = pack_h2(qval(c + 6), qval(c + 7));
-    }
+  for (int i = 0; i < KW; ++i) {
+    const int c = tig * (D / 4) + 8 * i;
+    qb[2 * i][0] = pack_h2(qp(c + 0), qp(c + 3));
+    qb[2 * i][1] = pack_h2(qp(c + 1), qp(c + 4));
+    qb[2 * i + 1][0] = pack_h2(qp(c + 2), qp(c + 5));
+    qb[2 * i + 1][1] = pack_h2(qp(c + 6), qp(c + 7));
   }
-  // slot operands per 32-channel group: k-step ks takes channels
-  // 8*tig + 4*ks + {0,1} and {2,3} of the group (one nibble word per token)
+  // slot operands per 32-channel group: thread tig owns the group's channels
+  // 8*tig .. +8 (one nibble word per token); k-step 0 takes (n0,n4) (n1,n5),
+  // k-step 1 (n2,n6) (n3,n7)
   if (kslot) {
     for (int x = threadIdx.x; x < G4 * 2 * 32; x += blockDim.x) {
       const int grp = x / 64, ks = (x / 32) % 2, ln = x % 32;
-      const int lq = (ln >> 2) >> 1, lp = (ln >> 2) & 1, lt = ln & 3;
+      const int lq = (ln >> 2) >> 1, lp = (ln >> 2) & 1, c0 = grp * 32 + 8 * (ln & 3) + 2 * ks;
       float v[4] = {0.f, 0.f, 0.f, 0.f};
-      if (lq < QN)
+      if (lq < QN) {
+        const int cs[4] = {c0, c0 + 4, c0 + 1, c0 + 5};
         for (int e = 0; e < 4; ++e) {
-          const float xq = load_act(a.q, (static_cast<int64_t>(s) * Hq + h * QN + lq) * D + grp * 32 + 8 * lt +
-                                             4 * ks + e, a.dt);
+          const float xq = q_sm[lq][cs[e]];
           const float hi = __half2float(__float2half_rn(xq));
           v[e] = lp ? xq - hi : hi;
         }
+      }
       qs[x] = make_uint2(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]));
     }
     __syncthreads();
   }
 
+  const Keys KY = {a.dq_keys[0], a.dq_keys[1], a.dq_keys[2], a.dq_keys[3], a.dq_keys[4]};
   float o[KS][4];
 #pragma unroll
   for (int j = 0; j < KS; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_run = -INFINITY, l_part = 0.f;
-  float* Srow = a.S + (static_cast<int64_t>(bh) * QN + tig) * a.p_used * kPage;
-  float* Wrow = kslot ? a.kw + (static_cast<int64_t>(bh) * QN + tig) * KG * kPage : nullptr;
   const bool q_ok = tig < QN;
+  float* Srow = a.S + (static_cast<int64_t>(bh) * QN + tig) * a.p_used * kPage + 2 * gid;
+  float* Wrow = kslot ? a.kw + (static_cast<int64_t>(bh) * QN + tig) * KG * kPage + 2 * gid : nullptr;
 
   // V side: thread gid owns packed words (D=128) 2gid, 2gid+1 / (D=64) gid
-  constexpr int VB = D == 128 ? 6 : 3;  // byte offset multiplier of the thread's first word
+  constexpr int VB = D == 128 ? 6 : 3;
   const int vo = VB * gid;
   const int vbase = vo & ~3, voff = vo & 3;
   const uint32_t vsel_l = 0x3210 + 0x1111 * voff;
   const uint32_t vsel_h = (0x3210 + 0x1111 * (voff + 3)) & 0x7777;
-  const int gk = (tig * (D / 4)) / d.gsize;            // K scale group of the thread's channels
+  const int gk = (tig * (D / 4)) / d.gsize;              // K scale group of the thread's channels
   const int gv = ((D == 128 ? 16 : 8) * gid) / d.gsize;  // V scale group
-  const int ra = 2 * tig;                               // V rows ra, ra+1, ra+8, ra+9
-  const uint32_t psel = part ? 0x7632u : 0x5410u;
+  const int ra = 2 * tig;                                 // V rows ra, ra+1, ra+8, ra+9
   const int src_a = 8 * tig + qi, src_b = src_a + 4;
+  const int ko0 = gid * R + (D == 128 ? 12 : 6) * tig, ko8 = ko0 + 8 * R;
+  const int kso0 = gid * G + gk, kso8 = (gid + 8) * G + gk;
+  const int vso0 = ra * G + gv, vso1 = (ra + 1) * G + gv, vso2 = (ra + 8) * G + gv, vso3 = (ra + 9) * G + gv;
+
+  // logits of one staged page for rows gid, gid+8
+  auto k_side = [&](const uint8_t* st, int pp, uint32_t km2, float& s0, float& s1) {
+    const uint8_t* kc = st + pp * kPage * R;
+    const uint8_t* ks = st + g.ksOff + pp * kPage * G;
+    const uint32_t sig = i8_scale_pair(static_cast<uint32_t>(ks[kso0]) | (static_cast<uint32_t>(ks[kso8]) << 16), km2);
+    const uint32_t sig0 = prmt(sig, sig, 0x1010), sig8 = prmt(sig, sig, 0x3232);
+    uint32_t w0[KW], w8[KW];
+    if constexpr (D == 128) {
+      const uint32_t x0 = lds32(kc + ko0), x1 = lds32(kc + ko0 + 4), x2 = lds32(kc + ko0 + 8);
+      const uint32_t y0 = lds32(kc + ko8), y1 = lds32(kc + ko8 + 4), y2 = lds32(kc + ko8 + 8);
+      w0[0] = x0; w0[1] = prmt(x0, x1, 0x6543); w0[2] = prmt(x1, x2, 0x5432); w0[3] = x2 >> 8;
+      w8[0] = y0; w8[1] = prmt(y0, y1, 0x6543); w8[2] = prmt(y1, y2, 0x5432); w8[3] = y2 >> 8;
+    } else {
+#pragma unroll
+      for (int i = 0; i < KW; ++i) {
+        w0[i] = word24_at(kc + gid * R, 6 * tig + 3 * i);
+        w8[i] = word24_at(kc + (gid + 8) * R, 6 * tig + 3 * i);
+      }
+    }
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int i = 0; i < KW; ++i) {
+      uint32_t p0[4], p8[4];
+      k_quads(w0[i], sig0, KY, p0);
+      k_quads(w8[i], sig8, KY, p8);
+      mma_f16(acc[i & 1], p0[0], p8[0], p0[1], p8[1], qb[2 * i][0], qb[2 * i][1]);
+      mma_f16(acc[i & 1], p0[2], p8[2], p0[3], p8[3], qb[2 * i + 1][0], qb[2 * i + 1][1]);
+    }
+    s0 = __fmul_rn((acc[0][0] + acc[1][0]) + (acc[0][1] + acc[1][1]), a.sf);
+    s1 = __fmul_rn((acc[0][2] + acc[1][2]) + (acc[0][3] + acc[1][3]), a.sf);
+  };
+
+  // w = q . R_K of the page's stored K slots
+  auto slot_side = [&](const uint8_t* st, int pp, int p, int mi, int nv) {
+    if (nv == 0) return;
+    for (int j = 0; j < SK; ++j) {
+      const int grp = m_grp[mi * SK + j];
+      if (grp < 0 || grp >= G4) continue;
+      const uint8_t* sl = st + g.slOff + (pp * SK + j) * 256 + 4 * tig;
+      uint32_t n0[4], n8[4];
+      nib_quads(lds32(sl + gid * 16), KY, n0);
+      nib_quads(lds32(sl + (gid + 8) * 16), KY, n8);
+      const uint2 b0 = qs[(grp * 2 + 0) * 32 + lane];
+      const uint2 b1 = qs[(grp * 2 + 1) * 32 + lane];
+      float cw[4] = {0.f, 0.f, 0.f, 0.f};
+      mma_f16(cw, n0[0], n8[0], n0[1], n8[1], b0.x, b0.y);
+      mma_f16(cw, n0[2], n8[2], n0[3], n8[3], b1.x, b1.y);
+      const float rs = m_rs[mi * SK + j];
+      if (q_ok)
+        *reinterpret_cast<float2*>(Wrow + (static_cast<int64_t>(p) * SK + j) * kPage) =
+            make_float2(__fmul_rn(cw[0] + cw[1], rs), __fmul_rn(cw[2] + cw[3], rs));
+    }
+  };
+
+  // O^T += V_hat^T . P^T for one staged page
+  auto v_side = [&](const uint8_t* st, int pp, uint32_t vm2, uint32_t pb0, uint32_t pb1) {
+    const uint8_t* vc = st + g.vOff + pp * kPage * R;
+    const uint8_t* vs = st + g.vsOff + pp * kPage * G;
+    const uint32_t sA = i8_scale_pair(static_cast<uint32_t>(vs[vso0]) | (static_cast<uint32_t>(vs[vso1]) << 16), vm2);
+    const uint32_t sB = i8_scale_pair(static_cast<uint32_t>(vs[vso2]) | (static_cast<uint32_t>(vs[vso3]) << 16), vm2);
+    if constexpr (D == 128) {
+      uint32_t wl[4], wh[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const uint8_t* rp = vc + (ra + (r & 1) + 8 * (r >> 1)) * R + vbase;
+        const uint32_t lo = lds32(rp), hi = lds32(rp + 4);
+        wl[r] = prmt(lo, hi, vsel_l);
+        wh[r] = prmt(lo, hi, vsel_h);
+      }
+      const VSrc x0 = v_src(wl[0], wl[1]), x1 = v_src(wh[0], wh[1]);
+      const VSrc x2 = v_src(wl[2], wl[3]), x3 = v_src(wh[2], wh[3]);
+#define CK_VF(F) \
+  mma_f16(o[F], v_field<F>(x0, KY, sA), v_field<F>(x1, KY, sA), v_field<F>(x2, KY, sB), v_field<F>(x3, KY, sB), pb0, pb1);
+      CK_VF(0) CK_VF(1) CK_VF(2) CK_VF(3) CK_VF(4) CK_VF(5) CK_VF(6) CK_VF(7)
+#undef CK_VF
+    } else {
+      uint32_t wv[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) wv[r] = word24_at(vc + (ra + (r & 1) + 8 * (r >> 1)) * R, vo);
+      const VSrc x0 = v_src(wv[0], wv[1]), x1 = v_src(wv[2], wv[3]);
+#define CK_VF(F)                                                                                           \
+  mma_f16(o[F], v_field<F>(x0, KY, sA), v_field<F + 4>(x0, KY, sA), v_field<F>(x1, KY, sB), v_field<F + 4>(x1, KY, sB), \
+          pb0, pb1);
+      CK_VF(0) CK_VF(1) CK_VF(2) CK_VF(3)
+#undef CK_VF
+    }
+  };
+
+  // P^T operands of one page: tokens 2tig, 2tig+1 | 2tig+8, 2tig+9 of query
+  // qi, from the (hi, lo) pairs of the lanes that computed them
+  auto p_operands = [&](float pr0, float pr1, uint32_t& pb0, uint32_t& pb1) {
+    const uint32_t HI = pack_h2(pr0, pr1);
+    const float2 hf = __half22float2(*reinterpret_cast<const __half2*>(&HI));
+    const uint32_t LO = pack_h2(pr0 - hf.x, pr1 - hf.y);
+    const uint32_t T0 = prmt(HI, LO, 0x5410), T1 = prmt(HI, LO, 0x7632);  // (hi, lo) of token gid / gid+8
+    const uint32_t xa = __shfl_sync(0xffffffffu, T0, src_a), xb = __shfl_sync(0xffffffffu, T0, src_b);
+    const uint32_t ya = __shfl_sync(0xffffffffu, T1, src_a), yb = __shfl_sync(0xffffffffu, T1, src_b);
+    const uint32_t sel = part ? 0x7632u : 0x5410u;
+    pb0 = prmt(xa, xb, sel);
+    pb1 = prmt(ya, yb, sel);
+  };
 
   bool failed = false;
   int fail_chunk = n_chunks;
   for (int c = 0; c < n_chunks; ++c) {
     const int pbase = pa + c * kCP;
-    if (((pbase - pa) % kWin) == 0) {
+    const int mi = (pbase - pa) & (kWin - 1);
+    if (mi == 0) {
       // per-page metadata of the next window
       __syncwarp();
       const int p = pbase + lane;
@@ -268,138 +413,53 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
       break;
     }
     const uint8_t* st = wsm + (c % kNS) * g.stage;
-    const int npg = min(kCP, pb - pbase);
-    for (int pp = 0; pp < npg; ++pp) {
-      const int p = pbase + pp;
-      const int mi = (p - pa) % kWin;
-      const int nv = m_valid[mi];
-      const uint32_t km2 = m_km[mi], vm2 = m_vm[mi];
-      const uint8_t* kc = st + pp * kPage * R;
-      const uint8_t* vc = st + g.vOff + pp * kPage * R;
-      const uint8_t* ks = st + g.ksOff + pp * kPage * G;
-      const uint8_t* vs = st + g.vsOff + pp * kPage * G;
+    const bool two = pbase + 1 < pb;
+    const int nv0 = m_valid[mi], nv1 = two ? m_valid[mi + 1] : 0;
 
-      // ── S^T = K_hat . Q^T: rows gid, gid+8 ──
-      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-      {
-        const uint32_t sig = i8_scale_pair(static_cast<uint32_t>(ks[gid * G + gk]) |
-                                               (static_cast<uint32_t>(ks[(gid + 8) * G + gk]) << 16),
-                                           km2);
-        const uint32_t sig0 = prmt(sig, sig, 0x1010), sig8 = prmt(sig, sig, 0x3232);
-        uint32_t w0[KW], w8[KW];
-        if constexpr (D == 128) {
-          const uint8_t* r0 = kc + gid * R + 12 * tig;
-          const uint8_t* r8 = r0 + 8 * R;
-          const uint32_t x0 = lds32(r0), x1 = lds32(r0 + 4), x2 = lds32(r0 + 8);
-          const uint32_t y0 = lds32(r8), y1 = lds32(r8 + 4), y2 = lds32(r8 + 8);
-          w0[0] = x0; w0[1] = prmt(x0, x1, 0x6543); w0[2] = prmt(x1, x2, 0x5432); w0[3] = x2 >> 8;
-          w8[0] = y0; w8[1] = prmt(y0, y1, 0x6543); w8[2] = prmt(y1, y2, 0x5432); w8[3] = y2 >> 8;
-        } else {
-#pragma unroll
-          for (int i = 0; i < KW; ++i) {
-            w0[i] = word24_at(kc + gid * R, 6 * tig + 3 * i);
-            w8[i] = word24_at(kc + (gid + 8) * R, 6 * tig + 3 * i);
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < KW; ++i) {
-          uint32_t p0[4], p8[4];
-          k_quads(w0[i], sig0, p0);
-          k_quads(w8[i], sig8, p8);
-          mma_f16(acc[i & 1], p0[0], p8[0], p0[1], p8[1], qb[2 * i][0], qb[2 * i][1]);
-          mma_f16(acc[i & 1], p0[2], p8[2], p0[3], p8[3], qb[2 * i + 1][0], qb[2 * i + 1][1]);
-        }
-      }
-      const float s0 = __fmul_rn((acc[0][0] + acc[1][0]) + (acc[0][1] + acc[1][1]), a.sf);
-      const float s1 = __fmul_rn((acc[0][2] + acc[1][2]) + (acc[0][3] + acc[1][3]), a.sf);
-      const bool t0 = gid < nv, t1 = gid + 8 < nv;
-      if (q_ok) {
-        Srow[p * kPage + gid] = s0;
-        Srow[p * kPage + gid + 8] = s1;
-      }
+    // ── logits of both pages ──
+    float s00, s01, s10 = 0.f, s11 = 0.f;
+    k_side(st, 0, m_km[mi], s00, s01);
+    if (two) k_side(st, 1, m_km[mi + 1], s10, s11);
+    if (q_ok) {
+      *reinterpret_cast<float2*>(Srow + static_cast<int64_t>(pbase) * kPage) = make_float2(s00, s01);
+      if (two) *reinterpret_cast<float2*>(Srow + static_cast<int64_t>(pbase + 1) * kPage) = make_float2(s10, s11);
+    }
+    if (kslot) {
+      slot_side(st, 0, pbase, mi, nv0);
+      if (two) slot_side(st, 1, pbase + 1, mi + 1, nv1);
+    }
 
-      // ── w = q . R_K of the page's stored K slots ──
-      if (kslot) {
-        const int mrow = mi * SK;
-        for (int j = 0; j < SK; ++j) {
-          const int grp = m_grp[mrow + j];
-          if (grp < 0 || grp >= G4 || nv == 0) continue;
-          const uint8_t* sl = st + g.slOff + (pp * SK + j) * 256;
-          const uint32_t u0 = lds32(sl + gid * 16 + 4 * tig);
-          const uint32_t u8 = lds32(sl + (gid + 8) * 16 + 4 * tig);
-          const uint2 b0 = qs[(grp * 2 + 0) * 32 + lane];
-          const uint2 b1 = qs[(grp * 2 + 1) * 32 + lane];
-          float cw[4] = {0.f, 0.f, 0.f, 0.f};
-          mma_f16(cw, nib_pair(u0, 0), nib_pair(u8, 0), nib_pair(u0, 1), nib_pair(u8, 1), b0.x, b0.y);
-          mma_f16(cw, nib_pair(u0, 2), nib_pair(u8, 2), nib_pair(u0, 3), nib_pair(u8, 3), b1.x, b1.y);
-          const float rs = m_rs[mrow + j];
-          if (q_ok) {
-            float* wr = Wrow + (static_cast<int64_t>(p) * SK + j) * kPage;
-            wr[gid] = __fmul_rn(cw[0] + cw[1], rs);
-            wr[gid + 8] = __fmul_rn(cw[2] + cw[3], rs);
-          }
-        }
-      }
-
-      // ── online softmax for query tig over the page's 16 tokens ──
-      float pmax = fmaxf(t0 ? s0 : -INFINITY, t1 ? s1 : -INFINITY);
-      pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 4));
-      pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 8));
-      pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 16));
+    // ── online softmax for query tig over the stage's tokens ──
+    const bool v00 = gid < nv0, v01 = gid + 8 < nv0, v10 = gid < nv1, v11 = gid + 8 < nv1;
+    float pmax = fmaxf(fmaxf(v00 ? s00 : -INFINITY, v01 ? s01 : -INFINITY),
+                       fmaxf(v10 ? s10 : -INFINITY, v11 ? s11 : -INFINITY));
+    pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 4));
+    pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 8));
+    pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 16));
+    if (__any_sync(0xffffffffu, pmax > m_run)) {
       const float m_new = fmaxf(m_run, pmax);
-      if (__any_sync(0xffffffffu, m_new > m_run)) {
-        const float alpha = m_new > m_run ? (m_run == -INFINITY ? 0.f : exp2f((m_run - m_new) * kLog2e)) : 1.f;
-        l_part *= alpha;
+      const float alpha = m_new > m_run ? (m_run == -INFINITY ? 0.f : ex2((m_run - m_new) * kLog2e)) : 1.f;
+      l_part *= alpha;
 #pragma unroll
-        for (int j = 0; j < KS; ++j) {
-          o[j][0] *= alpha; o[j][1] *= alpha; o[j][2] *= alpha; o[j][3] *= alpha;
-        }
-        m_run = m_new;
+      for (int j = 0; j < KS; ++j) {
+        o[j][0] *= alpha; o[j][1] *= alpha; o[j][2] *= alpha; o[j][3] *= alpha;
       }
-      const float pr0 = t0 ? exp2f((s0 - m_run) * kLog2e) : 0.f;
-      const float pr1 = t1 ? exp2f((s1 - m_run) * kLog2e) : 0.f;
-      l_part += pr0 + pr1;
-      // P^T operand: tokens 2tig, 2tig+1 | 2tig+8, 2tig+9 of query qi
-      const uint32_t h0 = hilo(pr0), h1 = hilo(pr1);
-      const uint32_t xa = __shfl_sync(0xffffffffu, h0, src_a), xb = __shfl_sync(0xffffffffu, h0, src_b);
-      const uint32_t ya = __shfl_sync(0xffffffffu, h1, src_a), yb = __shfl_sync(0xffffffffu, h1, src_b);
-      const uint32_t pb0 = prmt(xa, xb, psel), pb1 = prmt(ya, yb, psel);
+      m_run = m_new;
+    }
+    const float mb = m_run * kLog2e;
+    const float p00 = v00 ? ex2(fmaf(s00, kLog2e, -mb)) : 0.f;
+    const float p01 = v01 ? ex2(fmaf(s01, kLog2e, -mb)) : 0.f;
+    const float p10 = v10 ? ex2(fmaf(s10, kLog2e, -mb)) : 0.f;
+    const float p11 = v11 ? ex2(fmaf(s11, kLog2e, -mb)) : 0.f;
+    l_part += (p00 + p01) + (p10 + p11);
 
-      // ── O^T += V_hat^T . P^T ──
-      const uint32_t sA = i8_scale_pair(static_cast<uint32_t>(vs[ra * G + gv]) |
-                                            (static_cast<uint32_t>(vs[(ra + 1) * G + gv]) << 16),
-                                        vm2);
-      const uint32_t sB = i8_scale_pair(static_cast<uint32_t>(vs[(ra + 8) * G + gv]) |
-                                            (static_cast<uint32_t>(vs[(ra + 9) * G + gv]) << 16),
-                                        vm2);
-      if constexpr (D == 128) {
-        uint32_t wl[4], wh[4];
-        const int rows[4] = {ra, ra + 1, ra + 8, ra + 9};
-#pragma unroll
-        for (int r = 0; r < 4; ++r) {
-          const uint8_t* rp = vc + rows[r] * R + vbase;
-          const uint32_t lo = lds32(rp), hi = lds32(rp + 4);
-          wl[r] = prmt(lo, hi, vsel_l);
-          wh[r] = prmt(lo, hi, vsel_h);
-        }
-        uint32_t al[8], ah[8], bl[8], bhh[8];
-        v_octs(wl[0], wl[1], sA, al);
-        v_octs(wh[0], wh[1], sA, ah);
-        v_octs(wl[2], wl[3], sB, bl);
-        v_octs(wh[2], wh[3], sB, bhh);
-#pragma unroll
-        for (int f = 0; f < 8; ++f) mma_f16(o[f], al[f], ah[f], bl[f], bhh[f], pb0, pb1);
-      } else {
-        uint32_t wv[4];
-        const int rows[4] = {ra, ra + 1, ra + 8, ra + 9};
-#pragma unroll
-        for (int r = 0; r < 4; ++r) wv[r] = word24_at(vc + rows[r] * R, vo);
-        uint32_t va[8], vb[8];
-        v_octs(wv[0], wv[1], sA, va);
-        v_octs(wv[2], wv[3], sB, vb);
-#pragma unroll
-        for (int f = 0; f < 4; ++f) mma_f16(o[f], va[f], va[f + 4], vb[f], vb[f + 4], pb0, pb1);
-      }
+    // ── values ──
+    uint32_t pb0, pb1;
+    p_operands(p00, p01, pb0, pb1);
+    v_side(st, 0, m_vm[mi], pb0, pb1);
+    if (two) {
+      p_operands(p10, p11, pb0, pb1);
+      v_side(st, 1, m_vm[mi + 1], pb0, pb1);
     }
     __syncwarp();
     if (lane == 0 && c + kNS < n_chunks) {
@@ -410,7 +470,8 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   if (failed && lane == 0) {
     // let the copies already issued land (bounded) before the staging area
     // is reused or the CTA exits
-    for (int c2 = fail_chunk; c2 < min(n_chunks, fail_chunk + kNS); ++c2) (void)mbar_wait(&bar[c2 % kNS], (c2 / kNS) & 1);
+    for (int c2 = fail_chunk; c2 < min(n_chunks, fail_chunk + kNS); ++c2)
+      (void)mbar_wait(&bar[c2 % kNS], (c2 / kNS) & 1);
   }
 
   // ── merge: per query tig, reduce l over the 8 row lanes, then the warps ──
@@ -473,6 +534,7 @@ cudaError_t launch_decode_narrow(DecodeArgs& a, cudaStream_t st, int n_bh) {
     if (e != cudaSuccess) return e;
     attr_bytes = smem;
   }
+  a.s_perm = 1;
   dim3 grid(n_bh, a.n_splits);
   narrow::decode_narrow<QN, D><<<grid, narrow::kWarps * 32, smem, st>>>(a);
   return cudaGetLastError();

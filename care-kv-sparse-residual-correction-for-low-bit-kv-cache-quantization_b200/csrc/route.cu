@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(256, 4) route_kernel2(DecodeArgs a, int scores
         const float sa[4] = {s4.x, s4.y, s4.z, s4.w};
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          if (4 * q4 + u < nv) {
+          if (pos_tok(4 * q4 + u, a.s_perm) < nv) {
             const float dS = __fdiv_rn(wa[u], a.sqrt_d);
             const float A = exp2f((sa[u] - sm.M[i]) * kRL2e) * sm.invL[i];
             const float term = dS * (A * (1.f - A));
@@ -264,9 +264,10 @@ __global__ void __launch_bounds__(256, 4) route_kernel2(DecodeArgs a, int scores
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
       if (gid < QN) {
         const float* srow = Sb + gid * sst + p * kPage;
-        const float2 sa = *reinterpret_cast<const float2*>(srow + 2 * tig);
-        const float2 sb2 = *reinterpret_cast<const float2*>(srow + 8 + 2 * tig);
-        s4[0] = sa.x; s4[1] = sa.y; s4[2] = sb2.x; s4[3] = sb2.y;
+        s4[0] = srow[tok_pos(2 * tig, a.s_perm)];
+        s4[1] = srow[tok_pos(2 * tig + 1, a.s_perm)];
+        s4[2] = srow[tok_pos(8 + 2 * tig, a.s_perm)];
+        s4[3] = srow[tok_pos(9 + 2 * tig, a.s_perm)];
       }
       float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -326,7 +327,7 @@ __global__ void __launch_bounds__(256, 4) route_kernel2(DecodeArgs a, int scores
       const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
       float sv[QN];
 #pragma unroll
-      for (int i = 0; i < QN; ++i) sv[i] = t < nv ? Sb[i * sst + p * kPage + t] : 0.f;
+      for (int i = 0; i < QN; ++i) sv[i] = t < nv ? Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] : 0.f;
       const float vn2 = a.cache.v_norm2[pg];
       const uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
       float r[32];
@@ -416,7 +417,8 @@ __global__ void __launch_bounds__(256, 4) route_kernel2(DecodeArgs a, int scores
         const float err = f16_bits_to_f32(a.cache.v_err[pg * d.NV + vb]);
         for (int i = 0; i < QN; ++i) {
           float mass = 0.f;
-          for (int t = t0; t < t1; ++t) mass += exp2f((Sb[i * sst + p * kPage + t] - sm.M[i]) * kRL2e) * sm.invL[i];
+          for (int t = t0; t < t1; ++t)
+            mass += exp2f((Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
           sc[i * NG + KG + e] = __fmul_rn(__fmul_rn(mass, err), rp.sensitivity);
         }
       } else {
@@ -667,7 +669,7 @@ __global__ void __launch_bounds__(256, 4) route_kernel2(DecodeArgs a, int scores
       for (int j = 0; j < d.SK; ++j) {
         if (!((sm.kp_mask[u] >> j) & 1)) continue;
         if (a.kw != nullptr) {
-          acc += a.kw[((static_cast<int64_t>(bh) * QN + i) * KG + sm.kp_page[u] * d.SK + j) * kPage + t];
+          acc += a.kw[((static_cast<int64_t>(bh) * QN + i) * KG + sm.kp_page[u] * d.SK + j) * kPage + tok_pos(t, a.s_perm)];
           continue;
         }
         const int grp = a.cache.k_slot_group[pg * d.SK + j];
@@ -720,7 +722,7 @@ __global__ void __launch_bounds__(256, 4) route_kernel2(DecodeArgs a, int scores
           sm.stage_sc[warp][x] = read_scale(a.cache.v_scale, pg * kPage * G + x, d.scale_mode, mv);
         float cf = 0.f;
         if (lane < kPage && lane < nv) {
-          const float A = exp2f((Sb[i * sst + p * kPage + lane] - sm.M[i]) * kRL2e) * sm.invL[i];
+          const float A = exp2f((Sb[i * sst + p * kPage + tok_pos(lane, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
           const float wk = sm.ds[u][lane];
           if (exact) {
             const float dsv = __fdiv_rn(wk, a.sqrt_d);
@@ -767,7 +769,7 @@ __global__ void __launch_bounds__(256, 4) route_kernel2(DecodeArgs a, int scores
           const int t = t0 + lane;
           float cf = 0.f;
           if (t < t1) {
-            const float A = exp2f((Sb[i * sst + p * kPage + t] - sm.M[i]) * kRL2e) * sm.invL[i];
+            const float A = exp2f((Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
             float w = 1.f;
             if (exact) {
               const float dsv = u >= 0 ? __fdiv_rn(sm.ds[u][t], a.sqrt_d) : 0.f;
