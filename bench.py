@@ -97,6 +97,22 @@ def parse_clocks(path, gpu_index):
             "samples": len(sm)}
 
 
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "decode_attention_llama2_mha_b32_ctx4096.md")
+
+
+def profiled_traffic():
+    """DRAM bytes (read + write) of one decode-attention call, from the ncu
+    summary committed under profiles/ (None when it is absent)."""
+    try:
+        with open(PROFILE_SUMMARY) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_launch:"):
+                    return int(line.split(":", 1)[1])
+    except OSError:
+        pass
+    return None
+
+
 def measured_peak_gbs():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
@@ -330,9 +346,10 @@ def main():
                     heads=w["heads"], kv_heads=w["kv_heads"], head_dim=w["head_dim"], base_bits=w["bits"],
                     group_size=w["group_size"], store_slots="1K+1V per page", read_ratio=w["read_ratio"],
                     correction="combined_kvscore+joint+normalize+exact", parallelism=f"dp{world} (batch-sharded)",
-                    l2="inputs larger than L2 (KV per layer call ~14 GB)", cuda_graph=True),
+                    l2="inputs larger than L2 (each layer call reads ~0.5 GB of KV; 32 layers ~16 GB)", cuda_graph=True),
         roofline=dict(bound="hbm", achieved=achieved, peak=peak, unit="GB/s", frac=achieved / peak,
-                      traffic=None, kernel="carekv_decode_attention (split-K pass + route)",
+                      traffic=profiled_traffic(), traffic_source="ncu dram__bytes_read+write, " +
+                      os.path.relpath(PROFILE_SUMMARY, ROOT), kernel="carekv_decode_attention (split-K pass + route)",
                       bytes_per_launch=bytes_call, launch_ms=res["att_ms"], peak_source=peak_kind),
         e2e=dict(value=e2e_tok_s, unit=UNIT, h2d_bytes_per_step=res["h2d"], d2h_bytes_per_step=res["d2h"]),
         gpu_launches=res["launches"],
