@@ -150,7 +150,8 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   const Dims d = make_dims(a.cfg);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int gid = lane >> 2, tig = lane & 3;
-  const int bh = blockIdx.x, split = blockIdx.y;
+  // consecutive CTAs share a (sequence, kv head): bh-major, split-minor
+  const int bh = blockIdx.x / a.n_splits, split = blockIdx.x % a.n_splits;
   const int s = bh / d.H, h = bh % d.H, b = a.seq_begin + s;
   const int64_t lhp = d.lhp(b, a.layer, h);
   const int np = min(a.cache.num_pages[lhp], a.p_used);
@@ -535,8 +536,7 @@ cudaError_t launch_decode_narrow(DecodeArgs& a, cudaStream_t st, int n_bh) {
     attr_bytes = smem;
   }
   a.s_perm = 1;
-  dim3 grid(n_bh, a.n_splits);
-  narrow::decode_narrow<QN, D><<<grid, narrow::kWarps * 32, smem, st>>>(a);
+  narrow::decode_narrow<QN, D><<<n_bh * a.n_splits, narrow::kWarps * 32, smem, st>>>(a);
   return cudaGetLastError();
 }
 

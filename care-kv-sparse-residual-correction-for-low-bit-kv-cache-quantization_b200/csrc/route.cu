@@ -1,820 +1,17 @@
-// Route + correct (kernels K4 + K2): one CTA of 8 warps per (sequence, kv head).
-//
-//  1. merge the split-K partials into O_base, M and L;
-//  2. score every stored residual slot: K slots with combined_kvscore
-//     (attention.py:167-184) or the sketch proxy (attention.py:718-725), one
-//     half-warp per slot (lane = token, 16-byte payload row per lane, all
-//     loads issued before use); V slots with block attention mass x error
-//     norm (attention.py:787-790), one thread per slot;
-//  3. normalise per query (attention.py:830-844) and select the joint or
-//     separate top-k (attention.py:856-875) with a two-level warp argmax,
-//     ties to the lower grid index;
-//  4. apply the exact softmax renormalisation (attention.py:96-118, in the
-//     sparse form dO = (O + sum_S A(e^ds-1)V + sum_V A e^ds R_V) /
-//     (1 + sum_S A(e^ds-1)) - O) or the linear form, one selected page or slot
-//     per warp, rows staged in shared memory, and write O = O_base + dO.
-//
-// Grid index: K entries (page, slot j) at p*SK + j, then V entries at
-// KG + p*SV + j; slot tables keep groups in ascending order, so the index
-// order is the reference's (page, group) order with K before V.
+// Route + correct kernel (K4 + K2) after the wide or generic split-K pass:
+// one CTA of 8 warps per (sequence, kv head) runs route_body (route_body.cuh).
 #include "common.cuh"
 #include "internal.h"
 #include "decode_args.h"
-#include "ptx.cuh"
+#include "route_body.cuh"
 
 namespace carekv {
-
-constexpr int kRSel = 32;     // selected slots per query (host-validated)
-constexpr float kREps = 1e-6f;
-constexpr float kRL2e = 1.4426950408889634f;
-constexpr int kRWarps = 8;
-
-__device__ __forceinline__ bool rbetter(float s1, int i1, float s2, int i2) {
-  return s1 > s2 || (s1 == s2 && i1 < i2);
-}
-
-__device__ __forceinline__ void warp_argmax(float& v, int& i) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
-    if (rbetter(ov, oi, v, i)) { v = ov; i = oi; }
-  }
-}
-
-// 24-bit packed word at byte offset o of a staged row (bits 24..31 garbage).
-__device__ __forceinline__ uint32_t rword24(const uint8_t* row, int o) {
-  const uint32_t* p = reinterpret_cast<const uint32_t*>(row + (o & ~3));
-  return prmt(p[0], p[1], 0x3210 + 0x1111 * (o & 3));
-}
-// acc[j] += cf * fp16(code_j * sigma) for the 8 channels of packed INT3 word w
-// of a row (exact fp16 dequantization: field -> mantissa, HSUB2, HMUL2)
-__device__ __forceinline__ void acc_int3_word(const uint8_t* row, int w, uint32_t sig2, float cf, float (&acc)[8]) {
-  const uint32_t W = rword24(row, 3 * w);
-  const uint32_t t = prmt(W, W << 13, 0x7610);         // low W[0:16], high W[3:19]
-  const uint32_t t2 = prmt(W >> 12, W << 1, 0x7610);   // low W[12:28], high W[15:31]
-  const uint32_t h[4] = {i3_pair<0, 0>(t, sig2), i3_pair<6, 6>(t, sig2), i3_pair<0, 0>(t2, sig2),
-                         i3_pair<6, 6>(t2, sig2)};
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[k]));
-    acc[2 * k] = fmaf(cf, f.x, acc[2 * k]);
-    acc[2 * k + 1] = fmaf(cf, f.y, acc[2 * k + 1]);
-  }
-}
-// acc[j] += c * code_j for the 8 nibbles of a 4-bit residual word
-__device__ __forceinline__ void acc_nib_word(uint32_t u, float c, float (&acc)[8]) {
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    const uint32_t hk = nib_pair(u, k);
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hk));
-    acc[2 * k] = fmaf(c, f.x, acc[2 * k]);
-    acc[2 * k + 1] = fmaf(c, f.y, acc[2 * k + 1]);
-  }
-}
-
-struct RouteSmem {
-  float Q[8][128];
-  float O[8][128];
-  float M[8], invL[8], L[8];
-  float red[kRWarps][8], red2[kRWarps][8];
-  float nk[8], nv[8];
-  int sel[8][kRSel];
-  float selv[8][kRSel];
-  int nsel[8];
-  int cnt[2][kRWarps];
-  float gv[kRSel];
-  int gi[kRSel];
-  int gcount;
-  float ds[kRSel][kPage];         // wK (unscaled q.R_K) per selected K page and token
-  int kp_page[kRSel], kp_mask[kRSel];
-  int vsel[kRSel];
-  float acc[kRWarps][128];
-  float z[kRWarps];
-  __align__(16) uint32_t stage[kRWarps][16 * 64 / 4 + 8];  // one page of packed V rows (<= 64 B each) or a V slot payload
-  __align__(16) uint32_t qfrag[4][2][32][4];  // A fragments of q_hi / q_lo per channel group and k-step
-  float stage_sc[kRWarps][16 * 4];           // the page's V scales (fp16 values)
-  float coef[kRWarps][kPage];
-  int cnt_k, cnt_v, ntot, any_k, nkp, nvs;
-  float mshift;
-};
 
 template <int QN>
 __global__ void __launch_bounds__(256, 4) route_kernel2(DecodeArgs a, int scores_in_smem) {
   __shared__ RouteSmem sm;
   extern __shared__ float dyn[];
-  const Dims d = make_dims(a.cfg);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int bh = blockIdx.x;
-  const int s = bh / d.H, h = bh % d.H;
-  const int b = a.seq_begin + s;
-  const int D = d.D;
-  const int Hq = d.H * QN;
-  const int64_t lhp = d.lhp(b, a.layer, h);
-  const int np = min(a.cache.num_pages[lhp], a.p_used);
-  const carekv_route_params_t& rp = a.rp;
-
-  // ── 1. queries and the merged split-K partials ──
-  for (int idx = tid; idx < QN * D; idx += blockDim.x) {
-    const int i = idx / D, c = idx % D;
-    sm.Q[i][c] = load_act(a.q, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + c, a.dt);
-  }
-  if (tid < QN) {
-    const int64_t base = static_cast<int64_t>(bh) * a.n_splits * QN + tid;
-    float M = -INFINITY;
-    for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, a.pm[base + sp * QN]);
-    float L = 0.f;
-    if (M != -INFINITY)
-      for (int sp = 0; sp < a.n_splits; ++sp) {
-        const float m = a.pm[base + sp * QN];
-        if (m != -INFINITY) L += a.pl[base + sp * QN] * exp2f((m - M) * kRL2e);
-      }
-    sm.M[tid] = M;
-    sm.L[tid] = L;
-    sm.invL[tid] = L > 0.f ? 1.0f / L : 0.f;
-  }
-  if (tid == 0) { sm.cnt_k = 0; sm.cnt_v = 0; sm.ntot = 0; sm.any_k = 0; }
-  __syncthreads();
-  for (int idx = tid; idx < QN * D; idx += blockDim.x) {
-    const int i = idx / D, c = idx % D;
-    float O = 0.f;
-    if (sm.L[i] > 0.f) {
-      const int64_t base = static_cast<int64_t>(bh) * a.n_splits * QN + i;
-      for (int sp = 0; sp < a.n_splits; ++sp) {
-        const float m = a.pm[base + sp * QN];
-        if (m != -INFINITY) O += a.po[(base + sp * QN) * D + c] * exp2f((m - sm.M[i]) * kRL2e);
-      }
-      O = __fdiv_rn(O, sm.L[i]);
-    }
-    sm.O[i][c] = O;
-  }
-  __syncthreads();
-
-  // A fragments for the slot dots: rows gid = q_hi, gid+8 = q_lo of query gid;
-  // k-step ks of group g covers channels g*32 + 8*tig + 4*ks + {0..3}
-  for (int x = tid; x < d.C * 2 * 32; x += blockDim.x) {
-    const int g = x / 64, ks = (x / 32) % 2, ln = x % 32;
-    const int qg = ln >> 2, tg = ln & 3;
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (qg < QN)
-      for (int e = 0; e < 4; ++e) v[e] = sm.Q[qg][g * 32 + 8 * tg + 4 * ks + e];
-    float hi[4], lo[4];
-    for (int e = 0; e < 4; ++e) { hi[e] = __half2float(__float2half_rn(v[e])); lo[e] = v[e] - hi[e]; }
-    sm.qfrag[g][ks][ln][0] = pack_h2(hi[0], hi[1]);
-    sm.qfrag[g][ks][ln][1] = pack_h2(lo[0], lo[1]);
-    sm.qfrag[g][ks][ln][2] = pack_h2(hi[2], hi[3]);
-    sm.qfrag[g][ks][ln][3] = pack_h2(lo[2], lo[3]);
-  }
-  __syncthreads();
-
-  auto write_base = [&]() {
-    if (tid < QN) a.sel_out[(static_cast<int64_t>(bh) * QN + tid) * (kRSel + 1)] = 0;
-    for (int idx = tid; idx < QN * D; idx += blockDim.x) {
-      const int i = idx / D, c = idx % D;
-      store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + c, sm.O[i][c], a.dt);
-    }
-  };
-  if (np == 0 || rp.kind == CAREKV_KIND_NONE) {
-    write_base();
-    return;
-  }
-
-  const int KG = a.p_used * d.SK;
-  const int VG = a.p_used * d.SV;
-  const int NG = KG + VG;
-  float* sc = scores_in_smem ? dyn : a.scores + static_cast<int64_t>(bh) * QN * NG;
-  const float* Sb = a.S + static_cast<int64_t>(bh) * QN * a.p_used * kPage;
-  const int64_t sst = static_cast<int64_t>(a.p_used) * kPage;
-  const bool kind_k = rp.kind == CAREKV_KIND_BOTH || rp.kind == CAREKV_KIND_K;
-  const bool kind_v = rp.kind == CAREKV_KIND_BOTH || rp.kind == CAREKV_KIND_V;
-  const bool may_k = kind_k && (rp.budget_mode == 0 ? rp.read_k > 0 : rp.ratio_k > 0.0);
-  const bool may_v = kind_v && (rp.budget_mode == 0 ? rp.read_v > 0 : rp.ratio_v > 0.0);
-
-  // ── 2a. K scores ──
-  if (a.kw != nullptr) {
-    // combined_kvscore from q . R_K precomputed by the split-K pass: one
-    // thread per (query, stored slot); ||dS * A(1-A)|| over the page's valid
-    // tokens * ||V_page||_F * sens
-    int cnt = 0;
-    for (int idx = tid; idx < QN * KG; idx += blockDim.x) {
-      const int i = idx / KG, e = idx - i * KG;
-      const int p = e / d.SK, j = e - p * d.SK;
-      const int64_t pg = lhp * d.P + p;
-      int grp = -1, nv = 0;
-      if (p < np) {
-        grp = a.cache.k_slot_group[pg * d.SK + j];
-        nv = a.cache.valid[pg];
-      }
-      const bool ok = grp >= 0 && nv > 0;
-      if (i == 0) cnt += ok;
-      if (!ok || !may_k) {
-        sc[i * NG + e] = -1.f;
-        continue;
-      }
-      const float4* wv = reinterpret_cast<const float4*>(a.kw + ((static_cast<int64_t>(bh) * QN + i) * KG + e) * kPage);
-      const float4* sv = reinterpret_cast<const float4*>(Sb + i * sst + p * kPage);
-      const float vc = sqrtf(a.cache.v_norm2[pg]);
-      float ss = 0.f;
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        const float4 w4 = wv[q4], s4 = sv[q4];
-        const float wa[4] = {w4.x, w4.y, w4.z, w4.w};
-        const float sa[4] = {s4.x, s4.y, s4.z, s4.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (pos_tok(4 * q4 + u, a.s_perm) < nv) {
-            const float dS = __fdiv_rn(wa[u], a.sqrt_d);
-            const float A = exp2f((sa[u] - sm.M[i]) * kRL2e) * sm.invL[i];
-            const float term = dS * (A * (1.f - A));
-            ss = fmaf(term, term, ss);
-          }
-        }
-      }
-      float ks = sqrtf(ss) * vc;
-      if (!(ks == ks) || isinf(ks)) ks = 0.f;
-      sc[i * NG + e] = fmaxf(ks, 0.f) * rp.sensitivity;
-    }
-    cnt = __reduce_add_sync(0xffffffffu, cnt);
-    if (lane == 0 && cnt) atomicAdd(&sm.cnt_k, cnt);
-  } else if (rp.kscore_live || !may_k) {
-    // combined_kvscore, one warp per stored slot: q . R_K^T on the tensor
-    // cores (codes as exact fp16 integers, slot scale applied after), then
-    // ||dS * A(1-A)|| over the page's valid tokens * ||V_page||_F * sens.
-    const int gid = lane >> 2, tig = lane & 3;
-    int cnt = 0;
-    for (int e = warp; e < KG; e += kRWarps) {
-      const int p = e / d.SK, j = e % d.SK;
-      const int64_t pg = lhp * d.P + p;
-      int grp = -1, nv = 0;
-      if (p < np) {
-        grp = a.cache.k_slot_group[pg * d.SK + j];
-        nv = a.cache.valid[pg];
-      }
-      const bool ok = grp >= 0 && nv > 0;
-      cnt += ok;
-      if (!ok || !may_k) {
-        if (lane < QN) sc[lane * NG + e] = -1.f;
-        continue;
-      }
-      const uint8_t* pay = a.cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes;
-      const uint32_t w0 = *reinterpret_cast<const uint32_t*>(pay + gid * 16 + 4 * tig);
-      const uint32_t w1 = *reinterpret_cast<const uint32_t*>(pay + (gid + 8) * 16 + 4 * tig);
-      const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
-      const float vc = sqrtf(a.cache.v_norm2[pg]);
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};
-      if (gid < QN) {
-        const float* srow = Sb + gid * sst + p * kPage;
-        s4[0] = srow[tok_pos(2 * tig, a.s_perm)];
-        s4[1] = srow[tok_pos(2 * tig + 1, a.s_perm)];
-        s4[2] = srow[tok_pos(8 + 2 * tig, a.s_perm)];
-        s4[3] = srow[tok_pos(9 + 2 * tig, a.s_perm)];
-      }
-      float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-      for (int ks = 0; ks < 2; ++ks) {
-        const uint4 af = *reinterpret_cast<const uint4*>(&sm.qfrag[grp][ks][lane][0]);
-        mma_f16(c0, af.x, af.y, af.z, af.w, nib_pair(w0, 2 * ks), nib_pair(w0, 2 * ks + 1));
-        mma_f16(c1, af.x, af.y, af.z, af.w, nib_pair(w1, 2 * ks), nib_pair(w1, 2 * ks + 1));
-      }
-      // tokens 2tig, 2tig+1 (c0) and 8+2tig, 9+2tig (c1) of query gid
-      float ss = 0.f;
-      if (gid < QN) {
-        const float dots[4] = {c0[0] + c0[2], c0[1] + c0[3], c1[0] + c1[2], c1[1] + c1[3]};
-        const int toks[4] = {2 * tig, 2 * tig + 1, 8 + 2 * tig, 9 + 2 * tig};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (toks[u] < nv) {
-            const float dS = __fdiv_rn(__fmul_rn(dots[u], rs), a.sqrt_d);
-            const float A = exp2f((s4[u] - sm.M[gid]) * kRL2e) * sm.invL[gid];
-            const float term = dS * (A * (1.f - A));
-            ss = fmaf(term, term, ss);
-          }
-        }
-      }
-      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-      if (tig == 0 && gid < QN) {
-        float ks = sqrtf(ss) * vc;
-        if (!(ks == ks) || isinf(ks)) ks = 0.f;
-        sc[gid * NG + e] = fmaxf(ks, 0.f) * rp.sensitivity;
-      }
-    }
-    if (lane == 0 && cnt) atomicAdd(&sm.cnt_k, cnt);
-  } else
-  {
-    const int half = lane >> 4, t = lane & 15;
-    const unsigned hm = 0xFFFFu << (16 * half);   // shuffles stay inside the half-warp
-    int cnt = 0;
-    for (int e0 = 2 * warp; e0 < KG; e0 += 2 * kRWarps) {
-      const int e = e0 + half;
-      const bool in = e < KG;
-      const int p = in ? e / d.SK : 0;
-      const int j = in ? e % d.SK : 0;
-      const int64_t pg = lhp * d.P + p;
-      int grp = -1, nv = 0;
-      if (in && p < np) {
-        grp = a.cache.k_slot_group[pg * d.SK + j];
-        nv = a.cache.valid[pg];
-      }
-      const bool ok = grp >= 0 && nv > 0;
-      if (t == 0 && ok) ++cnt;
-      if (!ok || !may_k) {
-        if (in && t < QN) sc[t * NG + e] = -1.f;
-        continue;
-      }
-      const uint8_t* pay = a.cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes;
-      const uint4 raw = *reinterpret_cast<const uint4*>(pay + t * 16);
-      const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
-      float sv[QN];
-#pragma unroll
-      for (int i = 0; i < QN; ++i) sv[i] = t < nv ? Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] : 0.f;
-      const float vn2 = a.cache.v_norm2[pg];
-      const uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
-      float r[32];
-#pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        int v = (wds[c >> 3] >> (4 * (c & 7))) & 15;
-        v = v > 7 ? v - 16 : v;
-        r[c] = __fmul_rn(static_cast<float>(v), rs);
-      }
-      const float* qb = &sm.Q[0][grp * d.kcg];
-      if (rp.kscore_live) {
-        const float vc = sqrtf(vn2);
-#pragma unroll
-        for (int i = 0; i < QN; ++i) {
-          float dot = 0.f;
-#pragma unroll
-          for (int c = 0; c < 32; ++c) dot = fmaf(qb[i * 128 + c], r[c], dot);
-          float term = 0.f;
-          if (t < nv) {
-            const float dS = __fdiv_rn(dot, a.sqrt_d);
-            const float A = exp2f((sv[i] - sm.M[i]) * kRL2e) * sm.invL[i];
-            term = dS * (A * (1.f - A));
-          }
-          float ss = term * term;
-          ss += __shfl_xor_sync(hm, ss, 8);
-          ss += __shfl_xor_sync(hm, ss, 4);
-          ss += __shfl_xor_sync(hm, ss, 2);
-          ss += __shfl_xor_sync(hm, ss, 1);
-          float ks = sqrtf(ss) * vc;
-          if (!(ks == ks) || isinf(ks)) ks = 0.f;
-          if (t == 0) sc[i * NG + e] = fmaxf(ks, 0.f) * rp.sensitivity;
-        }
-      } else {
-        // sketch proxy: mass * |q_sketch . k_sketch| * boundary * vdiff * sens
-        const float mv = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
-        for (int i = 0; i < QN; ++i) {
-          float A = 0.f, inv = 0.f, vd = 0.f;
-          if (t < nv) {
-            A = exp2f((sv[i] - sm.M[i]) * kRL2e) * sm.invL[i];
-            inv = __fdiv_rn(1.f, fmaxf(sm.M[i] - sv[i], kREps));
-            float acc = 0.f;
-            for (int c = 0; c < D; ++c) {
-              const float svv = read_scale(a.cache.v_scale, (pg * kPage + t) * d.G + c / d.gsize, d.scale_mode, mv);
-              const float vh = f16r(__fmul_rn(static_cast<float>(unpack_code(a.cache.v_codes + (pg * kPage + t) * d.R, c, d.bits)), svv));
-              const float df = vh - sm.O[i][c];
-              acc = fmaf(df, df, acc);
-            }
-            vd = sqrtf(acc);
-          }
-          float mass = A, bnd = A * inv, pvd = A * vd;
-#pragma unroll
-          for (int o = 8; o > 0; o >>= 1) {
-            mass += __shfl_xor_sync(hm, mass, o);
-            bnd += __shfl_xor_sync(hm, bnd, o);
-            pvd += __shfl_xor_sync(hm, pvd, o);
-          }
-          float qd = 0.f;
-          for (int jj = t; jj < d.sketch; jj += 16) {
-            float qs = 0.f;
-            for (int c = 0; c < d.kcg; ++c) qs = fmaf(sm.Q[i][grp * d.kcg + c], a.sketch_proj[c * d.sketch + jj], qs);
-            qd += qs * f16_bits_to_f32(a.cache.k_sketch[(pg * d.C + grp) * d.sketch + jj]);
-          }
-#pragma unroll
-          for (int o = 8; o > 0; o >>= 1) qd += __shfl_xor_sync(hm, qd, o);
-          if (t == 0) sc[i * NG + e] = mass * fabsf(qd) * bnd * pvd * rp.sensitivity;
-        }
-      }
-    }
-    cnt += __shfl_xor_sync(0xffffffffu, cnt, 16);
-    if (lane == 0 && cnt) atomicAdd(&sm.cnt_k, cnt);
-  }
-  // ── 2b. V scores: thread per grid entry; page token count ──
-  {
-    int cnt = 0, ntok = 0;
-    for (int e = tid; e < VG; e += blockDim.x) {
-      const int p = e / d.SV, j = e % d.SV;
-      const int64_t pg = lhp * d.P + p;
-      int vb = -1, nv = 0;
-      if (p < np) {
-        vb = a.cache.v_slot_block[pg * d.SV + j];
-        nv = a.cache.valid[pg];
-      }
-      const int t0 = vb * d.vtb, t1 = min(t0 + d.vtb, nv);
-      const bool ok = vb >= 0 && t1 > t0;
-      cnt += ok;
-      if (ok && may_v) {
-        const float err = f16_bits_to_f32(a.cache.v_err[pg * d.NV + vb]);
-        for (int i = 0; i < QN; ++i) {
-          float mass = 0.f;
-          for (int t = t0; t < t1; ++t)
-            mass += exp2f((Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
-          sc[i * NG + KG + e] = __fmul_rn(__fmul_rn(mass, err), rp.sensitivity);
-        }
-      } else {
-        for (int i = 0; i < QN; ++i) sc[i * NG + KG + e] = -1.f;
-      }
-    }
-    for (int p = tid; p < np; p += blockDim.x) ntok += a.cache.valid[lhp * d.P + p];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
-      ntok += __shfl_xor_sync(0xffffffffu, ntok, o);
-    }
-    if (lane == 0) {
-      if (cnt) atomicAdd(&sm.cnt_v, cnt);
-      if (ntok) atomicAdd(&sm.ntot, ntok);
-    }
-  }
-  __syncthreads();
-
-  // ── budgets (residual_router.py:37-76) ──
-  const int n_k = sm.cnt_k, n_v = sm.cnt_v;
-  const bool want_k = kind_k && n_k > 0, want_v = kind_v && n_v > 0;
-  int bk, bv;
-  {
-    const int tk = want_k ? n_k : 0, tv = want_v ? n_v : 0;
-    if (rp.budget_mode == 0) {
-      bk = rp.read_k;
-      bv = rp.read_v;
-    } else {
-      bk = (rp.ratio_k > 0.0 && tk > 0) ? max(1, static_cast<int>(static_cast<double>(tk) * rp.ratio_k)) : 0;
-      bv = (rp.ratio_v > 0.0 && tv > 0) ? max(1, static_cast<int>(static_cast<double>(tv) * rp.ratio_v)) : 0;
-    }
-    if (rp.kind == CAREKV_KIND_V) bk = 0;
-    if (rp.kind == CAREKV_KIND_K) bv = 0;
-    bk = min(bk, tk);
-    bv = min(bv, tv);
-  }
-  if ((!want_k && !want_v) || (bk == 0 && bv == 0)) {
-    write_base();
-    return;
-  }
-  const bool score_k = want_k && bk > 0, score_v = want_v && bv > 0;
-
-  // ── 3a. normalisation; kinds that take no part are not candidates ──
-  const bool norm = rp.score_normalize && rp.kind == CAREKV_KIND_BOTH && score_k && score_v;
-  if (norm) {
-    for (int i = 0; i < QN; ++i) {
-      float ak = 0.f, av = 0.f;
-      for (int e = tid; e < NG; e += blockDim.x) {
-        const float v = sc[i * NG + e];
-        if (v >= 0.f) { if (e < KG) ak += v; else av += v; }
-      }
-      ak = warp_sum(ak);
-      av = warp_sum(av);
-      if (lane == 0) { sm.red[warp][i] = ak; sm.red2[warp][i] = av; }
-    }
-    __syncthreads();
-    if (tid < QN) {
-      float x = 0.f, y = 0.f;
-      for (int w = 0; w < kRWarps; ++w) { x += sm.red[w][tid]; y += sm.red2[w][tid]; }
-      sm.nk[tid] = fmaxf(__fdiv_rn(x, static_cast<float>(n_k)), kREps);
-      sm.nv[tid] = fmaxf(__fdiv_rn(y, static_cast<float>(n_v)), kREps);
-    }
-    __syncthreads();
-  }
-  for (int e = tid; e < NG; e += blockDim.x) {
-    const bool part = e < KG ? score_k : score_v;
-    for (int i = 0; i < QN; ++i) {
-      float v = sc[i * NG + e];
-      if (!part) v = -1.f;
-      else if (norm && v >= 0.f) {
-        v = e < KG ? __fdiv_rn(v, sm.nk[i]) : __fdiv_rn(v, sm.nv[i]);
-        if (rp.kscore_live) v = __fmul_rn(v, e < KG ? rp.lambda_k : rp.lambda_v);
-      }
-      sc[i * NG + e] = v;
-    }
-  }
-  __syncthreads();
-
-  // ── 3b. selection ──
-  const bool joint = rp.joint && rp.kind == CAREKV_KIND_BOTH && score_k && score_v;
-  // Top-k of sc[i][lo:hi) by (score desc, index asc), appended to sel[i].
-  // A block-wide bisection on the score's bit pattern (non-negative floats
-  // order like their bits; excluded entries hold -1) finds the k-th score T:
-  // every entry above T is taken, and ties at T go to the lowest indices
-  // (a second bisection over the index bound, only when T is shared).  One
-  // warp then sorts the <= 32 picks.
-  int flip = 0;
-  auto skey = [](float v) -> uint32_t { return v >= 0.f ? __float_as_uint(v) + 1u : 0u; };
-  auto bcount = [&](int c) -> int {   // block-wide sum, one barrier (double-buffered slots)
-    c = __reduce_add_sync(0xffffffffu, c);
-    if (lane == 0) sm.cnt[flip][warp] = c;
-    __syncthreads();
-    int tot = 0;
-#pragma unroll
-    for (int w = 0; w < kRWarps; ++w) tot += sm.cnt[flip][w];
-    flip ^= 1;
-    return tot;
-  };
-  auto pick = [&](int i, int lo, int hi, int k) {
-    if (k <= 0 || hi <= lo) return;
-    const float* row = sc + i * NG;
-    auto count_ge = [&](uint32_t t) {
-      int c = 0;
-      for (int e = lo + tid; e < hi; e += blockDim.x) c += skey(row[e]) >= t;
-      return bcount(c);
-    };
-    const int n_cand = count_ge(1u);
-    const int room = kRSel - sm.nsel[i];
-    int kk = min(k, n_cand);
-    if (kk > room) {   // more picks than the selection table holds
-      if (tid == 0) atomicOr(a.cache.error_flag, 8);
-      kk = room;
-    }
-    if (kk <= 0) return;
-    uint32_t T = 1u;
-    int ibound = hi;   // take key > T, and key == T at indices < ibound
-    if (n_cand > kk) {
-      uint32_t tlo = 1u, thi = 0x7F800002u;
-      int c_lo = n_cand, c_hi = 0;   // counts at tlo (>= kk) and thi (< kk)
-      while (thi - tlo > 1u) {
-        const uint32_t mid = tlo + (thi - tlo) / 2u;
-        const int c = count_ge(mid);
-        if (c >= kk) { tlo = mid; c_lo = c; } else { thi = mid; c_hi = c; }
-      }
-      T = tlo;
-      const int need = kk - c_hi;   // ties at T to take
-      if (c_lo - c_hi > need) {
-        int ilo = lo, ihi = hi;     // smallest bound with #{key == T, e < bound} >= need
-        while (ihi - ilo > 0) {
-          const int mid = ilo + (ihi - ilo) / 2;
-          int c = 0;
-          for (int e = lo + tid; e < mid; e += blockDim.x) c += skey(row[e]) == T;
-          if (bcount(c) >= need) ihi = mid; else ilo = mid + 1;
-        }
-        ibound = ilo;
-      }
-    }
-    if (tid == 0) sm.gcount = 0;
-    __syncthreads();
-    for (int e = lo + tid; e < hi; e += blockDim.x) {
-      const uint32_t kv = skey(row[e]);
-      if (kv > T || (kv == T && e < ibound)) {
-        const int slot = atomicAdd(&sm.gcount, 1);
-        if (slot < kRSel) { sm.gv[slot] = row[e]; sm.gi[slot] = e; }
-      }
-    }
-    __syncthreads();
-    if (warp == 0) {
-      const int n = min(sm.gcount, kk);
-      float v = lane < n ? sm.gv[lane] : -1.f;
-      int ix = lane < n ? sm.gi[lane] : 0x7fffffff;
-#pragma unroll
-      for (int size = 2; size <= 32; size <<= 1)
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, v, stride);
-          const int oi = __shfl_xor_sync(0xffffffffu, ix, stride);
-          const bool want_better = ((lane & stride) == 0) == ((lane & size) == 0 || size == 32);
-          const bool take = want_better ? rbetter(ov, oi, v, ix) : rbetter(v, ix, ov, oi);
-          if (take) { v = ov; ix = oi; }
-        }
-      const int base = sm.nsel[i];
-      if (lane < n) {
-        sm.sel[i][base + lane] = ix;
-        sm.selv[i][base + lane] = v;
-      }
-      const bool hk = lane < n && ix < KG;
-      if (__any_sync(0xffffffffu, hk) && lane == 0) sm.any_k = 1;
-      __syncwarp();
-      if (lane == 0) sm.nsel[i] = base + n;
-    }
-    __syncthreads();
-  };
-  if (tid < QN) sm.nsel[tid] = 0;
-  __syncthreads();
-  for (int i = 0; i < QN; ++i) {
-    if (joint) {
-      const int mb = (bk > 0 && bv > 0) ? bk + bv : max(bk, bv);
-      pick(i, 0, NG, min(mb, n_k + n_v));
-    } else {
-      if (score_k) pick(i, 0, KG, bk);
-      if (score_v) pick(i, KG, NG, bv);
-    }
-  }
-  if (tid < QN) {
-    int* so = a.sel_out + (static_cast<int64_t>(bh) * QN + tid) * (kRSel + 1);
-    so[0] = sm.nsel[tid];
-    for (int k = 0; k < sm.nsel[tid]; ++k) so[1 + k] = sm.sel[tid][k];
-  }
-  if (scores_in_smem) {
-    float* g = a.scores + static_cast<int64_t>(bh) * QN * NG;
-    for (int e = tid; e < QN * NG; e += blockDim.x) g[e] = sc[e];
-  }
-  __syncthreads();
-
-  // ── 4. apply ──
-  const bool exact = rp.exact && sm.any_k;
-  const int ntot = sm.ntot;
-  int reads_k = 0, reads_v = 0;
-  const int R = d.R, G = d.G;
-  // INT3 rows with int8 scales decode a packed word (8 channels) per lane;
-  // other layouts decode channel by channel
-  const bool fast3 = d.bits == 3 && d.scale_mode == CAREKV_SCALE_INT8 && (D == 64 || D == 128) && d.gsize % 8 == 0;
-  const int WPR = D / 8;      // packed words (8 channels) per row
-  const int RG = 32 / WPR;    // rows one warp walks side by side
-  const int wl = lane % WPR, rg = lane / WPR;
-  for (int i = 0; i < QN; ++i) {
-    // selected K pages (the first selection of a page leads it) and V slots
-    if (warp == 0) {
-      const int nsel = sm.nsel[i];
-      const int e = lane < nsel ? sm.sel[i][lane] : -1;
-      const bool isk = e >= 0 && e < KG, isv = e >= KG;
-      const int p = isk ? e / d.SK : -1;
-      bool leader = isk;
-      int msk = 0;
-      for (int k = 0; k < nsel; ++k) {
-        const int ek = sm.sel[i][k];
-        if (isk && ek < KG && ek / d.SK == p) {
-          if (k < lane) leader = false;
-          msk |= 1 << (ek % d.SK);
-        }
-      }
-      const unsigned lt = (1u << lane) - 1u;
-      const unsigned bl = __ballot_sync(0xffffffffu, leader);
-      const unsigned bv = __ballot_sync(0xffffffffu, isv);
-      const unsigned bk = __ballot_sync(0xffffffffu, isk);
-      if (leader) {
-        const int u = __popc(bl & lt);
-        sm.kp_page[u] = p;
-        sm.kp_mask[u] = msk;
-      }
-      if (isv) sm.vsel[__popc(bv & lt)] = e - KG;
-      if (lane == 0) {
-        sm.nkp = __popc(bl);
-        sm.nvs = __popc(bv);
-        reads_k += __popc(bk);
-        reads_v += __popc(bv);
-      }
-    }
-    __syncthreads();
-    const int nkp = sm.nkp, nvs = sm.nvs;
-    // wK per (selected K page, token): q . R_K summed over the page's selected groups
-    for (int x = tid; x < nkp * kPage; x += blockDim.x) {
-      const int u = x / kPage, t = x % kPage;
-      const int64_t pg = lhp * d.P + sm.kp_page[u];
-      float acc = 0.f;
-      for (int j = 0; j < d.SK; ++j) {
-        if (!((sm.kp_mask[u] >> j) & 1)) continue;
-        if (a.kw != nullptr) {
-          acc += a.kw[((static_cast<int64_t>(bh) * QN + i) * KG + sm.kp_page[u] * d.SK + j) * kPage + tok_pos(t, a.s_perm)];
-          continue;
-        }
-        const int grp = a.cache.k_slot_group[pg * d.SK + j];
-        const uint4 raw = *reinterpret_cast<const uint4*>(a.cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes + t * 16);
-        const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
-        const uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
-        float dot = 0.f;
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          int v = (wds[c >> 3] >> (4 * (c & 7))) & 15;
-          v = v > 7 ? v - 16 : v;
-          dot = fmaf(sm.Q[i][grp * d.kcg + c], __fmul_rn(static_cast<float>(v), rs), dot);
-        }
-        acc += dot;
-      }
-      sm.ds[u][t] = acc;
-    }
-    __syncthreads();
-    if (exact && warp == 0) {
-      float mx = -INFINITY;
-      int covered = 0;
-      for (int u = 0; u < nkp; ++u) {
-        const int nv = a.cache.valid[lhp * d.P + sm.kp_page[u]];
-        covered += nv;
-        if (lane < nv) mx = fmaxf(mx, __fdiv_rn(sm.ds[u][lane], a.sqrt_d));
-      }
-      mx = warp_max(mx);
-      if (lane == 0) sm.mshift = (nkp == 0) ? 0.f : (covered >= ntot ? mx : fmaxf(mx, 0.f));
-    }
-    __syncthreads();
-    const float mshift = exact ? sm.mshift : 0.f;
-    const float cbase = exact ? expf(-mshift) : 1.f;
-    // numerator sum_S cf * V_hat + sum_V cf * R_V and z = sum over K tokens of cf:
-    // exact  dO = (cbase O + num) / (cbase + z) - O,   linear  dO = num - z O
-    float num[4] = {0.f, 0.f, 0.f, 0.f};   // channel lane + 32 jj (per-channel decode)
-    float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // channels 8 wl + j (word decode)
-    float zp = 0.f;
-    for (int item = warp; item < nkp + nvs; item += kRWarps) {
-      uint8_t* stg = reinterpret_cast<uint8_t*>(sm.stage[warp]);
-      if (item < nkp) {
-        const int u = item, p = sm.kp_page[u];
-        const int64_t pg = lhp * d.P + p;
-        const int nv = a.cache.valid[pg];
-        const float mv = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
-        // stage the page's packed V rows and scales
-        const uint4* src = reinterpret_cast<const uint4*>(a.cache.v_codes + pg * kPage * R);
-        uint4* dst = reinterpret_cast<uint4*>(sm.stage[warp]);
-        for (int w = lane; w < kPage * R / 16; w += 32) dst[w] = src[w];
-        for (int x = lane; x < kPage * G; x += 32)
-          sm.stage_sc[warp][x] = read_scale(a.cache.v_scale, pg * kPage * G + x, d.scale_mode, mv);
-        float cf = 0.f;
-        if (lane < kPage && lane < nv) {
-          const float A = exp2f((Sb[i * sst + p * kPage + tok_pos(lane, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
-          const float wk = sm.ds[u][lane];
-          if (exact) {
-            const float dsv = __fdiv_rn(wk, a.sqrt_d);
-            cf = A * (dsv <= 80.f ? cbase * expm1f(dsv) : expf(dsv - mshift) - cbase);
-          } else {
-            cf = A * wk * rp.k_corr_scale;
-          }
-        }
-        if (lane < kPage) sm.coef[warp][lane] = cf;
-        zp += warp_sum(cf);
-        __syncwarp();
-        if (fast3) {
-          for (int t = rg; t < nv; t += RG) {
-            const float sg = sm.stage_sc[warp][t * G + (8 * wl) / d.gsize];
-            acc_int3_word(stg + t * R, wl, pack_h2(sg, sg), sm.coef[warp][t], acc8);
-          }
-        } else {
-          for (int t = 0; t < nv; ++t) {
-            const float c = sm.coef[warp][t];
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              const int ch = lane + 32 * jj;
-              if (ch < D) {
-                const float vh = f16r(__fmul_rn(static_cast<float>(unpack_code(stg + t * R, ch, d.bits)),
-                                                sm.stage_sc[warp][t * G + ch / d.gsize]));
-                num[jj] = fmaf(c, vh, num[jj]);
-              }
-            }
-          }
-        }
-      } else {
-        const int ev = sm.vsel[item - nkp];
-        const int p = ev / d.SV, j = ev % d.SV;
-        const int64_t pg = lhp * d.P + p;
-        const int vb = a.cache.v_slot_block[pg * d.SV + j];
-        const int nv = a.cache.valid[pg];
-        const int t0 = vb * d.vtb, t1 = min(t0 + d.vtb, nv);
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(a.cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes);
-        for (int w = lane; w < d.vslot_bytes / 4; w += 32) sm.stage[warp][w] = src[w];
-        const float rs = f16_bits_to_f32(a.cache.v_slot_scale[pg * d.SV + j]);
-        int u = -1;
-        for (int x = 0; x < nkp; ++x) if (sm.kp_page[x] == p) u = x;
-        if (lane < d.vtb) {
-          const int t = t0 + lane;
-          float cf = 0.f;
-          if (t < t1) {
-            const float A = exp2f((Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
-            float w = 1.f;
-            if (exact) {
-              const float dsv = u >= 0 ? __fdiv_rn(sm.ds[u][t], a.sqrt_d) : 0.f;
-              w = dsv <= 80.f ? cbase * expf(dsv) : expf(dsv - mshift);
-            }
-            cf = A * w;
-          }
-          sm.coef[warp][lane] = cf;
-        }
-        __syncwarp();
-        // row r of the payload: D/2 bytes, channel c at nibble c of the row
-        for (int r = rg; r < t1 - t0; r += RG)
-          acc_nib_word(sm.stage[warp][r * WPR + wl], sm.coef[warp][r] * rs, acc8);
-      }
-      __syncwarp();
-    }
-    // fold the word layout's row groups onto lanes 0 .. WPR-1
-    for (int o = WPR; o < 32; o <<= 1)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc8[j] += __shfl_xor_sync(0xffffffffu, acc8[j], o);
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const int c = lane + 32 * jj;
-      if (c < D) sm.acc[warp][c] = num[jj];
-    }
-    __syncwarp();
-    if (lane < WPR)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) sm.acc[warp][8 * lane + j] += acc8[j];
-    if (lane == 0) sm.z[warp] = zp;
-    __syncthreads();
-    if (tid < D) {
-      float n = 0.f, z = 0.f;
-      for (int w = 0; w < kRWarps; ++w) { n += sm.acc[w][tid]; z += sm.z[w]; }
-      const float ob = sm.O[i][tid];
-      const float delta = exact ? (__fdiv_rn(fmaf(cbase, ob, n), cbase + z) - ob) : (n - z * ob);
-      store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + tid, ob + delta, a.dt);
-    }
-    __syncthreads();
-  }
-  if (a.cache.read_counter != nullptr && tid == 0) {
-    unsigned long long* rc = a.cache.read_counter + (static_cast<int64_t>(a.layer) * d.H + h) * 2;
-    if (sm.any_k && reads_k) atomicAdd(rc, static_cast<unsigned long long>(reads_k));
-    if (reads_v) atomicAdd(rc + 1, static_cast<unsigned long long>(reads_v));
-  }
+  route_body<QN, kRWarps>(a, blockIdx.x, sm, dyn, scores_in_smem);
 }
 
 template <int QN>
