@@ -13,6 +13,9 @@ from .quantizer import (QuantConfig, KQuantizer, VQuantizer, quantize, dequantiz
                         pack_int2_2d, unpack_int2_2d, pack_int3_2d, unpack_int3_2d, pack_int4_2d, unpack_int4_2d,
                         pack_codes_2d, unpack_codes_2d, packed_row_bytes, pack_4bit, unpack_4bit)
 from .engine import DecodeEngine
+from .layer import CAREKVLayer, causal_attention, resolve_prefill_mode
+from .llama_patch import CAREKVLlamaAttention, patch_llama_model, reset_all_caches
+from .adapter import CAREKVAdapter
 
 __version__ = "0.2.0+b200"
 
@@ -22,5 +25,6 @@ __all__ = [
     "QuantConfig", "KQuantizer", "VQuantizer", "quantize", "dequantize", "quantize_and_residual",
     "pack_int2_2d", "unpack_int2_2d", "pack_int3_2d", "unpack_int3_2d", "pack_int4_2d", "unpack_int4_2d",
     "pack_codes_2d", "unpack_codes_2d", "packed_row_bytes", "pack_4bit", "unpack_4bit",
-    "DecodeEngine",
+    "DecodeEngine", "CAREKVLayer", "causal_attention", "resolve_prefill_mode",
+    "CAREKVLlamaAttention", "patch_llama_model", "reset_all_caches", "CAREKVAdapter",
 ]

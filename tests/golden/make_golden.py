@@ -311,17 +311,53 @@ def gen_correction(out):
     print("correction.npz", len(cases), "cases")
 
 
+# ───────────────────────────── layer ─────────────────────────────
+def gen_layer(out):
+    """CAREKVLayer.prefill + decode_step of the reference (layer.py:643-1163)."""
+    import torch
+    sys.path.insert(0, HERE)
+    from layer_case import LAYER_CASES, layer_inputs, layer_cfg_kwargs
+    from CARE_KV.care_kv.cache import CacheConfig, CAREKVCache
+    from CARE_KV.care_kv.layer import CAREKVLayer
+    env = dict(CAREKV_K_CORRECTION_MODE="exact", CAREKV_KSCORE_LIVE="1", CAREKV_SCORE_NORMALIZE="1",
+               CAREKV_PREFILL_RESIDUAL_KIND="both", CAREKV_STORE_POLICY="residual_kind_aware")
+    arrays, cases = {}, []
+    for ci, (name, Hq, Hkv, D, T, S, mode, seed) in enumerate(LAYER_CASES):
+        os.environ.update(env)
+        os.environ["CAREKV_PREFILL_MODE"] = mode
+        L = T + S
+        W_Q, W_K, W_V, W_O, hid, cos, sin = [torch.from_numpy(x) for x in layer_inputs(Hq, Hkv, D, L, seed)]
+        cfg = CacheConfig(**layer_cfg_kwargs(Hq, Hkv, D, L))
+        layer = CAREKVLayer(cfg, 0, W_Q, W_K, W_V, W_O)
+        cache = CAREKVCache(cfg)
+        pre = layer.prefill(cache, hid[:T], position_embeddings=(cos[:, :T], sin[:, :T]))
+        dec = [layer.decode_step(cache, hid[T + j:T + j + 1], position_embeddings=(cos[:, T + j:T + j + 1],
+                                                                               sin[:, T + j:T + j + 1]))
+               for j in range(S)]
+        key = f"l{ci}"
+        arrays[key + "_prefill"] = as_np(pre)
+        arrays[key + "_decode"] = as_np(torch.cat(dec, dim=0))
+        cases.append(dict(key=key, name=name, Hq=Hq, Hkv=Hkv, D=D, T=T, steps=S, prefill_mode=mode, seed=seed))
+    for k in list(env) + ["CAREKV_PREFILL_MODE"]:
+        os.environ.pop(k, None)
+    arrays["meta"] = np.array(json.dumps(cases))
+    np.savez_compressed(os.path.join(out, "layer.npz"), **arrays)
+    print("layer.npz", len(cases), "cases")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("CAREKV_REFERENCE", "/root/reference"))
     ap.add_argument("--out", default=HERE)
+    ap.add_argument("--only", default="", help="comma list of quant,store,correction,layer")
     a = ap.parse_args()
     import_reference(a.reference)
     import torch
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    gen_quant(a.out)
-    gen_store(a.out)
-    gen_correction(a.out)
+    only = set(x for x in a.only.split(",") if x)
+    for nm, fn in (("quant", gen_quant), ("store", gen_store), ("correction", gen_correction), ("layer", gen_layer)):
+        if not only or nm in only:
+            fn(a.out)
 
 
 if __name__ == "__main__":
