@@ -11,7 +11,8 @@ from .config import (CacheConfig, apply_carekv_env_overrides, layer_budget_multi
 from .cache import CAREKVCache, PageMeta
 from .quantizer import (QuantConfig, KQuantizer, VQuantizer, quantize, dequantize, quantize_and_residual,
                         pack_int2_2d, unpack_int2_2d, pack_int3_2d, unpack_int3_2d, pack_int4_2d, unpack_int4_2d,
-                        pack_codes_2d, unpack_codes_2d, packed_row_bytes, pack_4bit, unpack_4bit)
+                        pack_codes_2d, unpack_codes_2d, packed_row_bytes, pack_4bit, unpack_4bit,
+                        quant_dequant_kivi_k, quant_dequant_kivi_v)
 from .engine import DecodeEngine
 from .layer import CAREKVLayer, causal_attention, resolve_prefill_mode
 from .llama_patch import CAREKVLlamaAttention, patch_llama_model, reset_all_caches
@@ -25,6 +26,7 @@ __all__ = [
     "QuantConfig", "KQuantizer", "VQuantizer", "quantize", "dequantize", "quantize_and_residual",
     "pack_int2_2d", "unpack_int2_2d", "pack_int3_2d", "unpack_int3_2d", "pack_int4_2d", "unpack_int4_2d",
     "pack_codes_2d", "unpack_codes_2d", "packed_row_bytes", "pack_4bit", "unpack_4bit",
+    "quant_dequant_kivi_k", "quant_dequant_kivi_v",
     "DecodeEngine", "CAREKVLayer", "causal_attention", "resolve_prefill_mode",
     "CAREKVLlamaAttention", "patch_llama_model", "reset_all_caches", "CAREKVAdapter",
 ]

@@ -73,6 +73,8 @@ SIGNATURES = [
     ("carekv_unpack_codes", i32, [vp, vp, i64, i32, i32, vp]),
     ("carekv_pack_4bit", i32, [vp, vp, vp, i64, i32, vp]),
     ("carekv_unpack_4bit", i32, [vp, vp, vp, i64, i32, vp]),
+    ("carekv_kivi_quant_dequant_k", i32, [vp, vp, i64, i32, i32, i32, i32, vp]),
+    ("carekv_kivi_quant_dequant_v", i32, [vp, vp, i64, i32, i32, i32, vp]),
     ("carekv_prefill_store", i32, [ctypes.POINTER(Config), ctypes.POINTER(Cache), i32, vp, vp, i32, i32, i32,
                                    ctypes.POINTER(StoreParams), vp, vp]),
     ("carekv_append", i32, [ctypes.POINTER(Config), ctypes.POINTER(Cache), i32, vp, vp, i32, i32,

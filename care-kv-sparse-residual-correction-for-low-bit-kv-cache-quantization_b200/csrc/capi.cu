@@ -151,6 +151,20 @@ int carekv_quantize(const void* x, int8_t* codes, void* scale, int64_t rows, int
   return cuda_status(launch_quantize(x, codes, scale, rows, D, bits, group_size, dtype, as_stream(stream)));
 }
 
+int carekv_kivi_quant_dequant_k(const void* K, void* out, int64_t n, int32_t T, int32_t D, int32_t bits,
+                                int32_t dtype, void* stream) {
+  if (!K || !out || n < 0 || T < 0 || D <= 0 || bits < 2 || bits > 8) return CAREKV_ERR_INVALID_ARG;
+  CHECK(validate_dtype(dtype));
+  return cuda_status(launch_kivi_k(K, out, n, T, D, bits, dtype, as_stream(stream)));
+}
+
+int carekv_kivi_quant_dequant_v(const void* V, void* out, int64_t rows, int32_t D, int32_t bits, int32_t dtype,
+                                void* stream) {
+  if (!V || !out || rows < 0 || D <= 0 || bits < 2 || bits > 8) return CAREKV_ERR_INVALID_ARG;
+  CHECK(validate_dtype(dtype));
+  return cuda_status(launch_kivi_v(V, out, rows, D, bits, dtype, as_stream(stream)));
+}
+
 int carekv_dequantize(const int8_t* codes, const void* scale, void* out, int64_t rows, int32_t D,
                       int32_t group_size, int32_t dtype, void* stream) {
   if (!codes || !scale || !out || rows < 0 || D <= 0 || group_size <= 0 || D % group_size) return CAREKV_ERR_INVALID_ARG;

@@ -169,3 +169,27 @@ def unpack_4bit(packed: Tensor, scale: Tensor, numel: int) -> Tensor:
     _lib.check(_lib.lib().carekv_unpack_4bit(packed.data_ptr(), sc.data_ptr(), out.data_ptr(), 1, n2,
                                              _stream(packed)), "unpack_4bit")
     return out[:numel]
+
+
+def quant_dequant_kivi_k(K: Tensor, bits: int) -> Tensor:
+    """kivi_helpers.py:35-46: K (..., T, D) -> symmetric INT`bits`
+    quantize-dequantize with a per-channel scale over T, in K's dtype."""
+    K = _cuda(K, "quant_dequant_kivi_k").contiguous()
+    T, D = K.shape[-2], K.shape[-1]
+    n = K.numel() // (T * D) if T * D else 0
+    out = torch.empty_like(K)
+    _lib.check(_lib.lib().carekv_kivi_quant_dequant_k(K.data_ptr(), out.data_ptr(), n, T, D, bits, _DT[K.dtype],
+                                                      _stream(K)), "quant_dequant_kivi_k")
+    return out
+
+
+def quant_dequant_kivi_v(V: Tensor, bits: int) -> Tensor:
+    """kivi_helpers.py:49-59: V (..., T, D) -> symmetric INT`bits`
+    quantize-dequantize with a per-token scale over D, in V's dtype."""
+    V = _cuda(V, "quant_dequant_kivi_v").contiguous()
+    D = V.shape[-1]
+    rows = V.numel() // D if D else 0
+    out = torch.empty_like(V)
+    _lib.check(_lib.lib().carekv_kivi_quant_dequant_v(V.data_ptr(), out.data_ptr(), rows, D, bits, _DT[V.dtype],
+                                                      _stream(V)), "quant_dequant_kivi_v")
+    return out

@@ -11,6 +11,7 @@
  *   quantizer.py:31-99, 257-383     -> carekv_quantize / carekv_dequantize /
  *                                      carekv_pack_codes / carekv_unpack_codes
  *   residual_store.py:121-146       -> carekv_pack_4bit / carekv_unpack_4bit
+ *   kivi_helpers.py:35-59           -> carekv_kivi_quant_dequant_k / _v
  *   cache.py:430-536 (buffers)      -> carekv_cache_layout / carekv_cache_init
  *   layer.py:204-334 + cache.py:617-654 + residual_store.py:239-464
  *                                   -> carekv_prefill_store
@@ -171,6 +172,16 @@ int carekv_pack_4bit(const float *x, uint8_t *packed, uint16_t *scale_f16, int64
                      void *stream);
 int carekv_unpack_4bit(const uint8_t *packed, const uint16_t *scale_f16, float *out, int64_t n,
                        int32_t numel, void *stream);
+
+/* KIVI-style quantize-dequantize (kivi_helpers.py:35-59), in dtype:
+ * _k: K [n][T][D], symmetric INT`bits` codes with a per-channel scale
+ *     amax over T / qmax (quant_dequant_kivi_k);
+ * _v: V [rows][D], per-token scale amax over D / qmax (quant_dequant_kivi_v).
+ * out may alias the input. */
+int carekv_kivi_quant_dequant_k(const void *K, void *out, int64_t n, int32_t T, int32_t D, int32_t bits,
+                                int32_t dtype, void *stream);
+int carekv_kivi_quant_dequant_v(const void *V, void *out, int64_t rows, int32_t D, int32_t bits,
+                                int32_t dtype, void *stream);
 
 /* ---- cache path ----------------------------------------------------------- */
 /* Prefill store of `T` rows for sequences [seq_begin, seq_begin+seq_count)

@@ -173,3 +173,21 @@ def int8_scale_append(scale_row, master):
 def int8_scale_read(codes, master):
     """_maybe_dequant_scale (cache.py:713-718): fp16(code · master)."""
     return round_to(np.asarray(codes, np.float32) * np.float32(master), F16)
+
+
+def kivi_quant_dequant(x, bits, dt, axis):
+    """quant_dequant_kivi_k (axis=-2: per-channel scale over the token axis)
+    and quant_dequant_kivi_v (axis=-1: per-token scale over the channels) of
+    kivi_helpers.py:35-59.  scale = amax / qmax, then clamp(min=1e-8), all in
+    ``dt``; codes = clamp(round(x / scale), qmin, qmax); out = codes * scale.
+    NaN (0/0 on an all-zero fp16 slice, where the clamp bound is 0) stays NaN."""
+    x = np.asarray(x, dtype=np.float32)
+    qmax = 2 ** (bits - 1) - 1
+    amax = np.abs(x).max(axis=axis, keepdims=True)
+    scale = round_to(amax / np.float32(qmax), dt)
+    lo = np.float32(scalar_in(dt, 1e-8))
+    scale = np.where(scale < lo, lo, scale)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        q = np.round(round_to(x / scale, dt))
+        q = np.clip(q, -qmax - 1, qmax)
+        return round_to(q * scale, dt)

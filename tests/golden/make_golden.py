@@ -311,6 +311,34 @@ def gen_correction(out):
     print("correction.npz", len(cases), "cases")
 
 
+# ───────────────────────────── KIVI helpers ─────────────────────────────
+def gen_kivi(out):
+    """quant_dequant_kivi_k / _v (kivi_helpers.py:35-59) on seeded (B, H, T, D)."""
+    import torch
+    from CARE_KV.care_kv.kivi_helpers import quant_dequant_kivi_k, quant_dequant_kivi_v
+    g = torch.Generator().manual_seed(77)
+    arrays, cases = {}, []
+    ci = 0
+    for dt in ("fp32", "fp16", "bf16"):
+        for bits in (2, 3, 4):
+            for shape, special in (((1, 2, 19, 64), False), ((1, 2, 9, 128), True)):
+                x = torch.randn(*shape, generator=g) * 3.0
+                x[..., :2] *= 25.0
+                if special:
+                    x[0, 0, :, 5] = 0.0        # an all-zero channel (K scale)
+                    x[0, 1, 3, :] = 0.0        # an all-zero token (V scale)
+                x = x.to(tdt(dt))
+                key = f"k{ci}"
+                arrays[key + "_x"] = as_np(x)
+                arrays[key + "_k"] = as_np(quant_dequant_kivi_k(x, bits))
+                arrays[key + "_v"] = as_np(quant_dequant_kivi_v(x, bits))
+                cases.append(dict(key=key, dtype=dt, bits=bits, shape=list(shape)))
+                ci += 1
+    arrays["meta"] = np.array(json.dumps(cases))
+    np.savez_compressed(os.path.join(out, "kivi.npz"), **arrays)
+    print("kivi.npz", len(cases), "cases")
+
+
 # ───────────────────────────── layer ─────────────────────────────
 def gen_layer(out):
     """CAREKVLayer.prefill + decode_step of the reference (layer.py:643-1163)."""
@@ -349,13 +377,14 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("CAREKV_REFERENCE", "/root/reference"))
     ap.add_argument("--out", default=HERE)
-    ap.add_argument("--only", default="", help="comma list of quant,store,correction,layer")
+    ap.add_argument("--only", default="", help="comma list of quant,store,correction,layer,kivi")
     a = ap.parse_args()
     import_reference(a.reference)
     import torch
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     only = set(x for x in a.only.split(",") if x)
-    for nm, fn in (("quant", gen_quant), ("store", gen_store), ("correction", gen_correction), ("layer", gen_layer)):
+    for nm, fn in (("quant", gen_quant), ("store", gen_store), ("correction", gen_correction), ("layer", gen_layer),
+                   ("kivi", gen_kivi)):
         if not only or nm in only:
             fn(a.out)
 

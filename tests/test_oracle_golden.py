@@ -158,3 +158,17 @@ def test_correction_golden(ci):
         np.testing.assert_allclose(delta, z[f"{key}_delta_{h}"], rtol=1e-4, atol=2e-6)
         if c["name"] == "read0":
             assert np.all(delta == 0)
+
+
+# ───────────────────────────── KIVI helpers ─────────────────────────────
+KIVI = np.load(os.path.join(GOLDEN, "kivi.npz"))
+KIVI_META = json.loads(str(KIVI["meta"]))
+
+
+@pytest.mark.parametrize("case", KIVI_META, ids=[f"{c['dtype']}_b{c['bits']}_{c['key']}" for c in KIVI_META])
+def test_oracle_kivi_matches_reference(case):
+    from oracle.quant import kivi_quant_dequant
+    x = KIVI[case["key"] + "_x"]
+    for axis, name in ((-2, "_k"), (-1, "_v")):
+        got = kivi_quant_dequant(x, case["bits"], case["dtype"], axis)
+        np.testing.assert_array_equal(got, KIVI[case["key"] + name], err_msg=f"{case['key']}{name}")
