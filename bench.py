@@ -167,6 +167,22 @@ def cpu_baseline(seconds=12.0, N=None, seed=0):
 
 
 # ───────────────────────────── GPU arm ─────────────────────────────
+def max_over_ranks(values, world, device=None):
+    """Elementwise max of per-rank timings (all_reduce MAX; every rank gets it)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(list(values), dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
+def aggregate_tok_s(world, batch_per_rank, steps, ms_max):
+    """Whole-job tokens/s: every rank decodes `batch_per_rank` sequences per
+    step (weak scaling), timed as the slowest rank."""
+    return world * batch_per_rank * steps / (ms_max / 1e3)
+
+
 def run_gpu(args, rank, world):
     import torch
     import torch.distributed as dist
@@ -269,10 +285,7 @@ def run_gpu(args, rank, world):
     torch.cuda.synchronize()
     e2e_ms = f0.elapsed_time(f1)
 
-    t = torch.tensor([ms, e2e_ms, statistics.mean(att_ms)], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, e2e_ms, att_mean = t.tolist()
+    ms, e2e_ms, att_mean = max_over_ranks([ms, e2e_ms, statistics.mean(att_ms)], world, dev)
     res = dict(ms=ms, e2e_ms=e2e_ms, att_ms=att_mean, launches=launches, ctx_end=ctx_end,
                clocks=parse_clocks(clk_path, dev.index) if rank == 0 else None,
                out_finite=bool(torch.isfinite(out.float()).all().item()),
@@ -331,8 +344,8 @@ def main():
     if rank != 0:
         return
     B, L = w["batch"], args.layers
-    tok_s = world * B * args.steps / (res["ms"] / 1e3)
-    e2e_tok_s = world * B * args.e2e_steps / (res["e2e_ms"] / 1e3)
+    tok_s = aggregate_tok_s(world, B, args.steps, res["ms"])
+    e2e_tok_s = aggregate_tok_s(world, B, args.e2e_steps, res["e2e_ms"])
     peak, peak_kind = measured_peak_gbs()
     N_mid = res["ctx_end"]
     bytes_call = B * w["kv_heads"] * algorithmic_bytes_per_kvh(N_mid, D=w["head_dim"], bits=w["bits"],

@@ -1,0 +1,56 @@
+"""The N>1 host logic of bench.py on CPU: two gloo ranks (127.0.0.1).
+
+Each rank owns its own batch (weak scaling); the job time is the max over
+ranks of the device timings, which every rank receives, and the aggregate
+throughput counts every rank's sequences.  The path has no data collective;
+this covers the only exchange bench.py makes.
+"""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import bench
+        mine = [10.0 + 5 * rank, 20.0 - 3 * rank, 1.5 + rank]
+        got = bench.max_over_ranks(mine, world)
+        q.put((rank, got, bench.aggregate_tok_s(world, 32, 10, got[0])))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(120)
+def test_two_gloo_ranks_max_and_aggregate():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=100) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, got, tok in res:
+        assert got == [15.0, 20.0, 2.5]
+        assert tok == pytest.approx(2 * 32 * 10 / 0.015)
+
+
+def test_single_rank_passthrough():
+    import bench
+    assert bench.max_over_ranks([1.0, 2.0], 1) == [1.0, 2.0]
+    assert bench.aggregate_tok_s(1, 32, 20, 100.0) == pytest.approx(6400.0)
