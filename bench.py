@@ -333,7 +333,10 @@ def main():
     import torch.distributed as dist
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        # bind this rank's GPU before NCCL starts (no device guessing by rank)
+        local = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=local)
     if args.steps < 1 or args.warmup < 3:
         raise SystemExit("need --steps >= 1 and --warmup >= 3")
     res = run_gpu(args, rank, world)
