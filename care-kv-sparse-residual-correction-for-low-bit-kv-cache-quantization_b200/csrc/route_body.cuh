@@ -1,8 +1,6 @@
 // Route + correct (kernels K4 + K2) for one (sequence, kv head), as a
-// device function: run by route_kernel2 (route.cu, one CTA of 8 warps per
-// (sequence, kv head), after the wide or generic split-K pass) and by the
-// last CTA of each (sequence, kv head) of the narrow split-K pass
-// (decode_narrow.cu, 4 warps).
+// device function of NW warps; route_kernel2 (route.cu) runs it with one CTA
+// of 8 warps per (sequence, kv head) after every split-K pass.
 //
 //  1. merge the split-K partials into O_base, M and L;
 //  2. score every stored residual slot: K slots with combined_kvscore
@@ -11,9 +9,10 @@
 //     (attention.py:718-725); V slots with block attention mass x error
 //     norm (attention.py:787-790), one thread per slot;
 //  3. normalise per query (attention.py:830-844) and select the joint or
-//     separate top-k (attention.py:856-875): a block-wide bisection on the
-//     scores' bit patterns finds the k-th score, ties go to the lower grid
-//     index, and one warp sorts the picks;
+//     separate top-k (attention.py:856-875): a threshold from every warp's
+//     r-th best score leaves a few dozen candidates that one warp sorts
+//     (bitonic, ties to the lower grid index); when more survive, every warp
+//     keeps a running top-32 and warp 0 merges the lists;
 //  4. apply the exact softmax renormalisation (attention.py:96-118, in the
 //     sparse form dO = (O + sum_S A(e^ds-1)V + sum_V A e^ds R_V) /
 //     (1 + sum_S A(e^ds-1)) - O) or the linear form, one selected page or slot
@@ -101,8 +100,9 @@ struct RouteSmem {
   int sel[8][kRSel];
   float selv[8][kRSel];
   int nsel[8];
-  float gv[kRWarps * 32];   // per-warp top-32 lists of the selection
+  float gv[kRWarps * 32];   // per-warp top-32 lists / prefilter thresholds and candidates
   int gi[kRWarps * 32];
+  int gcount;
   float ds[kRSel][kPage];         // wK (unscaled q.R_K) per selected K page and token
   int kp_page[kRSel], kp_mask[kRSel];
   int vsel[kRSel];
@@ -524,9 +524,117 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   // of the block on the warp's shuffles, then a bitonic merge with the
   // running list); warp 0 merges the warps' lists the same way.  Excluded
   // entries hold a negative score and sort last.
+  // Sort up to 64 (score, index) pairs held two per lane, best first
+  // (bitonic network on the warp's shuffles); position = lane + 32 j.
+  auto warp_sort64 = [&](float (&v)[2], int (&ix)[2]) {
+#pragma unroll
+    for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        if (stride == 32) {
+          if (rbetter(v[1], ix[1], v[0], ix[0])) {
+            const float tv = v[0]; v[0] = v[1]; v[1] = tv;
+            const int ti = ix[0]; ix[0] = ix[1]; ix[1] = ti;
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const float ov = __shfl_xor_sync(0xffffffffu, v[j], stride);
+            const int oi = __shfl_xor_sync(0xffffffffu, ix[j], stride);
+            const bool primary = (((lane + 32 * j) & size) == 0);
+            const bool want_better = ((lane & stride) == 0) == primary;
+            if (want_better ? rbetter(ov, oi, v[j], ix[j]) : rbetter(v[j], ix[j], ov, oi)) {
+              v[j] = ov;
+              ix[j] = oi;
+            }
+          }
+        }
+      }
+    }
+  };
+  // Publish the first n of a sorted list (one element per lane) into sel[i].
+  auto publish = [&](int i, float mv, int mi, int k) {
+    const int base = sm.nsel[i];
+    const int room = kRSel - base;
+    int n = __popc(__ballot_sync(0xffffffffu, mv >= 0.f));
+    n = min(n, k);
+    if (n > room) {
+      if (lane == 0) atomicOr(a.cache.error_flag, 8);
+      n = room;
+    }
+    if (lane < n) {
+      sm.sel[i][base + lane] = mi;
+      sm.selv[i][base + lane] = mv;
+    }
+    if (__any_sync(0xffffffffu, lane < n && mi < KG) && lane == 0) sm.any_k = 1;
+    __syncwarp();
+    if (lane == 0) sm.nsel[i] = base + n;
+  };
   auto pick = [&](int i, int lo, int hi, int k) {
     if (k <= 0 || hi <= lo) return;
     const float* row = sc + i * NG;
+    // ── prefilter: tau = min over warps of each warp's r-th best score, r =
+    // ceil(k / NW); at least NW*r >= k entries score >= tau, so the top-k
+    // are among them.  With <= 64 such entries one warp sorts them; else
+    // (ties, or warps with fewer than r candidates) the full path runs.
+    {
+      const int r = (k + NW - 1) / NW;
+      float lv = INFINITY;
+      int li = -1;
+      for (int rr = 0; rr < r; ++rr) {
+        float bv = -2.f;
+        int bi = 0x7fffffff;
+        for (int e = lo + warp * 32 + lane; e < hi; e += NW * 32) {
+          float x = row[e];
+          x = x == x ? x : -1.f;
+          if (rbetter(lv, li, x, e) && rbetter(x, e, bv, bi)) { bv = x; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (rbetter(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+        }
+        lv = bv;
+        li = bi;
+      }
+      if (lane == 0) sm.gv[warp] = lv;
+      if (tid == 0) sm.gcount = 0;
+      __syncthreads();
+      float tau = sm.gv[0];
+      for (int w = 1; w < NW; ++w) tau = fminf(tau, sm.gv[w]);
+      if (tau >= 0.f) {
+        for (int e = lo + tid; e < hi; e += NT) {
+          const float x = row[e];
+          if (x >= tau) {
+            const int slot = atomicAdd(&sm.gcount, 1);
+            if (slot < 64) {
+              sm.gv[32 + slot] = x;
+              sm.gi[32 + slot] = e;
+            }
+          }
+        }
+        __syncthreads();
+        const int nc = sm.gcount;
+        if (nc <= 64) {
+          if (warp == 0) {
+            float v[2];
+            int ix[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const int c = lane + 32 * j;
+              v[j] = c < nc ? sm.gv[32 + c] : -2.f;
+              ix[j] = c < nc ? sm.gi[32 + c] : 0x7fffffff;
+            }
+            warp_sort64(v, ix);
+            publish(i, v[0], ix[0], k);
+          }
+          __syncthreads();
+          return;
+        }
+      }
+      __syncthreads();
+    }
     float rv = -2.f;
     int ri = 0x7fffffff;
     for (int b0 = lo + warp * 64; b0 < hi; b0 += NW * 64) {
@@ -539,31 +647,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         v[j] = x == x ? x : -1.f;
         ix[j] = e < hi ? e : 0x7fffffff;
       }
-      // bitonic sort of the 64 entries, descending; position = lane + 32 j
-#pragma unroll
-      for (int size = 2; size <= 64; size <<= 1) {
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-          if (stride == 32) {
-            if (rbetter(v[1], ix[1], v[0], ix[0])) {
-              const float tv = v[0]; v[0] = v[1]; v[1] = tv;
-              const int ti = ix[0]; ix[0] = ix[1]; ix[1] = ti;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const float ov = __shfl_xor_sync(0xffffffffu, v[j], stride);
-              const int oi = __shfl_xor_sync(0xffffffffu, ix[j], stride);
-              const bool primary = (((lane + 32 * j) & size) == 0);
-              const bool want_better = ((lane & stride) == 0) == primary;
-              if (want_better ? rbetter(ov, oi, v[j], ix[j]) : rbetter(v[j], ix[j], ov, oi)) {
-                v[j] = ov;
-                ix[j] = oi;
-              }
-            }
-          }
-        }
-      }
+      warp_sort64(v, ix);
       warp_merge32(rv, ri, v[0], ix[0], lane);
     }
     sm.gv[warp * 32 + lane] = rv;
@@ -573,21 +657,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       float mv = sm.gv[lane];
       int mi = sm.gi[lane];
       for (int w = 1; w < NW; ++w) warp_merge32(mv, mi, sm.gv[w * 32 + lane], sm.gi[w * 32 + lane], lane);
-      const int base = sm.nsel[i];
-      const int room = kRSel - base;
-      int n = __popc(__ballot_sync(0xffffffffu, mv >= 0.f));
-      n = min(n, k);
-      if (n > room) {
-        if (lane == 0) atomicOr(a.cache.error_flag, 8);
-        n = room;
-      }
-      if (lane < n) {
-        sm.sel[i][base + lane] = mi;
-        sm.selv[i][base + lane] = mv;
-      }
-      if (__any_sync(0xffffffffu, lane < n && mi < KG) && lane == 0) sm.any_k = 1;
-      __syncwarp();
-      if (lane == 0) sm.nsel[i] = base + n;
+      publish(i, mv, mi, k);
     }
     __syncthreads();
   };
