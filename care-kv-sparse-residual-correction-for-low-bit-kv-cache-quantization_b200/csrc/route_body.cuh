@@ -138,40 +138,38 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
     const int i = idx / D, c = idx % D;
     sm.Q[i][c] = load_act(a.q, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + c, a.dt);
   }
-  if (tid < QN) {
-    const int64_t base = static_cast<int64_t>(bh) * a.n_splits * QN + tid;
-    float M = -INFINITY;
-    for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, a.pm[base + sp * QN]);
-    float L = 0.f;
-    if (M != -INFINITY)
-      for (int sp = 0; sp < a.n_splits; ++sp) {
-        const float m = a.pm[base + sp * QN];
-        if (m != -INFINITY) L += a.pl[base + sp * QN] * exp2f((m - M) * kRL2e);
-      }
-    sm.M[tid] = M;
-    sm.L[tid] = L;
-    sm.invL[tid] = L > 0.f ? 1.0f / L : 0.f;
-  }
+  // every (query, channel) thread loads all splits' m, l and its O entry at
+  // once (one round trip) and merges them; channel 0 publishes M, L
   if (tid == 0) { sm.cnt_k = 0; sm.cnt_v = 0; sm.ntot = 0; sm.any_k = 0; }
-  __syncthreads();
   for (int idx = tid; idx < QN * D; idx += NT) {
     const int i = idx / D, c = idx % D;
-    float O = 0.f;
-    if (sm.L[i] > 0.f) {
-      const int64_t base = static_cast<int64_t>(bh) * a.n_splits * QN + i;
+    const int64_t base = static_cast<int64_t>(bh) * a.n_splits * QN + i;
+    float M = -INFINITY;
+    for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, a.pm[base + sp * QN]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
       for (int sp = 0; sp < a.n_splits; ++sp) {
         const float m = a.pm[base + sp * QN];
-        if (m != -INFINITY) O += a.po[(base + sp * QN) * D + c] * exp2f((m - sm.M[i]) * kRL2e);
+        if (m == -INFINITY) continue;
+        const float f = exp2f((m - M) * kRL2e);
+        L += a.pl[base + sp * QN] * f;
+        O += a.po[(base + sp * QN) * D + c] * f;
       }
-      O = __fdiv_rn(O, sm.L[i]);
+      O = __fdiv_rn(O, L);
     }
     sm.O[i][c] = O;
+    if (c == 0) {
+      sm.M[i] = M;
+      sm.L[i] = L;
+      sm.invL[i] = L > 0.f ? 1.0f / L : 0.f;
+    }
   }
   __syncthreads();
 
   // A fragments for the slot dots: rows gid = q_hi, gid+8 = q_lo of query gid;
   // k-step ks of group g covers channels g*32 + 8*tig + 4*ks + {0..3}
-  for (int x = tid; x < d.C * 2 * 32; x += NT) {
+  const int nqfrag = a.kw != nullptr ? 0 : d.C * 2 * 32;   // unused when q.R_K is precomputed
+  for (int x = tid; x < nqfrag; x += NT) {
     const int g = x / 64, ks = (x / 32) % 2, ln = x % 32;
     const int qg = ln >> 2, tg = ln & 3;
     float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -242,7 +240,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           if (pos_tok(4 * q4 + u, a.s_perm) < nv) {
-            const float dS = __fdiv_rn(wa[u], a.sqrt_d);
+            const float dS = wa[u] * a.sf;   // q.R_K / sqrt(D) to within one ulp of the division
             const float A = exp2f((sa[u] - sm.M[i]) * kRL2e) * sm.invL[i];
             const float term = dS * (A * (1.f - A));
             ss = fmaf(term, term, ss);
