@@ -1,5 +1,6 @@
-// Route + correct kernel (K4 + K2) after the wide or generic split-K pass:
-// one CTA of 8 warps per (sequence, kv head) runs route_body (route_body.cuh).
+// Route + correct kernel (K4 + K2) after every split-K pass: one CTA of
+// kRouteWarps warps per (sequence, kv head) runs route_body (route_body.cuh);
+// small CTAs with per-QN scratch keep 8 of them resident per SM.
 #include "common.cuh"
 #include "internal.h"
 #include "decode_args.h"
@@ -7,19 +8,21 @@
 
 namespace carekv {
 
+constexpr int kRouteWarps = 4;
+
 template <int QN>
-__global__ void __launch_bounds__(256, 4) route_kernel2(DecodeArgs a, int scores_in_smem) {
-  __shared__ RouteSmem sm;
+__global__ void __launch_bounds__(kRouteWarps * 32, 8) route_kernel2(DecodeArgs a, int scores_in_smem) {
+  __shared__ RouteSmem<QN, kRouteWarps> sm;
   extern __shared__ float dyn[];
-  route_body<QN, kRWarps>(a, blockIdx.x, sm, dyn, scores_in_smem);
+  route_body<QN, kRouteWarps>(a, blockIdx.x, sm, dyn, scores_in_smem);
 }
 
 template <int QN>
 cudaError_t launch_route(DecodeArgs& a, cudaStream_t st, int n_bh) {
   const int NG = a.p_used * (a.cfg.k_slots_per_page + a.cfg.v_slots_per_page);
   const size_t sc_bytes = static_cast<size_t>(QN) * NG * sizeof(float);
-  const int in_smem = sc_bytes + sizeof(RouteSmem) <= 46 * 1024 ? 1 : 0;
-  route_kernel2<QN><<<n_bh, kRWarps * 32, in_smem ? sc_bytes : 0, st>>>(a, in_smem);
+  const int in_smem = sc_bytes + sizeof(RouteSmem<QN, kRouteWarps>) <= 46 * 1024 ? 1 : 0;
+  route_kernel2<QN><<<n_bh, kRouteWarps * 32, in_smem ? sc_bytes : 0, st>>>(a, in_smem);
   return cudaGetLastError();
 }
 

@@ -32,7 +32,6 @@ namespace carekv {
 constexpr int kRSel = 32;     // selected slots per query (host-validated)
 constexpr float kREps = 1e-6f;
 constexpr float kRL2e = 1.4426950408889634f;
-constexpr int kRWarps = 8;   // scratch arrays are sized for 8 warps
 
 __device__ __forceinline__ bool rbetter(float s1, int i1, float s2, int i2) {
   return s1 > s2 || (s1 == s2 && i1 < i2);
@@ -91,27 +90,31 @@ __device__ __forceinline__ void acc_nib_word(uint32_t u, float c, float (&acc)[8
   }
 }
 
+// Scratch of one routing CTA: QN queries, NW warps.
+template <int QN, int NW>
 struct RouteSmem {
-  float Q[8][128];
-  float O[8][128];
-  float M[8], invL[8], L[8];
-  float red[kRWarps][8], red2[kRWarps][8];
-  float nk[8], nv[8];
-  int sel[8][kRSel];
-  float selv[8][kRSel];
-  int nsel[8];
-  float gv[kRWarps * 32];   // per-warp top-32 lists / prefilter thresholds and candidates
-  int gi[kRWarps * 32];
+  float Q[QN][128];
+  float O[QN][128];
+  float M[QN], invL[QN], L[QN];
+  float red[NW][QN], red2[NW][QN];
+  float nk[QN], nv[QN];
+  int sel[QN][kRSel];
+  float selv[QN][kRSel];
+  int nsel[QN];
+  // per-warp top-32 lists of the selection; the prefilter uses the first NW
+  // entries for thresholds and entries 32..95 for candidates
+  float gv[NW * 32 > 96 ? NW * 32 : 96];
+  int gi[NW * 32 > 96 ? NW * 32 : 96];
   int gcount;
   float ds[kRSel][kPage];         // wK (unscaled q.R_K) per selected K page and token
   int kp_page[kRSel], kp_mask[kRSel];
   int vsel[kRSel];
-  float acc[kRWarps][128];
-  float z[kRWarps];
-  __align__(16) uint32_t stage[kRWarps][16 * 64 / 4 + 8];  // one page of packed V rows (<= 64 B each) or a V slot payload
+  float acc[NW][128];
+  float z[NW];
+  __align__(16) uint32_t stage[NW][16 * 64 / 4 + 8];  // one page of packed V rows (<= 64 B each) or a V slot payload
   __align__(16) uint32_t qfrag[4][2][32][4];  // A fragments of q_hi / q_lo per channel group and k-step
-  float stage_sc[kRWarps][16 * 4];           // the page's V scales (fp16 values)
-  float coef[kRWarps][kPage];
+  float stage_sc[NW][16 * 4];           // the page's V scales (fp16 values)
+  float coef[NW][kPage];
   int cnt_k, cnt_v, ntot, any_k, nkp, nvs;
   float mshift;
 };
@@ -120,7 +123,7 @@ struct RouteSmem {
 // calling CTA.  `sm` is the CTA's scratch; the scores live in `dyn` when
 // scores_in_smem, else in the workspace.  Every thread of the CTA calls it.
 template <int QN, int NW>
-__device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSmem& sm, float* dyn,
+__device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSmem<QN, NW>& sm, float* dyn,
                                            int scores_in_smem) {
   constexpr int NT = NW * 32;
   const Dims d = make_dims(a.cfg);
