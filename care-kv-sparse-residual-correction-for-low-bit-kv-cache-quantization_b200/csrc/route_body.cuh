@@ -33,6 +33,14 @@ constexpr int kRSel = 32;     // selected slots per query (host-validated)
 constexpr float kREps = 1e-6f;
 constexpr float kRL2e = 1.4426950408889634f;
 
+// 2^x with the SFU approximation (relative error ~2^-22; results below
+// 2^-126 flush to zero): attention weights A = 2^((s - M) log2 e) / L.
+__device__ __forceinline__ float rex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ bool rbetter(float s1, int i1, float s2, int i2) {
   return s1 > s2 || (s1 == s2 && i1 < i2);
 }
@@ -107,7 +115,7 @@ struct RouteSmem {
   int gi[NW * 32 > 96 ? NW * 32 : 96];
   int gcount;
   float ds[kRSel][kPage];         // wK (unscaled q.R_K) per selected K page and token
-  int kp_page[kRSel], kp_mask[kRSel];
+  int kp_page[kRSel], kp_mask[kRSel], kp_nv[kRSel];
   int vsel[kRSel];
   float acc[NW][128];
   float z[NW];
@@ -154,7 +162,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       for (int sp = 0; sp < a.n_splits; ++sp) {
         const float m = a.pm[base + sp * QN];
         if (m == -INFINITY) continue;
-        const float f = exp2f((m - M) * kRL2e);
+        const float f = rex2((m - M) * kRL2e);
         L += a.pl[base + sp * QN] * f;
         O += a.po[(base + sp * QN) * D + c] * f;
       }
@@ -212,50 +220,87 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
 
   // ── 2a. K scores ──
   if (a.kw != nullptr) {
-    // combined_kvscore from q . R_K precomputed by the split-K pass: one
-    // thread per (query, stored slot); ||dS * A(1-A)|| over the page's valid
-    // tokens * ||V_page||_F * sens
-    int cnt = 0;
-    for (int idx = tid; idx < QN * KG; idx += NT) {
-      const int i = idx / KG, e = idx - i * KG;
-      const int p = e / d.SK, j = e - p * d.SK;
+    // Thread per page: combined_kvscore of its stored K slots from q . R_K
+    // precomputed by the split-K pass (||dS * A(1-A)|| over the page's valid
+    // tokens * ||V_page||_F * sens), its V slots' block mass * error * sens,
+    // and the slot / token counts -- all loads of a page in one round trip.
+    int cntk = 0, cntv = 0, ntok = 0;
+    for (int p = tid; p < a.p_used; p += NT) {
+      const bool live = p < np;
       const int64_t pg = lhp * d.P + p;
-      int grp = -1, nv = 0;
-      if (p < np) {
-        grp = a.cache.k_slot_group[pg * d.SK + j];
-        nv = a.cache.valid[pg];
-      }
-      const bool ok = grp >= 0 && nv > 0;
-      if (i == 0) cnt += ok;
-      if (!ok || !may_k) {
-        sc[i * NG + e] = -1.f;
-        continue;
-      }
-      const float4* wv = reinterpret_cast<const float4*>(a.kw + ((static_cast<int64_t>(bh) * QN + i) * KG + e) * kPage);
-      const float4* sv = reinterpret_cast<const float4*>(Sb + i * sst + p * kPage);
-      const float vc = sqrtf(a.cache.v_norm2[pg]);
-      float ss = 0.f;
+      // every load of the page is issued before any result is used (the
+      // workspace rows exist for every page, so no load waits on a check)
+      const int nv = live ? a.cache.valid[pg] : 0;
+      const float vc = live ? sqrtf(a.cache.v_norm2[pg]) : 0.f;
+      ntok += nv;
+      for (int i = 0; i < QN; ++i) {
+        const float4* srow = reinterpret_cast<const float4*>(Sb + i * sst + p * kPage);
+        float sv[16];
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        const float4 w4 = wv[q4], s4 = sv[q4];
-        const float wa[4] = {w4.x, w4.y, w4.z, w4.w};
-        const float sa[4] = {s4.x, s4.y, s4.z, s4.w};
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const float4 x = srow[q4];
+          sv[4 * q4] = x.x; sv[4 * q4 + 1] = x.y; sv[4 * q4 + 2] = x.z; sv[4 * q4 + 3] = x.w;
+        }
+        // attention weight of position j (token pos_tok(j)); 0 past the valid rows
+        float A[16];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (pos_tok(4 * q4 + u, a.s_perm) < nv) {
-            const float dS = wa[u] * a.sf;   // q.R_K / sqrt(D) to within one ulp of the division
-            const float A = exp2f((sa[u] - sm.M[i]) * kRL2e) * sm.invL[i];
-            const float term = dS * (A * (1.f - A));
-            ss = fmaf(term, term, ss);
+        for (int j = 0; j < 16; ++j)
+          A[j] = pos_tok(j, a.s_perm) < nv ? rex2((sv[j] - sm.M[i]) * kRL2e) * sm.invL[i] : 0.f;
+        for (int j = 0; j < d.SK; ++j) {
+          const int e = p * d.SK + j;
+          const int grp = live ? a.cache.k_slot_group[pg * d.SK + j] : -1;
+          const float4* wrow = reinterpret_cast<const float4*>(a.kw + ((static_cast<int64_t>(bh) * QN + i) * KG + e) * kPage);
+          float ss = 0.f;
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const float4 w4 = wrow[q4];
+            const float wa[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float Au = A[4 * q4 + u];
+              const float term = (wa[u] * a.sf) * (Au * (1.f - Au));   // dS = q.R_K / sqrt(D) (one ulp of the division)
+              ss = fmaf(term, term, ss);
+            }
           }
+          const bool ok = grp >= 0 && nv > 0;
+          if (i == 0) cntk += ok;
+          float v = -1.f;
+          if (ok && may_k) {
+            float ks = sqrtf(ss) * vc;
+            if (!(ks == ks) || isinf(ks)) ks = 0.f;
+            v = fmaxf(ks, 0.f) * rp.sensitivity;
+          }
+          sc[i * NG + e] = v;
+        }
+        for (int j = 0; j < d.SV; ++j) {
+          const int e = p * d.SV + j;
+          const int vb = live ? a.cache.v_slot_block[pg * d.SV + j] : -1;
+          const int t0 = vb * d.vtb, t1 = min(t0 + d.vtb, nv);
+          const bool ok = vb >= 0 && t1 > t0;
+          if (i == 0) cntv += ok;
+          float v = -1.f;
+          if (ok && may_v) {
+            const float err = f16_bits_to_f32(a.cache.v_err[pg * d.NV + vb]);
+            float mass = 0.f;
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) {
+              const int t = pos_tok(jj, a.s_perm);
+              if (t >= t0 && t < t1) mass += A[jj];
+            }
+            v = __fmul_rn(__fmul_rn(mass, err), rp.sensitivity);
+          }
+          sc[i * NG + KG + e] = v;
         }
       }
-      float ks = sqrtf(ss) * vc;
-      if (!(ks == ks) || isinf(ks)) ks = 0.f;
-      sc[i * NG + e] = fmaxf(ks, 0.f) * rp.sensitivity;
     }
-    cnt = __reduce_add_sync(0xffffffffu, cnt);
-    if (lane == 0 && cnt) atomicAdd(&sm.cnt_k, cnt);
+    cntk = __reduce_add_sync(0xffffffffu, cntk);
+    cntv = __reduce_add_sync(0xffffffffu, cntv);
+    ntok = __reduce_add_sync(0xffffffffu, ntok);
+    if (lane == 0) {
+      if (cntk) atomicAdd(&sm.cnt_k, cntk);
+      if (cntv) atomicAdd(&sm.cnt_v, cntv);
+      if (ntok) atomicAdd(&sm.ntot, ntok);
+    }
   } else if (rp.kscore_live || !may_k) {
     // combined_kvscore, one warp per stored slot: q . R_K^T on the tensor
     // cores (codes as exact fp16 integers, slot scale applied after), then
@@ -305,7 +350,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         for (int u = 0; u < 4; ++u) {
           if (toks[u] < nv) {
             const float dS = __fdiv_rn(__fmul_rn(dots[u], rs), a.sqrt_d);
-            const float A = exp2f((s4[u] - sm.M[gid]) * kRL2e) * sm.invL[gid];
+            const float A = rex2((s4[u] - sm.M[gid]) * kRL2e) * sm.invL[gid];
             const float term = dS * (A * (1.f - A));
             ss = fmaf(term, term, ss);
           }
@@ -368,7 +413,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           float term = 0.f;
           if (t < nv) {
             const float dS = __fdiv_rn(dot, a.sqrt_d);
-            const float A = exp2f((sv[i] - sm.M[i]) * kRL2e) * sm.invL[i];
+            const float A = rex2((sv[i] - sm.M[i]) * kRL2e) * sm.invL[i];
             term = dS * (A * (1.f - A));
           }
           float ss = term * term;
@@ -386,7 +431,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         for (int i = 0; i < QN; ++i) {
           float A = 0.f, inv = 0.f, vd = 0.f;
           if (t < nv) {
-            A = exp2f((sv[i] - sm.M[i]) * kRL2e) * sm.invL[i];
+            A = rex2((sv[i] - sm.M[i]) * kRL2e) * sm.invL[i];
             inv = __fdiv_rn(1.f, fmaxf(sm.M[i] - sv[i], kREps));
             float acc = 0.f;
             for (int c = 0; c < D; ++c) {
@@ -420,7 +465,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
     if (lane == 0 && cnt) atomicAdd(&sm.cnt_k, cnt);
   }
   // ── 2b. V scores: thread per grid entry; page token count ──
-  {
+  if (a.kw == nullptr) {
     int cnt = 0, ntok = 0;
     for (int e = tid; e < VG; e += NT) {
       const int p = e / d.SV, j = e % d.SV;
@@ -438,7 +483,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         for (int i = 0; i < QN; ++i) {
           float mass = 0.f;
           for (int t = t0; t < t1; ++t)
-            mass += exp2f((Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
+            mass += rex2((Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
           sc[i * NG + KG + e] = __fmul_rn(__fmul_rn(mass, err), rp.sensitivity);
         }
       } else {
@@ -719,6 +764,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         const int u = __popc(bl & lt);
         sm.kp_page[u] = p;
         sm.kp_mask[u] = msk;
+        sm.kp_nv[u] = a.cache.valid[lhp * d.P + p];
       }
       if (isv) sm.vsel[__popc(bv & lt)] = e - KG;
       if (lane == 0) {
@@ -761,7 +807,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       float mx = -INFINITY;
       int covered = 0;
       for (int u = 0; u < nkp; ++u) {
-        const int nv = a.cache.valid[lhp * d.P + sm.kp_page[u]];
+        const int nv = sm.kp_nv[u];
         covered += nv;
         if (lane < nv) mx = fmaxf(mx, __fdiv_rn(sm.ds[u][lane], a.sqrt_d));
       }
@@ -781,7 +827,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       if (item < nkp) {
         const int u = item, p = sm.kp_page[u];
         const int64_t pg = lhp * d.P + p;
-        const int nv = a.cache.valid[pg];
+        const int nv = sm.kp_nv[u];
         const float mv = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
         // stage the page's packed V rows and scales
         const uint4* src = reinterpret_cast<const uint4*>(a.cache.v_codes + pg * kPage * R);
@@ -791,7 +837,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           sm.stage_sc[warp][x] = read_scale(a.cache.v_scale, pg * kPage * G + x, d.scale_mode, mv);
         float cf = 0.f;
         if (lane < kPage && lane < nv) {
-          const float A = exp2f((Sb[i * sst + p * kPage + tok_pos(lane, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
+          const float A = rex2((Sb[i * sst + p * kPage + tok_pos(lane, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
           const float wk = sm.ds[u][lane];
           if (exact) {
             const float dsv = __fdiv_rn(wk, a.sqrt_d);
@@ -838,7 +884,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           const int t = t0 + lane;
           float cf = 0.f;
           if (t < t1) {
-            const float A = exp2f((Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
+            const float A = rex2((Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
             float w = 1.f;
             if (exact) {
               const float dsv = u >= 0 ? __fdiv_rn(sm.ds[u][t], a.sqrt_d) : 0.f;
