@@ -159,17 +159,19 @@ inline SplitPlan split_plan(int n_bh, int p_used, int slots) {
 
 static inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 
-// Split-K pass chosen for a layout.  NARROW: INT3 / int8 scales with at most
+// Split-K pass chosen for a layout.  NARROW: INT3 or INT4 / int8 scales with at most
 // 4 query heads per kv head (decode_narrow.cu, 4 CTAs per SM, also computes
 // q . R_K of the stored K slots); WIDE: the same layout with 8 query heads
 // (decode_fast.cu, 2 CTAs per SM); GENERIC: every other layout.
 enum class Pass { GENERIC, WIDE, NARROW };
 inline Pass choose_pass(const carekv_config_t& c) {
   const int D = c.head_dim;
-  const bool int3 = c.base_bits == 3 && c.scale_mode == CAREKV_SCALE_INT8 && (D == 64 || D == 128) &&
-                    c.group_size % (D / 4) == 0 && c.group_size % (D / 8) == 0 && c.page_size == kPage;
-  if (!int3) return Pass::GENERIC;
-  return c.num_heads / c.num_kv_heads <= 4 ? Pass::NARROW : Pass::WIDE;
+  const bool tiled = c.scale_mode == CAREKV_SCALE_INT8 && (D == 64 || D == 128) &&
+                     c.group_size % (D / 4) == 0 && c.group_size % (D / 8) == 0 && c.page_size == kPage;
+  const int qn = c.num_heads / c.num_kv_heads;
+  if (tiled && qn <= 4 && (c.base_bits == 3 || c.base_bits == 4)) return Pass::NARROW;
+  if (tiled && c.base_bits == 3) return Pass::WIDE;
+  return Pass::GENERIC;
 }
 inline int pass_slots(Pass p) { return p == Pass::NARROW ? 4 * 148 : 2 * 148; }
 

@@ -1,4 +1,4 @@
-// Narrow-group split-K decode pass over packed INT3 pages (kernel K3n,
+// Narrow-group split-K decode pass over packed INT3 / INT4 pages (kernel K3n,
 // sm_100a): kv heads whose query group has at most 4 heads (MHA, GQA-2,
 // GQA-4).
 //
@@ -49,9 +49,9 @@ constexpr float kLog2e = 1.4426950408889634f;
 struct Geo {
   int R, G, SK, kbytes, vOff, ksOff, vsOff, slOff, stage, meta, qs, total;
 };
-__host__ __device__ inline Geo geo(int D, int G, int SK, bool kslot) {
+__host__ __device__ inline Geo geo(int D, int G, int SK, bool kslot, int bits) {
   Geo g;
-  g.R = D * 3 / 8;
+  g.R = D * bits / 8;
   g.G = G;
   g.SK = SK;
   g.kbytes = kCP * kPage * g.R;
@@ -135,9 +135,44 @@ __device__ __forceinline__ void nib_quads(uint32_t u, const Keys& K, uint32_t (&
   o[3] = h2sub((v & 0x00F000F0u) ^ K.n4, K.n4);
 }
 
-template <int QN, int D>
+// exact half2 (code_lo, code_hi) * sig2 of two 4-bit fields at mantissa bit S (0 or 4)
+template <int S>
+__device__ __forceinline__ uint32_t i4p(uint32_t t, uint32_t key, uint32_t sig2) {
+  uint32_t x;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(x) : "r"(t), "n"((15u << S) | (15u << (16 + S))), "r"(key));
+  return h2mul(h2sub(x, key), sig2);
+}
+// One packed INT4 K word (nibbles n0..n7, even channel low) -> half2 operands
+// (n0,n4) (n1,n5) (n2,n6) (n3,n7).
+__device__ __forceinline__ void k_quads4(uint32_t u, uint32_t sig2, const Keys& K, uint32_t (&o)[4]) {
+  const uint32_t v = u >> 8;
+  o[0] = i4p<0>(u, K.n0, sig2);
+  o[1] = i4p<4>(u, K.n4, sig2);
+  o[2] = i4p<0>(v, K.n0, sig2);
+  o[3] = i4p<4>(v, K.n4, sig2);
+}
+// The same INT4 word of rows a (low halves) and b (high halves): byte k of
+// both rows in r[k], its nibbles (channels 2k, 2k+1) at bits 0 and 4.
+struct VSrc4 {
+  uint32_t r[4];
+};
+__device__ __forceinline__ VSrc4 v_src4(uint32_t Wa, uint32_t Wb) {
+  VSrc4 v;
+  v.r[0] = prmt(Wa, Wb, 0x4400);
+  v.r[1] = prmt(Wa, Wb, 0x5511);
+  v.r[2] = prmt(Wa, Wb, 0x6622);
+  v.r[3] = prmt(Wa, Wb, 0x7733);
+  return v;
+}
+template <int F>
+__device__ __forceinline__ uint32_t v_field4(const VSrc4& v, const Keys& K, uint32_t sig2) {
+  return i4p<4 * (F & 1)>(v.r[F >> 1], (F & 1) ? K.n4 : K.n0, sig2);
+}
+
+template <int QN, int D, int BITS>
 __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
-  constexpr int R = D * 3 / 8;
+  static_assert(BITS == 3 || BITS == 4, "narrow pass: INT3 or INT4 rows");
+  constexpr int R = D * BITS / 8;
   constexpr int KS = D / 16;   // k-steps of Q.K^T = m-tiles of O^T
   constexpr int KW = D / 32;   // packed K words per thread and row
   constexpr int G4 = D / 32;   // 32-channel groups (K residual slots)
@@ -163,7 +198,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   const int Hq = d.H * QN;
   const int G = d.G, SK = d.SK;
   const bool kslot = a.kw != nullptr;
-  const Geo g = geo(D, G, SK, kslot);
+  const Geo g = geo(D, G, SK, kslot, BITS);
   const int64_t page0 = lhp * d.P;
   const int KG = a.p_used * SK;
 
@@ -223,10 +258,17 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
 #pragma unroll
   for (int i = 0; i < KW; ++i) {
     const int c = tig * (D / 4) + 8 * i;
-    qb[2 * i][0] = pack_h2(qp(c + 0), qp(c + 3));
-    qb[2 * i][1] = pack_h2(qp(c + 1), qp(c + 4));
-    qb[2 * i + 1][0] = pack_h2(qp(c + 2), qp(c + 5));
-    qb[2 * i + 1][1] = pack_h2(qp(c + 6), qp(c + 7));
+    if constexpr (BITS == 3) {   // k_quads: (f0,f3) (f1,f4) | (f2,f5) (f6,f7)
+      qb[2 * i][0] = pack_h2(qp(c + 0), qp(c + 3));
+      qb[2 * i][1] = pack_h2(qp(c + 1), qp(c + 4));
+      qb[2 * i + 1][0] = pack_h2(qp(c + 2), qp(c + 5));
+      qb[2 * i + 1][1] = pack_h2(qp(c + 6), qp(c + 7));
+    } else {                     // k_quads4: (n0,n4) (n1,n5) | (n2,n6) (n3,n7)
+      qb[2 * i][0] = pack_h2(qp(c + 0), qp(c + 4));
+      qb[2 * i][1] = pack_h2(qp(c + 1), qp(c + 5));
+      qb[2 * i + 1][0] = pack_h2(qp(c + 2), qp(c + 6));
+      qb[2 * i + 1][1] = pack_h2(qp(c + 3), qp(c + 7));
+    }
   }
   // slot operands per 32-channel group: thread tig owns the group's channels
   // 8*tig .. +8 (one nibble word per token); k-step 0 takes (n0,n4) (n1,n5),
@@ -259,7 +301,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   float* Wrow = kslot ? a.kw + (static_cast<int64_t>(bh) * QN + tig) * KG * kPage + 2 * gid : nullptr;
 
   // V side: thread gid owns packed words (D=128) 2gid, 2gid+1 / (D=64) gid
-  constexpr int VB = D == 128 ? 6 : 3;
+  constexpr int VB = (D == 128 ? 2 : 1) * BITS;   // bytes of the thread's V words: one 8-channel word = BITS bytes
   const int vo = VB * gid;
   const int vbase = vo & ~3, voff = vo & 3;
   const uint32_t vsel_l = 0x3210 + 0x1111 * voff;
@@ -268,7 +310,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   const int gv = ((D == 128 ? 16 : 8) * gid) / d.gsize;  // V scale group
   const int ra = 2 * tig;                                 // V rows ra, ra+1, ra+8, ra+9
   const int src_a = 8 * tig + qi, src_b = src_a + 4;
-  const int ko0 = gid * R + (D == 128 ? 12 : 6) * tig, ko8 = ko0 + 8 * R;
+  const int ko0 = gid * R + (D / 4) * BITS / 8 * tig, ko8 = ko0 + 8 * R;   // thread's K channel block
   const int kso0 = gid * G + gk, kso8 = (gid + 8) * G + gk;
   const int vso0 = ra * G + gv, vso1 = (ra + 1) * G + gv, vso2 = (ra + 8) * G + gv, vso3 = (ra + 9) * G + gv;
 
@@ -279,7 +321,13 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
     const uint32_t sig = i8_scale_pair(static_cast<uint32_t>(ks[kso0]) | (static_cast<uint32_t>(ks[kso8]) << 16), km2);
     const uint32_t sig0 = prmt(sig, sig, 0x1010), sig8 = prmt(sig, sig, 0x3232);
     uint32_t w0[KW], w8[KW];
-    if constexpr (D == 128) {
+    if constexpr (BITS == 4) {
+#pragma unroll
+      for (int i = 0; i < KW; ++i) {
+        w0[i] = lds32(kc + ko0 + 4 * i);
+        w8[i] = lds32(kc + ko8 + 4 * i);
+      }
+    } else if constexpr (D == 128) {
       const uint32_t x0 = lds32(kc + ko0), x1 = lds32(kc + ko0 + 4), x2 = lds32(kc + ko0 + 8);
       const uint32_t y0 = lds32(kc + ko8), y1 = lds32(kc + ko8 + 4), y2 = lds32(kc + ko8 + 8);
       w0[0] = x0; w0[1] = prmt(x0, x1, 0x6543); w0[2] = prmt(x1, x2, 0x5432); w0[3] = x2 >> 8;
@@ -295,8 +343,13 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
 #pragma unroll
     for (int i = 0; i < KW; ++i) {
       uint32_t p0[4], p8[4];
-      k_quads(w0[i], sig0, KY, p0);
-      k_quads(w8[i], sig8, KY, p8);
+      if constexpr (BITS == 4) {
+        k_quads4(w0[i], sig0, KY, p0);
+        k_quads4(w8[i], sig8, KY, p8);
+      } else {
+        k_quads(w0[i], sig0, KY, p0);
+        k_quads(w8[i], sig8, KY, p8);
+      }
       mma_f16(acc[i & 1], p0[0], p8[0], p0[1], p8[1], qb[2 * i][0], qb[2 * i][1]);
       mma_f16(acc[i & 1], p0[2], p8[2], p0[3], p8[3], qb[2 * i + 1][0], qb[2 * i + 1][1]);
     }
@@ -332,7 +385,33 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
     const uint8_t* vs = st + g.vsOff + pp * kPage * G;
     const uint32_t sA = i8_scale_pair(static_cast<uint32_t>(vs[vso0]) | (static_cast<uint32_t>(vs[vso1]) << 16), vm2);
     const uint32_t sB = i8_scale_pair(static_cast<uint32_t>(vs[vso2]) | (static_cast<uint32_t>(vs[vso3]) << 16), vm2);
-    if constexpr (D == 128) {
+    if constexpr (BITS == 4) {
+      if constexpr (D == 128) {
+        uint32_t wl[4], wh[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const uint2 w2 = *reinterpret_cast<const uint2*>(vc + (ra + (r & 1) + 8 * (r >> 1)) * R + vo);
+          wl[r] = w2.x;
+          wh[r] = w2.y;
+        }
+        const VSrc4 x0 = v_src4(wl[0], wl[1]), x1 = v_src4(wh[0], wh[1]);
+        const VSrc4 x2 = v_src4(wl[2], wl[3]), x3 = v_src4(wh[2], wh[3]);
+#define CK_VF(F) \
+  mma_f16(o[F], v_field4<F>(x0, KY, sA), v_field4<F>(x1, KY, sA), v_field4<F>(x2, KY, sB), v_field4<F>(x3, KY, sB), pb0, pb1);
+        CK_VF(0) CK_VF(1) CK_VF(2) CK_VF(3) CK_VF(4) CK_VF(5) CK_VF(6) CK_VF(7)
+#undef CK_VF
+      } else {
+        uint32_t wv[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) wv[r] = lds32(vc + (ra + (r & 1) + 8 * (r >> 1)) * R + vo);
+        const VSrc4 x0 = v_src4(wv[0], wv[1]), x1 = v_src4(wv[2], wv[3]);
+#define CK_VF(F)                                                                                                   \
+  mma_f16(o[F], v_field4<F>(x0, KY, sA), v_field4<F + 4>(x0, KY, sA), v_field4<F>(x1, KY, sB), v_field4<F + 4>(x1, KY, sB), \
+          pb0, pb1);
+        CK_VF(0) CK_VF(1) CK_VF(2) CK_VF(3)
+#undef CK_VF
+      }
+    } else if constexpr (D == 128) {
       uint32_t wl[4], wh[4];
 #pragma unroll
       for (int r = 0; r < 4; ++r) {
@@ -522,22 +601,27 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
 
 size_t narrow_smem_bytes(const carekv_config_t& c, bool kslot) {
   const int G = c.head_dim / c.group_size;
-  return static_cast<size_t>(narrow::geo(c.head_dim, G, c.k_slots_per_page, kslot).total);
+  return static_cast<size_t>(narrow::geo(c.head_dim, G, c.k_slots_per_page, kslot, c.base_bits).total);
 }
 
-template <int QN, int D>
-cudaError_t launch_decode_narrow(DecodeArgs& a, cudaStream_t st, int n_bh) {
+template <int QN, int D, int BITS>
+static cudaError_t launch_narrow_bits(DecodeArgs& a, cudaStream_t st, int n_bh) {
   const int smem = static_cast<int>(narrow_smem_bytes(a.cfg, a.kw != nullptr));
   static int attr_bytes = 0;  // per process; the attribute is per function, not per device
   if (smem > attr_bytes) {
-    cudaError_t e = cudaFuncSetAttribute(narrow::decode_narrow<QN, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         smem);
+    cudaError_t e = cudaFuncSetAttribute(narrow::decode_narrow<QN, D, BITS>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr_bytes = smem;
   }
   a.s_perm = 1;
-  narrow::decode_narrow<QN, D><<<n_bh * a.n_splits, narrow::kWarps * 32, smem, st>>>(a);
+  narrow::decode_narrow<QN, D, BITS><<<n_bh * a.n_splits, narrow::kWarps * 32, smem, st>>>(a);
   return cudaGetLastError();
+}
+
+template <int QN, int D>
+cudaError_t launch_decode_narrow(DecodeArgs& a, cudaStream_t st, int n_bh) {
+  return a.cfg.base_bits == 4 ? launch_narrow_bits<QN, D, 4>(a, st, n_bh) : launch_narrow_bits<QN, D, 3>(a, st, n_bh);
 }
 
 #define CK_INST(QN, D) template cudaError_t launch_decode_narrow<QN, D>(DecodeArgs&, cudaStream_t, int);

@@ -71,6 +71,8 @@ CASES = [
     ("kind_v_exact", 64, 3, 32, 4, 1, "fp16", 40, 8, (2, 4), "absolute", (2, 4), "joint", True, "exact", "v"),
     ("kind_k_linear", 128, 3, 32, 8, 1, "fp32", 48, 8, (2, 4), "absolute", (3, 0), "joint", True, "linear", "k"),
     ("ratio_gqa8_d64", 64, 3, 32, 32, 4, "fp32", 512, 4, (1, 1), "ratio", 0.03, "joint", True, "exact", "both"),
+    ("int4_d64_mha_fp16", 64, 4, 32, 3, 3, "fp16", 70, 12, (1, 1), "absolute", (2, 2), "joint", True, "exact", "both"),
+    ("int4_d128_g64_mha_bf16", 128, 4, 64, 2, 2, "bf16", 96, 10, (1, 1), "ratio", 0.05, "joint", True, "exact", "both"),
 ]
 
 
