@@ -181,6 +181,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   __shared__ __align__(8) uint64_t bars[kWarps][kNS];
   __shared__ float sm_m[kWarps][4], sm_l[kWarps][4];
   __shared__ __align__(16) float q_sm[QN][D];
+  __shared__ uint2 qbs[KS][32];   // Q^T operands per k-step and lane
 
   const Dims d = make_dims(a.cfg);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -253,21 +254,17 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
     return part ? x - hi : hi;
   };
   // K side: thread tig owns channels tig*D/4 .. +D/4 (KW packed words); word
-  // i feeds k-steps 2i ((f0,f3) (f1,f4)) and 2i+1 ((f2,f5) (f6,f7)).
-  uint32_t qb[KS][2];
-#pragma unroll
-  for (int i = 0; i < KW; ++i) {
+  // i feeds k-steps 2i and 2i+1 (channel pairs as the k_quads / k_quads4
+  // operands pair them).  Built once per CTA: warp w fills the k-steps of the
+  // words i with i % kWarps == w; every warp then loads all of them.
+  for (int i = warp; i < KW; i += kWarps) {
     const int c = tig * (D / 4) + 8 * i;
     if constexpr (BITS == 3) {   // k_quads: (f0,f3) (f1,f4) | (f2,f5) (f6,f7)
-      qb[2 * i][0] = pack_h2(qp(c + 0), qp(c + 3));
-      qb[2 * i][1] = pack_h2(qp(c + 1), qp(c + 4));
-      qb[2 * i + 1][0] = pack_h2(qp(c + 2), qp(c + 5));
-      qb[2 * i + 1][1] = pack_h2(qp(c + 6), qp(c + 7));
+      qbs[2 * i][lane] = make_uint2(pack_h2(qp(c + 0), qp(c + 3)), pack_h2(qp(c + 1), qp(c + 4)));
+      qbs[2 * i + 1][lane] = make_uint2(pack_h2(qp(c + 2), qp(c + 5)), pack_h2(qp(c + 6), qp(c + 7)));
     } else {                     // k_quads4: (n0,n4) (n1,n5) | (n2,n6) (n3,n7)
-      qb[2 * i][0] = pack_h2(qp(c + 0), qp(c + 4));
-      qb[2 * i][1] = pack_h2(qp(c + 1), qp(c + 5));
-      qb[2 * i + 1][0] = pack_h2(qp(c + 2), qp(c + 6));
-      qb[2 * i + 1][1] = pack_h2(qp(c + 3), qp(c + 7));
+      qbs[2 * i][lane] = make_uint2(pack_h2(qp(c + 0), qp(c + 4)), pack_h2(qp(c + 1), qp(c + 5)));
+      qbs[2 * i + 1][lane] = make_uint2(pack_h2(qp(c + 2), qp(c + 6)), pack_h2(qp(c + 3), qp(c + 7)));
     }
   }
   // slot operands per 32-channel group: thread tig owns the group's channels
@@ -288,7 +285,14 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
       }
       qs[x] = make_uint2(pack_h2(v[0], v[1]), pack_h2(v[2], v[3]));
     }
-    __syncthreads();
+  }
+  __syncthreads();
+  uint32_t qb[KS][2];
+#pragma unroll
+  for (int kb = 0; kb < KS; ++kb) {
+    const uint2 v = qbs[kb][lane];
+    qb[kb][0] = v.x;
+    qb[kb][1] = v.y;
   }
 
   const Keys KY = {a.dq_keys[0], a.dq_keys[1], a.dq_keys[2], a.dq_keys[3], a.dq_keys[4]};
