@@ -10,7 +10,7 @@
 //     norm (attention.py:787-790), one thread per slot;
 //  3. normalise per query (attention.py:830-844) and select the joint or
 //     separate top-k (attention.py:856-875): a threshold from every warp's
-//     r-th best score leaves a few dozen candidates that one warp sorts
+//     r-th best lane maximum leaves a few dozen candidates that one warp sorts
 //     (bitonic, ties to the lower grid index); when more survive, every warp
 //     keeps a running top-32 and warp 0 merges the lists;
 //  4. apply the exact softmax renormalisation (attention.py:96-118, in the
@@ -30,6 +30,7 @@
 namespace carekv {
 
 constexpr int kRSel = 32;     // selected slots per query (host-validated)
+constexpr int kRStg = 12 * 1024;   // apply staging bytes per CTA
 constexpr float kREps = 1e-6f;
 constexpr float kRL2e = 1.4426950408889634f;
 
@@ -63,6 +64,37 @@ __device__ __forceinline__ void warp_merge32(float& rv, int& ri, float bv, int b
     if (want_better ? rbetter(xv, xi, rv, ri) : rbetter(rv, ri, xv, xi)) {
       rv = xv;
       ri = xi;
+    }
+  }
+}
+
+// One compare-exchange of a bitonic network on (score, index) pairs held one
+// per lane; pos = the pair's position in the sequence.
+__device__ __forceinline__ void rcx(float& v, int& ix, int pos, int size, int stride) {
+  const float ov = __shfl_xor_sync(0xffffffffu, v, stride);
+  const int oi = __shfl_xor_sync(0xffffffffu, ix, stride);
+  const bool want_better = ((pos & stride) == 0) == ((pos & size) == 0);
+  if (want_better ? rbetter(ov, oi, v, ix) : rbetter(v, ix, ov, oi)) {
+    v = ov;
+    ix = oi;
+  }
+}
+// Sort up to 64 (score, index) pairs held two per lane (position lane and
+// lane + 32), best first: bitonic network on the warp's shuffles.
+__device__ __forceinline__ void rsort64(float& v0, int& i0, float& v1, int& i1, int lane) {
+#pragma unroll
+  for (int size = 2; size <= 64; size <<= 1) {
+#pragma unroll
+    for (int stride = size >> 1; stride > 0; stride >>= 1) {
+      if (stride == 32) {
+        if (rbetter(v1, i1, v0, i0)) {
+          const float tv = v0; v0 = v1; v1 = tv;
+          const int ti = i0; i0 = i1; i1 = ti;
+        }
+      } else {
+        rcx(v0, i0, lane, size, stride);
+        rcx(v1, i1, lane + 32, size, stride);
+      }
     }
   }
 }
@@ -116,11 +148,17 @@ struct RouteSmem {
   int gcount;
   float ds[kRSel][kPage];         // wK (unscaled q.R_K) per selected K page and token
   int kp_page[kRSel], kp_mask[kRSel], kp_nv[kRSel];
-  int vsel[kRSel];
+  float kp_vm[kRSel];
+  int vsel[kRSel], vs_t0[kRSel], vs_t1[kRSel];
+  float vs_rs[kRSel];
+  int ioff[2 * kRSel], bnd[2 * kRSel + 1], nb;
+  uint64_t stg_bar;
   float acc[NW][128];
   float z[NW];
-  __align__(16) uint32_t stage[NW][16 * 64 / 4 + 8];  // one page of packed V rows (<= 64 B each) or a V slot payload
-  __align__(16) uint32_t qfrag[4][2][32][4];  // A fragments of q_hi / q_lo per channel group and k-step
+  union {
+    __align__(16) uint32_t qfrag[4][2][32][4];  // A fragments of q_hi / q_lo per channel group and k-step (scoring)
+    __align__(16) uint8_t stg[kRStg];           // staged items (apply)
+  };
   float stage_sc[NW][16 * 4];           // the page's V scales (fp16 values)
   float coef[NW][kPage];
   int cnt_k, cnt_v, ntot, any_k, nkp, nvs;
@@ -232,6 +270,10 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       // workspace rows exist for every page, so no load waits on a check)
       const int nv = live ? a.cache.valid[pg] : 0;
       const float vc = live ? sqrtf(a.cache.v_norm2[pg]) : 0.f;
+      // the page's 4 V block errors in one load (NV == 4), so the error of a
+      // kept block does not wait for the block index
+      uint2 ve4 = make_uint2(0u, 0u);
+      if (live && d.NV == 4) ve4 = *reinterpret_cast<const uint2*>(a.cache.v_err + pg * 4);
       ntok += nv;
       for (int i = 0; i < QN; ++i) {
         const float4* srow = reinterpret_cast<const float4*>(Sb + i * sst + p * kPage);
@@ -280,7 +322,8 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           if (i == 0) cntv += ok;
           float v = -1.f;
           if (ok && may_v) {
-            const float err = f16_bits_to_f32(a.cache.v_err[pg * d.NV + vb]);
+            const float err = f16_bits_to_f32(d.NV == 4 ? static_cast<uint16_t>(((vb & 2) ? ve4.y : ve4.x) >> (16 * (vb & 1)))
+                                                        : a.cache.v_err[pg * d.NV + vb]);
             float mass = 0.f;
 #pragma unroll
             for (int jj = 0; jj < 16; ++jj) {
@@ -570,34 +613,6 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   // of the block on the warp's shuffles, then a bitonic merge with the
   // running list); warp 0 merges the warps' lists the same way.  Excluded
   // entries hold a negative score and sort last.
-  // Sort up to 64 (score, index) pairs held two per lane, best first
-  // (bitonic network on the warp's shuffles); position = lane + 32 j.
-  auto warp_sort64 = [&](float (&v)[2], int (&ix)[2]) {
-#pragma unroll
-    for (int size = 2; size <= 64; size <<= 1) {
-#pragma unroll
-      for (int stride = size >> 1; stride > 0; stride >>= 1) {
-        if (stride == 32) {
-          if (rbetter(v[1], ix[1], v[0], ix[0])) {
-            const float tv = v[0]; v[0] = v[1]; v[1] = tv;
-            const int ti = ix[0]; ix[0] = ix[1]; ix[1] = ti;
-          }
-        } else {
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const float ov = __shfl_xor_sync(0xffffffffu, v[j], stride);
-            const int oi = __shfl_xor_sync(0xffffffffu, ix[j], stride);
-            const bool primary = (((lane + 32 * j) & size) == 0);
-            const bool want_better = ((lane & stride) == 0) == primary;
-            if (want_better ? rbetter(ov, oi, v[j], ix[j]) : rbetter(v[j], ix[j], ov, oi)) {
-              v[j] = ov;
-              ix[j] = oi;
-            }
-          }
-        }
-      }
-    }
-  };
   // Publish the first n of a sorted list (one element per lane) into sel[i].
   auto publish = [&](int i, float mv, int mi, int k) {
     const int base = sm.nsel[i];
@@ -619,31 +634,30 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   auto pick = [&](int i, int lo, int hi, int k) {
     if (k <= 0 || hi <= lo) return;
     const float* row = sc + i * NG;
-    // ── prefilter: tau = min over warps of each warp's r-th best score, r =
-    // ceil(k / NW); at least NW*r >= k entries score >= tau, so the top-k
-    // are among them.  With <= 64 such entries one warp sorts them; else
-    // (ties, or warps with fewer than r candidates) the full path runs.
+    // ── prefilter: tau = min over warps of each warp's r-th best lane
+    // maximum, r = ceil(k / NW); the r best lanes of every warp hold
+    // distinct entries >= tau, so at least NW*r >= k entries score >= tau
+    // and the top-k are among them.  With <= 64 such entries one warp sorts
+    // them; else (ties, or warps with fewer than r live lanes) the full path
+    // runs.
     {
-      const int r = (k + NW - 1) / NW;
-      float lv = INFINITY;
-      int li = -1;
-      for (int rr = 0; rr < r; ++rr) {
-        float bv = -2.f;
-        int bi = 0x7fffffff;
-        for (int e = lo + warp * 32 + lane; e < hi; e += NW * 32) {
-          float x = row[e];
-          x = x == x ? x : -1.f;
-          if (rbetter(lv, li, x, e) && rbetter(x, e, bv, bi)) { bv = x; bi = e; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-          if (rbetter(ov, oi, bv, bi)) { bv = ov; bi = oi; }
-        }
-        lv = bv;
-        li = bi;
+      const int r = (k + NW - 1) / NW;   // <= kRSel / NW <= 32
+      // r-th best lane maximum of the warp: each lane's best entry, then a
+      // descending bitonic sort of the 32 lane maxima (values only)
+      float lv = -2.f;
+      for (int e = lo + tid; e < hi; e += NT) {
+        const float x = row[e];
+        lv = fmaxf(lv, x == x ? x : -1.f);
       }
+#pragma unroll
+      for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+          const float o = __shfl_xor_sync(0xffffffffu, lv, stride);
+          lv = (((lane & stride) == 0) == ((lane & size) == 0)) ? fmaxf(lv, o) : fminf(lv, o);
+        }
+      }
+      lv = __shfl_sync(0xffffffffu, lv, r - 1);
       if (lane == 0) sm.gv[warp] = lv;
       if (tid == 0) sm.gcount = 0;
       __syncthreads();
@@ -664,16 +678,12 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         const int nc = sm.gcount;
         if (nc <= 64) {
           if (warp == 0) {
-            float v[2];
-            int ix[2];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const int c = lane + 32 * j;
-              v[j] = c < nc ? sm.gv[32 + c] : -2.f;
-              ix[j] = c < nc ? sm.gi[32 + c] : 0x7fffffff;
-            }
-            warp_sort64(v, ix);
-            publish(i, v[0], ix[0], k);
+            float v0 = lane < nc ? sm.gv[32 + lane] : -2.f;
+            int i0 = lane < nc ? sm.gi[32 + lane] : 0x7fffffff;
+            float v1 = lane + 32 < nc ? sm.gv[64 + lane] : -2.f;
+            int i1 = lane + 32 < nc ? sm.gi[64 + lane] : 0x7fffffff;
+            rsort64(v0, i0, v1, i1, lane);
+            publish(i, v0, i0, k);
           }
           __syncthreads();
           return;
@@ -684,17 +694,13 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
     float rv = -2.f;
     int ri = 0x7fffffff;
     for (int b0 = lo + warp * 64; b0 < hi; b0 += NW * 64) {
-      float v[2];
-      int ix[2];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int e = b0 + lane + 32 * j;
-        const float x = e < hi ? row[e] : -2.f;
-        v[j] = x == x ? x : -1.f;
-        ix[j] = e < hi ? e : 0x7fffffff;
-      }
-      warp_sort64(v, ix);
-      warp_merge32(rv, ri, v[0], ix[0], lane);
+      const int e0 = b0 + lane, e1 = b0 + lane + 32;
+      float v0 = e0 < hi ? row[e0] : -2.f, v1 = e1 < hi ? row[e1] : -2.f;
+      v0 = v0 == v0 ? v0 : -1.f;
+      v1 = v1 == v1 ? v1 : -1.f;
+      int i0 = e0 < hi ? e0 : 0x7fffffff, i1 = e1 < hi ? e1 : 0x7fffffff;
+      rsort64(v0, i0, v1, i1, lane);
+      warp_merge32(rv, ri, v0, i0, lane);
     }
     sm.gv[warp * 32 + lane] = rv;
     sm.gi[warp * 32 + lane] = ri;
@@ -740,8 +746,27 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   const int WPR = D / 8;      // packed words (8 channels) per row
   const int RG = 32 / WPR;    // rows one warp walks side by side
   const int wl = lane % WPR, rg = lane / WPR;
+  // Staging of the selected items (a K page: its packed V rows, V scales and
+  // logits; a V slot: its payload and its page's logits) in batches that fit
+  // sm.stg.  Every segment is a multiple of 16 bytes; with 16-byte aligned
+  // sources the lanes of warp 0 stage a batch with bulk copies (one round
+  // trip), else every warp copies its own items.
+  const int es = d.scale_mode == CAREKV_SCALE_INT8 ? 1 : (d.scale_mode == CAREKV_SCALE_F32 ? 4 : 2);
+  const int k_codes_b = kPage * R, k_sc_b = kPage * G * es;
+  const int k_item_b = k_codes_b + k_sc_b + kPage * 4;
+  const int v_item_b = d.vslot_bytes + kPage * 4;
+  const bool bulk = ((reinterpret_cast<uintptr_t>(a.cache.v_codes) | reinterpret_cast<uintptr_t>(a.cache.v_scale) |
+                      reinterpret_cast<uintptr_t>(a.cache.v_slot_data) | reinterpret_cast<uintptr_t>(a.S)) & 15) == 0 &&
+                    k_codes_b % 16 == 0 && k_sc_b % 16 == 0 && d.vslot_bytes % 16 == 0;
+  if (tid == 0) {
+    mbar_init(&sm.stg_bar, 1);
+    fence_mbar_init();
+  }
+  int n_batches = 0;    // batches staged so far (mbarrier phase)
+  bool stg_failed = false;
   for (int i = 0; i < QN; ++i) {
-    // selected K pages (the first selection of a page leads it) and V slots
+    // selected K pages (the first selection of a page leads it) and V slots,
+    // with the per-item scalars (one round trip)
     if (warp == 0) {
       const int nsel = sm.nsel[i];
       const int e = lane < nsel ? sm.sel[i][lane] : -1;
@@ -760,22 +785,80 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       const unsigned bl = __ballot_sync(0xffffffffu, leader);
       const unsigned bv = __ballot_sync(0xffffffffu, isv);
       const unsigned bk = __ballot_sync(0xffffffffu, isk);
+      const int nkp_w = __popc(bl);
       if (leader) {
         const int u = __popc(bl & lt);
+        const int64_t pg = lhp * d.P + p;
         sm.kp_page[u] = p;
         sm.kp_mask[u] = msk;
-        sm.kp_nv[u] = a.cache.valid[lhp * d.P + p];
+        sm.kp_nv[u] = a.cache.valid[pg];
+        sm.kp_vm[u] = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
       }
-      if (isv) sm.vsel[__popc(bv & lt)] = e - KG;
+      if (isv) {
+        const int v = __popc(bv & lt), ev = e - KG;
+        const int pv = ev / d.SV, j = ev % d.SV;
+        const int64_t pg = lhp * d.P + pv;
+        sm.vsel[v] = ev;
+        const int vb = a.cache.v_slot_block[pg * d.SV + j];
+        const int t0 = vb * d.vtb;
+        sm.vs_t0[v] = t0;
+        sm.vs_t1[v] = min(t0 + d.vtb, a.cache.valid[pg]);
+        sm.vs_rs[v] = f16_bits_to_f32(a.cache.v_slot_scale[pg * d.SV + j]);
+      }
       if (lane == 0) {
-        sm.nkp = __popc(bl);
+        sm.nkp = nkp_w;
         sm.nvs = __popc(bv);
         reads_k += __popc(bk);
         reads_v += __popc(bv);
       }
     }
     __syncthreads();
-    const int nkp = sm.nkp, nvs = sm.nvs;
+    const int nkp = sm.nkp, nvs = sm.nvs, nit = nkp + nvs;
+    // batch plan: item -> staging offset, batch boundaries
+    if (tid == 0) {
+      int off = 0, nb = 0;
+      sm.bnd[0] = 0;
+      for (int it = 0; it < nit; ++it) {
+        const int sz = it < nkp ? k_item_b : v_item_b;
+        if (off + sz > kRStg) {
+          sm.bnd[++nb] = it;
+          off = 0;
+        }
+        sm.ioff[it] = off;
+        off += sz;
+      }
+      sm.bnd[++nb] = nit;
+      sm.nb = nb;
+    }
+    __syncthreads();
+    const int nb = sm.nb;
+    // bulk copies of batch `bt` by the lanes of warp 0 (item per lane)
+    auto stage_batch = [&](int bt) {
+      if (!bulk || warp != 0) return;
+      const int lo = sm.bnd[bt], hi = sm.bnd[bt + 1];
+      uint32_t bytes = 0;
+      for (int it = lo; it < hi; ++it) bytes += it < nkp ? k_item_b : v_item_b;
+      if (lane == 0) mbar_expect_tx(&sm.stg_bar, bytes);
+      __syncwarp();
+      for (int it = lo + lane; it < hi; it += 32) {
+        uint8_t* dst = sm.stg + sm.ioff[it];
+        fence_proxy_async();
+        if (it < nkp) {
+          const int p = sm.kp_page[it];
+          const int64_t pg = lhp * d.P + p;
+          bulk_g2s(dst, a.cache.v_codes + pg * k_codes_b, k_codes_b, &sm.stg_bar);
+          bulk_g2s(dst + k_codes_b, reinterpret_cast<const uint8_t*>(a.cache.v_scale) + pg * k_sc_b, k_sc_b, &sm.stg_bar);
+          bulk_g2s(dst + k_codes_b + k_sc_b, Sb + i * sst + p * kPage, kPage * 4, &sm.stg_bar);
+        } else {
+          const int ev = sm.vsel[it - nkp];
+          const int pv = ev / d.SV, j = ev % d.SV;
+          const int64_t pg = lhp * d.P + pv;
+          bulk_g2s(dst, a.cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes, d.vslot_bytes, &sm.stg_bar);
+          bulk_g2s(dst + d.vslot_bytes, Sb + i * sst + pv * kPage, kPage * 4, &sm.stg_bar);
+        }
+      }
+    };
+    stage_batch(0);
     // wK per (selected K page, token): q . R_K summed over the page's selected groups
     for (int x = tid; x < nkp * kPage; x += NT) {
       const int u = x / kPage, t = x % kPage;
@@ -822,84 +905,117 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
     float num[4] = {0.f, 0.f, 0.f, 0.f};   // channel lane + 32 jj (per-channel decode)
     float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // channels 8 wl + j (word decode)
     float zp = 0.f;
-    for (int item = warp; item < nkp + nvs; item += NW) {
-      uint8_t* stg = reinterpret_cast<uint8_t*>(sm.stage[warp]);
-      if (item < nkp) {
-        const int u = item, p = sm.kp_page[u];
-        const int64_t pg = lhp * d.P + p;
-        const int nv = sm.kp_nv[u];
-        const float mv = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
-        // stage the page's packed V rows and scales
-        const uint4* src = reinterpret_cast<const uint4*>(a.cache.v_codes + pg * kPage * R);
-        uint4* dst = reinterpret_cast<uint4*>(sm.stage[warp]);
-        for (int w = lane; w < kPage * R / 16; w += 32) dst[w] = src[w];
-        for (int x = lane; x < kPage * G; x += 32)
-          sm.stage_sc[warp][x] = read_scale(a.cache.v_scale, pg * kPage * G + x, d.scale_mode, mv);
-        float cf = 0.f;
-        if (lane < kPage && lane < nv) {
-          const float A = rex2((Sb[i * sst + p * kPage + tok_pos(lane, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
-          const float wk = sm.ds[u][lane];
-          if (exact) {
-            const float dsv = __fdiv_rn(wk, a.sqrt_d);
-            cf = A * (dsv <= 80.f ? cbase * expm1f(dsv) : expf(dsv - mshift) - cbase);
+    for (int bt = 0; bt < nb; ++bt) {
+      if (bt > 0) {
+        __syncthreads();   // every warp is done with the previous batch
+        stage_batch(bt);
+      }
+      if (bulk) {
+        // bounded wait; the outcome is made CTA-uniform
+        stg_failed = __syncthreads_or(!mbar_wait(&sm.stg_bar, n_batches & 1)) != 0;
+        if (stg_failed) break;
+        ++n_batches;
+      }
+      for (int item = sm.bnd[bt] + warp; item < sm.bnd[bt + 1]; item += NW) {
+        uint8_t* stg = sm.stg + sm.ioff[item];
+        if (item < nkp) {
+          const int u = item, p = sm.kp_page[u];
+          const int64_t pg = lhp * d.P + p;
+          const int nv = sm.kp_nv[u];
+          if (!bulk) {
+            for (int w = lane; w < k_codes_b / 4; w += 32)
+              reinterpret_cast<uint32_t*>(stg)[w] = reinterpret_cast<const uint32_t*>(a.cache.v_codes + pg * k_codes_b)[w];
+            for (int w = lane; w < k_sc_b; w += 32)
+              stg[k_codes_b + w] = reinterpret_cast<const uint8_t*>(a.cache.v_scale)[pg * k_sc_b + w];
+            if (lane < kPage)
+              reinterpret_cast<float*>(stg + k_codes_b + k_sc_b)[lane] = Sb[i * sst + p * kPage + lane];
+            __syncwarp();
+          }
+          const float* srow = reinterpret_cast<const float*>(stg + k_codes_b + k_sc_b);
+          for (int x = lane; x < kPage * G; x += 32)
+            sm.stage_sc[warp][x] = read_scale(stg + k_codes_b, x, d.scale_mode, sm.kp_vm[u]);
+          float cf = 0.f;
+          if (lane < kPage && lane < nv) {
+            const float A = rex2((srow[tok_pos(lane, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
+            const float wk = sm.ds[u][lane];
+            if (exact) {
+              const float dsv = __fdiv_rn(wk, a.sqrt_d);
+              cf = A * (dsv <= 80.f ? cbase * expm1f(dsv) : expf(dsv - mshift) - cbase);
+            } else {
+              cf = A * wk * rp.k_corr_scale;
+            }
+          }
+          if (lane < kPage) sm.coef[warp][lane] = cf;
+          zp += warp_sum(cf);
+          __syncwarp();
+          if (fast3) {
+            for (int t = rg; t < nv; t += RG) {
+              const float sg = sm.stage_sc[warp][t * G + (8 * wl) / d.gsize];
+              acc_int3_word(stg + t * R, wl, pack_h2(sg, sg), sm.coef[warp][t], acc8);
+            }
           } else {
-            cf = A * wk * rp.k_corr_scale;
-          }
-        }
-        if (lane < kPage) sm.coef[warp][lane] = cf;
-        zp += warp_sum(cf);
-        __syncwarp();
-        if (fast3) {
-          for (int t = rg; t < nv; t += RG) {
-            const float sg = sm.stage_sc[warp][t * G + (8 * wl) / d.gsize];
-            acc_int3_word(stg + t * R, wl, pack_h2(sg, sg), sm.coef[warp][t], acc8);
-          }
-        } else {
-          for (int t = 0; t < nv; ++t) {
-            const float c = sm.coef[warp][t];
+            for (int t = 0; t < nv; ++t) {
+              const float c = sm.coef[warp][t];
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              const int ch = lane + 32 * jj;
-              if (ch < D) {
-                const float vh = f16r(__fmul_rn(static_cast<float>(unpack_code(stg + t * R, ch, d.bits)),
-                                                sm.stage_sc[warp][t * G + ch / d.gsize]));
-                num[jj] = fmaf(c, vh, num[jj]);
+              for (int jj = 0; jj < 4; ++jj) {
+                const int ch = lane + 32 * jj;
+                if (ch < D) {
+                  const float vh = f16r(__fmul_rn(static_cast<float>(unpack_code(stg + t * R, ch, d.bits)),
+                                                  sm.stage_sc[warp][t * G + ch / d.gsize]));
+                  num[jj] = fmaf(c, vh, num[jj]);
+                }
               }
             }
           }
-        }
-      } else {
-        const int ev = sm.vsel[item - nkp];
-        const int p = ev / d.SV, j = ev % d.SV;
-        const int64_t pg = lhp * d.P + p;
-        const int vb = a.cache.v_slot_block[pg * d.SV + j];
-        const int nv = a.cache.valid[pg];
-        const int t0 = vb * d.vtb, t1 = min(t0 + d.vtb, nv);
-        const uint32_t* src = reinterpret_cast<const uint32_t*>(a.cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes);
-        for (int w = lane; w < d.vslot_bytes / 4; w += 32) sm.stage[warp][w] = src[w];
-        const float rs = f16_bits_to_f32(a.cache.v_slot_scale[pg * d.SV + j]);
-        int u = -1;
-        for (int x = 0; x < nkp; ++x) if (sm.kp_page[x] == p) u = x;
-        if (lane < d.vtb) {
-          const int t = t0 + lane;
-          float cf = 0.f;
-          if (t < t1) {
-            const float A = rex2((Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
-            float w = 1.f;
-            if (exact) {
-              const float dsv = u >= 0 ? __fdiv_rn(sm.ds[u][t], a.sqrt_d) : 0.f;
-              w = dsv <= 80.f ? cbase * expf(dsv) : expf(dsv - mshift);
-            }
-            cf = A * w;
+        } else {
+          const int v = item - nkp;
+          const int ev = sm.vsel[v];
+          const int p = ev / d.SV, j = ev % d.SV;
+          const int t0 = sm.vs_t0[v], t1 = sm.vs_t1[v];
+          if (!bulk) {
+            const int64_t pg = lhp * d.P + p;
+            const uint32_t* src = reinterpret_cast<const uint32_t*>(a.cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes);
+            for (int w = lane; w < d.vslot_bytes / 4; w += 32) reinterpret_cast<uint32_t*>(stg)[w] = src[w];
+            if (lane < kPage)
+              reinterpret_cast<float*>(stg + d.vslot_bytes)[lane] = Sb[i * sst + p * kPage + lane];
+            __syncwarp();
           }
-          sm.coef[warp][lane] = cf;
+          const float* srow = reinterpret_cast<const float*>(stg + d.vslot_bytes);
+          const float rs = sm.vs_rs[v];
+          int u = -1;
+          for (int x = 0; x < nkp; ++x) if (sm.kp_page[x] == p) u = x;
+          if (lane < d.vtb) {
+            const int t = t0 + lane;
+            float cf = 0.f;
+            if (t < t1) {
+              const float A = rex2((srow[tok_pos(t, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
+              float w = 1.f;
+              if (exact) {
+                const float dsv = u >= 0 ? __fdiv_rn(sm.ds[u][t], a.sqrt_d) : 0.f;
+                w = dsv <= 80.f ? cbase * expf(dsv) : expf(dsv - mshift);
+              }
+              cf = A * w;
+            }
+            sm.coef[warp][lane] = cf;
+          }
+          __syncwarp();
+          // row r of the payload: D/2 bytes, channel c at nibble c of the row
+          const uint32_t* pay = reinterpret_cast<const uint32_t*>(stg);
+          for (int r = rg; r < t1 - t0; r += RG) acc_nib_word(pay[r * WPR + wl], sm.coef[warp][r] * rs, acc8);
         }
         __syncwarp();
-        // row r of the payload: D/2 bytes, channel c at nibble c of the row
-        for (int r = rg; r < t1 - t0; r += RG)
-          acc_nib_word(sm.stage[warp][r * WPR + wl], sm.coef[warp][r] * rs, acc8);
       }
-      __syncwarp();
+    }
+    if (stg_failed) {
+      // the staging copies did not land in time: flag it, let the copies in
+      // flight land (bounded) before the CTA exits, keep the base output
+      if (tid == 0) {
+        atomicOr(a.cache.error_flag, 4);
+        (void)mbar_wait(&sm.stg_bar, n_batches & 1);
+      }
+      __syncthreads();
+      write_base();
+      return;
     }
     // fold the word layout's row groups onto lanes 0 .. WPR-1
     for (int o = WPR; o < 32; o <<= 1)
