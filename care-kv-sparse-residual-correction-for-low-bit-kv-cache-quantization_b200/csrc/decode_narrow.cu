@@ -222,6 +222,9 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   // bulk copies of chunk c (pages pa + 2c, pa + 2c + 1); sources are
   // recomputed from the arguments on every issue (one lane, once per chunk)
   const int n_chunks = (pb - pa + kCP - 1) / kCP;
+  // the packed pages are read once (evict first); S and q . R_K are read
+  // back by the router right after this pass (evict last)
+  const uint64_t pol_stream = l2_evict_first(), pol_keep = l2_evict_last();
   auto issue = [&](int c) {
     const int p = pa + c * kCP;
     const int n = min(kCP, pb - p);
@@ -232,11 +235,11 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
     const uint32_t cbytes = n * kPage * R, sbytes = n * kPage * G;
     const uint32_t slbytes = kslot ? n * SK * 256 : 0;
     mbar_expect_tx(br, 2 * cbytes + 2 * sbytes + slbytes);
-    bulk_g2s(st, a.cache.k_codes + pg * (kPage * R), cbytes, br);
-    bulk_g2s(st + g.vOff, a.cache.v_codes + pg * (kPage * R), cbytes, br);
-    bulk_g2s(st + g.ksOff, reinterpret_cast<const int8_t*>(a.cache.k_scale) + pg * kPage * G, sbytes, br);
-    bulk_g2s(st + g.vsOff, reinterpret_cast<const int8_t*>(a.cache.v_scale) + pg * kPage * G, sbytes, br);
-    if (slbytes) bulk_g2s(st + g.slOff, a.cache.k_slot_data + pg * SK * 256, slbytes, br);
+    bulk_g2s_pol(st, a.cache.k_codes + pg * (kPage * R), cbytes, br, pol_stream);
+    bulk_g2s_pol(st + g.vOff, a.cache.v_codes + pg * (kPage * R), cbytes, br, pol_stream);
+    bulk_g2s_pol(st + g.ksOff, reinterpret_cast<const int8_t*>(a.cache.k_scale) + pg * kPage * G, sbytes, br, pol_stream);
+    bulk_g2s_pol(st + g.vsOff, reinterpret_cast<const int8_t*>(a.cache.v_scale) + pg * kPage * G, sbytes, br, pol_stream);
+    if (slbytes) bulk_g2s_pol(st + g.slOff, a.cache.k_slot_data + pg * SK * 256, slbytes, br, pol_stream);
   };
   if (lane == 0)
     for (int c = 0; c < min(kNS, n_chunks); ++c) issue(c);
@@ -378,8 +381,8 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
       mma_f16(cw, n0[2], n8[2], n0[3], n8[3], b1.x, b1.y);
       const float rs = m_rs[mi * SK + j];
       if (q_ok)
-        *reinterpret_cast<float2*>(Wrow + (static_cast<int64_t>(p) * SK + j) * kPage) =
-            make_float2(__fmul_rn(cw[0] + cw[1], rs), __fmul_rn(cw[2] + cw[3], rs));
+        st_f2_pol(Wrow + (static_cast<int64_t>(p) * SK + j) * kPage, __fmul_rn(cw[0] + cw[1], rs),
+                  __fmul_rn(cw[2] + cw[3], rs), pol_keep);
     }
   };
 
@@ -505,8 +508,8 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
     k_side(st, 0, m_km[mi], s00, s01);
     if (two) k_side(st, 1, m_km[mi + 1], s10, s11);
     if (q_ok) {
-      *reinterpret_cast<float2*>(Srow + static_cast<int64_t>(pbase) * kPage) = make_float2(s00, s01);
-      if (two) *reinterpret_cast<float2*>(Srow + static_cast<int64_t>(pbase + 1) * kPage) = make_float2(s10, s11);
+      st_f2_pol(Srow + static_cast<int64_t>(pbase) * kPage, s00, s01, pol_keep);
+      if (two) st_f2_pol(Srow + static_cast<int64_t>(pbase + 1) * kPage, s10, s11, pol_keep);
     }
     if (kslot) {
       slot_side(st, 0, pbase, mi, nv0);

@@ -42,61 +42,65 @@ __device__ __forceinline__ float rex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ bool rbetter(float s1, int i1, float s2, int i2) {
-  return s1 > s2 || (s1 == s2 && i1 < i2);
+// Selection order (score descending, grid index ascending) as one unsigned
+// 64-bit key: the score's bits made order-preserving in the high word (-0
+// folded onto +0), the complemented index in the low word, so a larger key
+// ranks first and every compare-exchange is a branch-free min / max.
+__device__ __forceinline__ uint64_t rkey(float s, int i) {
+  uint32_t b = __float_as_uint(__fadd_rn(s, 0.0f));
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<uint64_t>(b) << 32) | static_cast<uint32_t>(~i);
 }
-
-// Merge two descending 32-lists held one element per lane (lane 0 best):
-// keep the better of run[l] and blk[31 - l] (a bitonic sequence holding the
-// top 32 of both) and sort it descending.
-__device__ __forceinline__ void warp_merge32(float& rv, int& ri, float bv, int bi, int lane) {
-  const float ov = __shfl_sync(0xffffffffu, bv, 31 - lane);
-  const int oi = __shfl_sync(0xffffffffu, bi, 31 - lane);
-  if (rbetter(ov, oi, rv, ri)) {
-    rv = ov;
-    ri = oi;
-  }
-#pragma unroll
-  for (int stride = 16; stride > 0; stride >>= 1) {
-    const float xv = __shfl_xor_sync(0xffffffffu, rv, stride);
-    const int xi = __shfl_xor_sync(0xffffffffu, ri, stride);
-    const bool want_better = (lane & stride) == 0;
-    if (want_better ? rbetter(xv, xi, rv, ri) : rbetter(rv, ri, xv, xi)) {
-      rv = xv;
-      ri = xi;
-    }
-  }
+__device__ __forceinline__ float rkey_score(uint64_t k) {
+  uint32_t b = static_cast<uint32_t>(k >> 32);
+  b = (b & 0x80000000u) ? (b & 0x7fffffffu) : ~b;
+  return __uint_as_float(b);
 }
-
-// One compare-exchange of a bitonic network on (score, index) pairs held one
-// per lane; pos = the pair's position in the sequence.
-__device__ __forceinline__ void rcx(float& v, int& ix, int pos, int size, int stride) {
-  const float ov = __shfl_xor_sync(0xffffffffu, v, stride);
-  const int oi = __shfl_xor_sync(0xffffffffu, ix, stride);
-  const bool want_better = ((pos & stride) == 0) == ((pos & size) == 0);
-  if (want_better ? rbetter(ov, oi, v, ix) : rbetter(v, ix, ov, oi)) {
-    v = ov;
-    ix = oi;
-  }
+__device__ __forceinline__ int rkey_index(uint64_t k) { return static_cast<int>(~static_cast<uint32_t>(k)); }
+__device__ __forceinline__ uint64_t rshfl_xor(uint64_t k, int m) {
+  const uint32_t lo = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(k), m);
+  const uint32_t hi = __shfl_xor_sync(0xffffffffu, static_cast<uint32_t>(k >> 32), m);
+  return (static_cast<uint64_t>(hi) << 32) | lo;
 }
-// Sort up to 64 (score, index) pairs held two per lane (position lane and
-// lane + 32), best first: bitonic network on the warp's shuffles.
-__device__ __forceinline__ void rsort64(float& v0, int& i0, float& v1, int& i1, int lane) {
+__device__ __forceinline__ uint64_t rshfl(uint64_t k, int src) {
+  const uint32_t lo = __shfl_sync(0xffffffffu, static_cast<uint32_t>(k), src);
+  const uint32_t hi = __shfl_sync(0xffffffffu, static_cast<uint32_t>(k >> 32), src);
+  return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+// One compare-exchange of a bitonic network on keys held one per lane;
+// pos = the key's position in the sequence.
+__device__ __forceinline__ uint64_t rcx(uint64_t k, int pos, int size, int stride) {
+  const uint64_t o = rshfl_xor(k, stride);
+  const bool keep_max = ((pos & stride) == 0) == ((pos & size) == 0);
+  return keep_max ? (o > k ? o : k) : (o < k ? o : k);
+}
+// Sort up to 64 keys held two per lane (positions lane and lane + 32),
+// best first: bitonic network on the warp's shuffles.
+__device__ __forceinline__ void rsort64(uint64_t& k0, uint64_t& k1, int lane) {
 #pragma unroll
   for (int size = 2; size <= 64; size <<= 1) {
 #pragma unroll
     for (int stride = size >> 1; stride > 0; stride >>= 1) {
       if (stride == 32) {
-        if (rbetter(v1, i1, v0, i0)) {
-          const float tv = v0; v0 = v1; v1 = tv;
-          const int ti = i0; i0 = i1; i1 = ti;
-        }
+        const uint64_t hi = k0 > k1 ? k0 : k1, lo = k0 > k1 ? k1 : k0;
+        k0 = hi;
+        k1 = lo;
       } else {
-        rcx(v0, i0, lane, size, stride);
-        rcx(v1, i1, lane + 32, size, stride);
+        k0 = rcx(k0, lane, size, stride);
+        k1 = rcx(k1, lane + 32, size, stride);
       }
     }
   }
+}
+// Merge two descending 32-lists held one key per lane (lane 0 best): keep
+// the better of run[l] and blk[31 - l] (a bitonic sequence holding the top
+// 32 of both) and sort it descending.
+__device__ __forceinline__ uint64_t rmerge32(uint64_t run, uint64_t blk, int lane) {
+  const uint64_t o = rshfl(blk, 31 - lane);
+  run = o > run ? o : run;
+#pragma unroll
+  for (int stride = 16; stride > 0; stride >>= 1) run = rcx(run, lane, 64, stride);
+  return run;
 }
 
 // 24-bit packed word at byte offset o of a staged row (bits 24..31 garbage).
@@ -135,7 +139,7 @@ template <int QN, int NW>
 struct RouteSmem {
   float Q[QN][128];
   float O[QN][128];
-  float M[QN], invL[QN], L[QN];
+  float M[QN], invL[QN], L[QN], mlb[QN];   // mlb = M log2(e) + log2(L)
   float red[NW][QN], red2[NW][QN];
   float nk[QN], nv[QN];
   int sel[QN][kRSel];
@@ -211,6 +215,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       sm.M[i] = M;
       sm.L[i] = L;
       sm.invL[i] = L > 0.f ? 1.0f / L : 0.f;
+      sm.mlb[i] = L > 0.f ? fmaf(M, kRL2e, __log2f(L)) : INFINITY;
     }
   }
   __syncthreads();
@@ -283,15 +288,29 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           const float4 x = srow[q4];
           sv[4 * q4] = x.x; sv[4 * q4 + 1] = x.y; sv[4 * q4 + 2] = x.z; sv[4 * q4 + 3] = x.w;
         }
-        // attention weight of position j (token pos_tok(j)); 0 past the valid rows
+        // attention weight of position j (token pos_tok(j)); 0 past the valid
+        // rows: 2^(s log2(e) - M log2(e) - log2(L))
         float A[16];
+        const float mlb = sm.mlb[i];
 #pragma unroll
-        for (int j = 0; j < 16; ++j)
-          A[j] = pos_tok(j, a.s_perm) < nv ? rex2((sv[j] - sm.M[i]) * kRL2e) * sm.invL[i] : 0.f;
+        for (int j = 0; j < 16; ++j) A[j] = pos_tok(j, a.s_perm) < nv ? rex2(fmaf(sv[j], kRL2e, -mlb)) : 0.f;
+        // attention mass of each 4-token V block (positions in ascending order)
+        float bm[4] = {0.f, 0.f, 0.f, 0.f};
+        if (d.vtb == 4) {
+          if (a.s_perm) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) bm[((j >> 1) + 8 * (j & 1)) >> 2] += A[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) bm[j >> 2] += A[j];
+          }
+        }
         for (int j = 0; j < d.SK; ++j) {
           const int e = p * d.SK + j;
           const int grp = live ? a.cache.k_slot_group[pg * d.SK + j] : -1;
           const float4* wrow = reinterpret_cast<const float4*>(a.kw + ((static_cast<int64_t>(bh) * QN + i) * KG + e) * kPage);
+          // ||dS * A(1-A)|| with dS = q.R_K / sqrt(D): the 1/sqrt(D) is
+          // applied to the root
           float ss = 0.f;
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
@@ -300,7 +319,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
 #pragma unroll
             for (int u = 0; u < 4; ++u) {
               const float Au = A[4 * q4 + u];
-              const float term = (wa[u] * a.sf) * (Au * (1.f - Au));   // dS = q.R_K / sqrt(D) (one ulp of the division)
+              const float term = wa[u] * fmaf(-Au, Au, Au);
               ss = fmaf(term, term, ss);
             }
           }
@@ -308,7 +327,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           if (i == 0) cntk += ok;
           float v = -1.f;
           if (ok && may_k) {
-            float ks = sqrtf(ss) * vc;
+            float ks = sqrtf(ss) * a.sf * vc;
             if (!(ks == ks) || isinf(ks)) ks = 0.f;
             v = fmaxf(ks, 0.f) * rp.sensitivity;
           }
@@ -325,10 +344,14 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
             const float err = f16_bits_to_f32(d.NV == 4 ? static_cast<uint16_t>(((vb & 2) ? ve4.y : ve4.x) >> (16 * (vb & 1)))
                                                         : a.cache.v_err[pg * d.NV + vb]);
             float mass = 0.f;
+            if (d.vtb == 4) {
+              mass = vb == 0 ? bm[0] : (vb == 1 ? bm[1] : (vb == 2 ? bm[2] : bm[3]));
+            } else {
 #pragma unroll
-            for (int jj = 0; jj < 16; ++jj) {
-              const int t = pos_tok(jj, a.s_perm);
-              if (t >= t0 && t < t1) mass += A[jj];
+              for (int jj = 0; jj < 16; ++jj) {
+                const int t = pos_tok(jj, a.s_perm);
+                if (t >= t0 && t < t1) mass += A[jj];
+              }
             }
             v = __fmul_rn(__fmul_rn(mass, err), rp.sensitivity);
           }
@@ -678,12 +701,10 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         const int nc = sm.gcount;
         if (nc <= 64) {
           if (warp == 0) {
-            float v0 = lane < nc ? sm.gv[32 + lane] : -2.f;
-            int i0 = lane < nc ? sm.gi[32 + lane] : 0x7fffffff;
-            float v1 = lane + 32 < nc ? sm.gv[64 + lane] : -2.f;
-            int i1 = lane + 32 < nc ? sm.gi[64 + lane] : 0x7fffffff;
-            rsort64(v0, i0, v1, i1, lane);
-            publish(i, v0, i0, k);
+            uint64_t k0 = rkey(lane < nc ? sm.gv[32 + lane] : -2.f, lane < nc ? sm.gi[32 + lane] : 0x7fffffff);
+            uint64_t k1 = rkey(lane + 32 < nc ? sm.gv[64 + lane] : -2.f, lane + 32 < nc ? sm.gi[64 + lane] : 0x7fffffff);
+            rsort64(k0, k1, lane);
+            publish(i, rkey_score(k0), rkey_index(k0), k);
           }
           __syncthreads();
           return;
@@ -691,25 +712,23 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       }
       __syncthreads();
     }
-    float rv = -2.f;
-    int ri = 0x7fffffff;
+    uint64_t run = rkey(-2.f, 0x7fffffff);
     for (int b0 = lo + warp * 64; b0 < hi; b0 += NW * 64) {
       const int e0 = b0 + lane, e1 = b0 + lane + 32;
       float v0 = e0 < hi ? row[e0] : -2.f, v1 = e1 < hi ? row[e1] : -2.f;
       v0 = v0 == v0 ? v0 : -1.f;
       v1 = v1 == v1 ? v1 : -1.f;
-      int i0 = e0 < hi ? e0 : 0x7fffffff, i1 = e1 < hi ? e1 : 0x7fffffff;
-      rsort64(v0, i0, v1, i1, lane);
-      warp_merge32(rv, ri, v0, i0, lane);
+      uint64_t k0 = rkey(v0, e0 < hi ? e0 : 0x7fffffff), k1 = rkey(v1, e1 < hi ? e1 : 0x7fffffff);
+      rsort64(k0, k1, lane);
+      run = rmerge32(run, k0, lane);
     }
-    sm.gv[warp * 32 + lane] = rv;
-    sm.gi[warp * 32 + lane] = ri;
+    sm.gv[warp * 32 + lane] = rkey_score(run);
+    sm.gi[warp * 32 + lane] = rkey_index(run);
     __syncthreads();
     if (warp == 0) {
-      float mv = sm.gv[lane];
-      int mi = sm.gi[lane];
-      for (int w = 1; w < NW; ++w) warp_merge32(mv, mi, sm.gv[w * 32 + lane], sm.gi[w * 32 + lane], lane);
-      publish(i, mv, mi, k);
+      uint64_t m = rkey(sm.gv[lane], sm.gi[lane]);
+      for (int w = 1; w < NW; ++w) m = rmerge32(m, rkey(sm.gv[w * 32 + lane], sm.gi[w * 32 + lane]), lane);
+      publish(i, rkey_score(m), rkey_index(m), k);
     }
     __syncthreads();
   };
@@ -772,13 +791,14 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       const int e = lane < nsel ? sm.sel[i][lane] : -1;
       const bool isk = e >= 0 && e < KG, isv = e >= KG;
       const int p = isk ? e / d.SK : -1;
+      const int e_lo = isk ? p * d.SK : 0, e_hi = isk ? e_lo + d.SK : 0;   // the page's K entries
       bool leader = isk;
       int msk = 0;
       for (int k = 0; k < nsel; ++k) {
         const int ek = sm.sel[i][k];
-        if (isk && ek < KG && ek / d.SK == p) {
+        if (ek >= e_lo && ek < e_hi) {
           if (k < lane) leader = false;
-          msk |= 1 << (ek % d.SK);
+          msk |= 1 << (ek - e_lo);
         }
       }
       const unsigned lt = (1u << lane) - 1u;
