@@ -270,6 +270,10 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
   a.dq_keys[2] = i3_key2(6, 6);
   a.dq_keys[3] = 0x64086408u;
   a.dq_keys[4] = 0x54805480u;
+  a.dq_keys[5] = i3_key2(1, 0);
+  a.dq_keys[6] = i3_key2(4, 3);
+  a.dq_keys[7] = i3_key2(7, 6);
+  a.dq_keys[8] = i3_key2(2, 2);
   a.sketch_proj = sketch_proj;
   a.rp = rp;
   a.force_generic = 0;

@@ -30,6 +30,7 @@
 // removed with HSUB2 and the scale applied with HMUL2, i.e. fp16(code *
 // scale) rounded once, as the reference dequantizes; scale codes become
 // fp16(int8 * master) the same way.
+#include <type_traits>
 #include "common.cuh"
 #include "internal.h"
 #include "decode_args.h"
@@ -86,7 +87,7 @@ __device__ __forceinline__ uint32_t word24_at(const uint8_t* row, int o) {
 // in registers: a key is both the XOR operand of the LOP3 (whose immediate
 // slot holds the mask) and the subtrahend of the HSUB2.
 struct Keys {
-  uint32_t k0, k3, k6, n0, n4;
+  uint32_t k0, k3, k6, n0, n4, p10, p43, p76, p22;
 };
 // exact half2 (code_lo, code_hi) * sig2 of two 3-bit fields at mantissa bit S
 template <int S>
@@ -94,6 +95,54 @@ __device__ __forceinline__ uint32_t i3p(uint32_t t, uint32_t key, uint32_t sig2)
   uint32_t x;  // (t & mask) ^ key in one LOP3
   asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(x) : "r"(t), "n"(i3_mask2(S, S)), "r"(key));
   return h2mul(h2sub(x, key), sig2);
+}
+
+// exact half2 (code_lo, code_hi) * sig2 of a 3-bit field at mantissa bit SL
+// of the low half and one at bit SH of the high half
+template <int SL, int SH>
+__device__ __forceinline__ uint32_t i3q(uint32_t t, uint32_t key, uint32_t sig2) {
+  uint32_t x;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(x) : "r"(t), "n"(i3_mask2(SL, SH)), "r"(key));
+  return h2mul(h2sub(x, key), sig2);
+}
+
+// A thread's 32 INT3 channels of a K row (96 bits in x0..x2, channel i at
+// bit 3i) -> 16 half2 operands, channel pairs kPairs[j], from seven 32-bit
+// windows of the row: a window starting at bit b = 2 (mod 3) holds three
+// fields at bits 1, 4, 7 of its low half and three at bits 0, 3, 6 of its
+// high half, so one LOP3 per pair picks both fields without further shifts.
+//   window  start bit  pairs (low channel, high channel)
+//   x0 << 1     -1     (0,5) (1,6) (2,7)
+//   x1:x0 >> 8   8     (3,8) (4,9)
+//   x1:x0 >> 29 29     (10,15) (11,16) (12,17)
+//   x2:x1 >> 6  38     (13,18) (14,19)
+//   x2:x1 >> 27 59     (20,25) (21,26) (22,27)
+//   x2 >> 4     68     (23,28) (24,29)
+//   (x2 >> 24) * (1 + 2^13): channel 30 at bit 2, channel 31 at bit 18
+__device__ constexpr int kPairs[16][2] = {{0, 5},   {1, 6},   {2, 7},   {3, 8},   {4, 9},   {10, 15},
+                                          {11, 16}, {12, 17}, {13, 18}, {14, 19}, {20, 25}, {21, 26},
+                                          {22, 27}, {23, 28}, {24, 29}, {30, 31}};
+__device__ __forceinline__ void k_row32(uint32_t x0, uint32_t x1, uint32_t x2, uint32_t sig2, const Keys& K,
+                                        uint32_t (&o)[16]) {
+  const uint32_t w1 = x0 << 1, w2 = __funnelshift_r(x0, x1, 8), w3 = __funnelshift_r(x0, x1, 29);
+  const uint32_t w4 = __funnelshift_r(x1, x2, 6), w5 = __funnelshift_r(x1, x2, 27), w6 = x2 >> 4;
+  const uint32_t w7 = (x2 >> 24) * 8193u;
+  o[0] = i3q<1, 0>(w1, K.p10, sig2);
+  o[1] = i3q<4, 3>(w1, K.p43, sig2);
+  o[2] = i3q<7, 6>(w1, K.p76, sig2);
+  o[3] = i3q<1, 0>(w2, K.p10, sig2);
+  o[4] = i3q<4, 3>(w2, K.p43, sig2);
+  o[5] = i3q<1, 0>(w3, K.p10, sig2);
+  o[6] = i3q<4, 3>(w3, K.p43, sig2);
+  o[7] = i3q<7, 6>(w3, K.p76, sig2);
+  o[8] = i3q<1, 0>(w4, K.p10, sig2);
+  o[9] = i3q<4, 3>(w4, K.p43, sig2);
+  o[10] = i3q<1, 0>(w5, K.p10, sig2);
+  o[11] = i3q<4, 3>(w5, K.p43, sig2);
+  o[12] = i3q<7, 6>(w5, K.p76, sig2);
+  o[13] = i3q<1, 0>(w6, K.p10, sig2);
+  o[14] = i3q<4, 3>(w6, K.p43, sig2);
+  o[15] = i3q<2, 2>(w7, K.p22, sig2);
 }
 
 // One packed K word (codes f0..f7, 3 bits each) -> half2 operands
@@ -260,7 +309,15 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   // i feeds k-steps 2i and 2i+1 (channel pairs as the k_quads / k_quads4
   // operands pair them).  Built once per CTA: warp w fills the k-steps of the
   // words i with i % kWarps == w; every warp then loads all of them.
-  for (int i = warp; i < KW; i += kWarps) {
+  constexpr bool kRow32 = BITS == 3 && D == 128;   // k_row32 operand order
+  if constexpr (kRow32) {        // k-step ks takes channel pairs 2ks, 2ks+1 of kPairs
+    for (int ks = warp; ks < KS; ks += kWarps) {
+      const int c = tig * 32;
+      qbs[ks][lane] = make_uint2(pack_h2(qp(c + kPairs[2 * ks][0]), qp(c + kPairs[2 * ks][1])),
+                                 pack_h2(qp(c + kPairs[2 * ks + 1][0]), qp(c + kPairs[2 * ks + 1][1])));
+    }
+  }
+  for (int i = warp; i < (kRow32 ? 0 : KW); i += kWarps) {
     const int c = tig * (D / 4) + 8 * i;
     if constexpr (BITS == 3) {   // k_quads: (f0,f3) (f1,f4) | (f2,f5) (f6,f7)
       qbs[2 * i][lane] = make_uint2(pack_h2(qp(c + 0), qp(c + 3)), pack_h2(qp(c + 1), qp(c + 4)));
@@ -298,7 +355,8 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
     qb[kb][1] = v.y;
   }
 
-  const Keys KY = {a.dq_keys[0], a.dq_keys[1], a.dq_keys[2], a.dq_keys[3], a.dq_keys[4]};
+  const Keys KY = {a.dq_keys[0], a.dq_keys[1], a.dq_keys[2], a.dq_keys[3], a.dq_keys[4],
+                   a.dq_keys[5], a.dq_keys[6], a.dq_keys[7], a.dq_keys[8]};
   float o[KS][4];
 #pragma unroll
   for (int j = 0; j < KS; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
@@ -327,6 +385,18 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
     const uint8_t* ks = st + g.ksOff + pp * kPage * G;
     const uint32_t sig = i8_scale_pair(static_cast<uint32_t>(ks[kso0]) | (static_cast<uint32_t>(ks[kso8]) << 16), km2);
     const uint32_t sig0 = prmt(sig, sig, 0x1010), sig8 = prmt(sig, sig, 0x3232);
+    if constexpr (kRow32) {
+      uint32_t p0[16], p8[16];
+      k_row32(lds32(kc + ko0), lds32(kc + ko0 + 4), lds32(kc + ko0 + 8), sig0, KY, p0);
+      k_row32(lds32(kc + ko8), lds32(kc + ko8 + 4), lds32(kc + ko8 + 8), sig8, KY, p8);
+      float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+      for (int ks = 0; ks < KS; ++ks)
+        mma_f16(acc[ks & 1], p0[2 * ks], p8[2 * ks], p0[2 * ks + 1], p8[2 * ks + 1], qb[ks][0], qb[ks][1]);
+      s0 = __fmul_rn((acc[0][0] + acc[1][0]) + (acc[0][1] + acc[1][1]), a.sf);
+      s1 = __fmul_rn((acc[0][2] + acc[1][2]) + (acc[0][3] + acc[1][3]), a.sf);
+      return;
+    }
     uint32_t w0[KW], w8[KW];
     if constexpr (BITS == 4) {
 #pragma unroll
@@ -500,54 +570,62 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
       break;
     }
     const uint8_t* st = wsm + (c % kNS) * g.stage;
-    const bool two = pbase + 1 < pb;
-    const int nv0 = m_valid[mi], nv1 = two ? m_valid[mi + 1] : 0;
+    // a full stage (two pages) runs as one straight-line block; the odd
+    // last page of a range takes the one-page form
+    auto stage = [&](auto npc) {
+      constexpr bool two = decltype(npc)::value == 2;
+      const int nv0 = m_valid[mi], nv1 = two ? m_valid[mi + 1] : 0;
 
-    // ── logits of both pages ──
-    float s00, s01, s10 = 0.f, s11 = 0.f;
-    k_side(st, 0, m_km[mi], s00, s01);
-    if (two) k_side(st, 1, m_km[mi + 1], s10, s11);
-    if (q_ok) {
-      st_f2_pol(Srow + static_cast<int64_t>(pbase) * kPage, s00, s01, pol_keep);
-      if (two) st_f2_pol(Srow + static_cast<int64_t>(pbase + 1) * kPage, s10, s11, pol_keep);
-    }
-    if (kslot) {
-      slot_side(st, 0, pbase, mi, nv0);
-      if (two) slot_side(st, 1, pbase + 1, mi + 1, nv1);
-    }
-
-    // ── online softmax for query tig over the stage's tokens ──
-    const bool v00 = gid < nv0, v01 = gid + 8 < nv0, v10 = gid < nv1, v11 = gid + 8 < nv1;
-    float pmax = fmaxf(fmaxf(v00 ? s00 : -INFINITY, v01 ? s01 : -INFINITY),
-                       fmaxf(v10 ? s10 : -INFINITY, v11 ? s11 : -INFINITY));
-    pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 4));
-    pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 8));
-    pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 16));
-    if (__any_sync(0xffffffffu, pmax > m_run)) {
-      const float m_new = fmaxf(m_run, pmax);
-      const float alpha = m_new > m_run ? (m_run == -INFINITY ? 0.f : ex2((m_run - m_new) * kLog2e)) : 1.f;
-      l_part *= alpha;
-#pragma unroll
-      for (int j = 0; j < KS; ++j) {
-        o[j][0] *= alpha; o[j][1] *= alpha; o[j][2] *= alpha; o[j][3] *= alpha;
+      // ── logits of both pages ──
+      float s00, s01, s10 = 0.f, s11 = 0.f;
+      k_side(st, 0, m_km[mi], s00, s01);
+      if constexpr (two) k_side(st, 1, m_km[mi + 1], s10, s11);
+      if (q_ok) {
+        st_f2_pol(Srow + static_cast<int64_t>(pbase) * kPage, s00, s01, pol_keep);
+        if constexpr (two) st_f2_pol(Srow + static_cast<int64_t>(pbase + 1) * kPage, s10, s11, pol_keep);
       }
-      m_run = m_new;
-    }
-    const float mb = m_run * kLog2e;
-    const float p00 = v00 ? ex2(fmaf(s00, kLog2e, -mb)) : 0.f;
-    const float p01 = v01 ? ex2(fmaf(s01, kLog2e, -mb)) : 0.f;
-    const float p10 = v10 ? ex2(fmaf(s10, kLog2e, -mb)) : 0.f;
-    const float p11 = v11 ? ex2(fmaf(s11, kLog2e, -mb)) : 0.f;
-    l_part += (p00 + p01) + (p10 + p11);
+      if (kslot) {
+        slot_side(st, 0, pbase, mi, nv0);
+        if constexpr (two) slot_side(st, 1, pbase + 1, mi + 1, nv1);
+      }
 
-    // ── values ──
-    uint32_t pb0, pb1;
-    p_operands(p00, p01, pb0, pb1);
-    v_side(st, 0, m_vm[mi], pb0, pb1);
-    if (two) {
-      p_operands(p10, p11, pb0, pb1);
-      v_side(st, 1, m_vm[mi + 1], pb0, pb1);
-    }
+      // ── online softmax for query tig over the stage's tokens ──
+      const bool v00 = gid < nv0, v01 = gid + 8 < nv0, v10 = gid < nv1, v11 = gid + 8 < nv1;
+      float pmax = fmaxf(fmaxf(v00 ? s00 : -INFINITY, v01 ? s01 : -INFINITY),
+                         fmaxf(v10 ? s10 : -INFINITY, v11 ? s11 : -INFINITY));
+      pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 4));
+      pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 8));
+      pmax = fmaxf(pmax, __shfl_xor_sync(0xffffffffu, pmax, 16));
+      if (__any_sync(0xffffffffu, pmax > m_run)) {
+        const float m_new = fmaxf(m_run, pmax);
+        const float alpha = m_new > m_run ? (m_run == -INFINITY ? 0.f : ex2((m_run - m_new) * kLog2e)) : 1.f;
+        l_part *= alpha;
+#pragma unroll
+        for (int j = 0; j < KS; ++j) {
+          o[j][0] *= alpha; o[j][1] *= alpha; o[j][2] *= alpha; o[j][3] *= alpha;
+        }
+        m_run = m_new;
+      }
+      const float mb = m_run * kLog2e;
+      const float p00 = v00 ? ex2(fmaf(s00, kLog2e, -mb)) : 0.f;
+      const float p01 = v01 ? ex2(fmaf(s01, kLog2e, -mb)) : 0.f;
+      const float p10 = v10 ? ex2(fmaf(s10, kLog2e, -mb)) : 0.f;
+      const float p11 = v11 ? ex2(fmaf(s11, kLog2e, -mb)) : 0.f;
+      l_part += (p00 + p01) + (p10 + p11);
+
+      // ── values ──
+      uint32_t pb0, pb1;
+      p_operands(p00, p01, pb0, pb1);
+      v_side(st, 0, m_vm[mi], pb0, pb1);
+      if constexpr (two) {
+        p_operands(p10, p11, pb0, pb1);
+        v_side(st, 1, m_vm[mi + 1], pb0, pb1);
+      }
+    };
+    if (pbase + 1 < pb)
+      stage(std::integral_constant<int, 2>{});
+    else
+      stage(std::integral_constant<int, 1>{});
     __syncwarp();
     if (lane == 0 && c + kNS < n_chunks) {
       fence_proxy_async();
