@@ -274,6 +274,10 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
   a.dq_keys[6] = i3_key2(4, 3);
   a.dq_keys[7] = i3_key2(7, 6);
   a.dq_keys[8] = i3_key2(2, 2);
+  a.dq_keys[9] = i3_key2(1, 1);
+  a.dq_keys[10] = i3_key2(4, 4);
+  a.dq_keys[11] = i3_key2(7, 7);
+  a.dq_keys[12] = i3_key2(5, 5);
   a.sketch_proj = sketch_proj;
   a.rp = rp;
   a.force_generic = 0;

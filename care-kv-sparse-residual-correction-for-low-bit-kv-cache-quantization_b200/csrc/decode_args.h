@@ -29,10 +29,10 @@ struct DecodeArgs {
   int s_perm;       // 1: S and kw hold a page's 16 tokens in tok_pos() order
   // fp16 magic keys of the exact low-bit dequantization (3-bit fields at
   // mantissa bit 0, 3, 6 of both halves; 4-bit fields at bit 0, 4; 3-bit
-  // field pairs at bits (1, 0), (4, 3), (7, 6), (2, 2) of the low / high
-  // half), passed as arguments so the kernels hold them in registers
-  // instead of re-creating them per use
-  uint32_t dq_keys[9];
+  // field pairs at bits (1, 0), (4, 3), (7, 6), (2, 2), (1, 1), (4, 4),
+  // (7, 7), (5, 5) of the low / high half), passed as arguments so the
+  // kernels hold them in registers instead of re-creating them per use
+  uint32_t dq_keys[13];
   const float* sketch_proj;
   carekv_route_params_t rp;
   int force_generic;  // 1: use the generic split-K pass (tests)

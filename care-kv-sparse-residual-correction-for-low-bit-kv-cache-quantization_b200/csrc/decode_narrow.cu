@@ -26,7 +26,7 @@
 // their int8 scale codes and the pages' K slot payloads.  Per-page metadata
 // (valid rows, fp16 masters, slot groups and scales) is read 32 pages at a
 // time into shared memory.  Dequantization is exact: 3-bit fields are moved
-// to mantissa bit 0, 3 or 6 of an fp16 half (PRMT / SHF / LOP3), the offset
+// to a mantissa bit 0..7 of an fp16 half (PRMT / SHF / LOP3), the offset
 // removed with HSUB2 and the scale applied with HMUL2, i.e. fp16(code *
 // scale) rounded once, as the reference dequantizes; scale codes become
 // fp16(int8 * master) the same way.
@@ -87,7 +87,7 @@ __device__ __forceinline__ uint32_t word24_at(const uint8_t* row, int o) {
 // in registers: a key is both the XOR operand of the LOP3 (whose immediate
 // slot holds the mask) and the subtrahend of the HSUB2.
 struct Keys {
-  uint32_t k0, k3, k6, n0, n4, p10, p43, p76, p22;
+  uint32_t k0, k3, k6, n0, n4, p10, p43, p76, p22, p11, p44, p77, p55;
 };
 // exact half2 (code_lo, code_hi) * sig2 of two 3-bit fields at mantissa bit S
 template <int S>
@@ -155,22 +155,25 @@ __device__ __forceinline__ void k_quads(uint32_t W, uint32_t sig2, const Keys& K
   o[2] = i3p<6>(t1, K.k6, sig2);
   o[3] = i3p<6>(t2, K.k6, sig2);
 }
-// The same packed word of two rows a (low halves) and b (high halves):
-// fields f0..f2 in r[0], f3..f5 in r[1], f6, f7 in r[2], at bits 0, 3, 6.
+// The same packed word of two rows a (low halves) and b (high halves), one
+// PRMT per register: f0..f2 in r[0] at bits 0, 3, 6; f3..f5 in r[1] at
+// bits 1, 4, 7; f6, f7 in r[2] at bits 2, 5.
 struct VSrc {
   uint32_t r[3];
 };
 __device__ __forceinline__ VSrc v_src(uint32_t Wa, uint32_t Wb) {
   VSrc v;
   v.r[0] = prmt(Wa, Wb, 0x5410);
-  v.r[1] = prmt(Wa, Wb, 0x6521) >> 1;
-  v.r[2] = prmt(Wa, Wb, 0x7632) >> 2;
+  v.r[1] = prmt(Wa, Wb, 0x6521);
+  v.r[2] = prmt(Wa, Wb, 0x7632);
   return v;
 }
 template <int F>
 __device__ __forceinline__ uint32_t v_field(const VSrc& v, const Keys& K, uint32_t sig2) {
-  constexpr int S = 3 * (F < 6 ? F % 3 : F - 6);
-  const uint32_t key = S == 0 ? K.k0 : (S == 3 ? K.k3 : K.k6);
+  // r[0]: f0..f2 at bits 0, 3, 6; r[1]: f3..f5 at 1, 4, 7; r[2]: f6, f7 at 2, 5
+  constexpr int S = F < 3 ? 3 * F : (F < 6 ? 3 * (F - 3) + 1 : 3 * (F - 6) + 2);
+  const uint32_t key = S == 0 ? K.k0 : S == 3 ? K.k3 : S == 6 ? K.k6 : S == 1 ? K.p11 : S == 4 ? K.p44 : S == 7 ? K.p77
+                     : S == 2 ? K.p22 : K.p55;
   return i3p<S>(v.r[F < 3 ? 0 : (F < 6 ? 1 : 2)], key, sig2);
 }
 
@@ -355,8 +358,9 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
     qb[kb][1] = v.y;
   }
 
-  const Keys KY = {a.dq_keys[0], a.dq_keys[1], a.dq_keys[2], a.dq_keys[3], a.dq_keys[4],
-                   a.dq_keys[5], a.dq_keys[6], a.dq_keys[7], a.dq_keys[8]};
+  const Keys KY = {a.dq_keys[0], a.dq_keys[1],  a.dq_keys[2],  a.dq_keys[3],  a.dq_keys[4],
+                   a.dq_keys[5], a.dq_keys[6],  a.dq_keys[7],  a.dq_keys[8],  a.dq_keys[9],
+                   a.dq_keys[10], a.dq_keys[11], a.dq_keys[12]};
   float o[KS][4];
 #pragma unroll
   for (int j = 0; j < KS; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
