@@ -7,10 +7,6 @@ what this library builds:
 
 * ``setup_model`` patches a model object (or loads a local checkpoint
   directory); this build has no model hub access.
-* ``prefill_mode`` defaults to ``fp``: the reference writes
-  ``carekv_stored``, the prefill residual correction (layer.py:458-637),
-  which is not built here (CAREKVLayer raises NotImplementedError for it).
-  Decode runs the full CARE-KV path either way.
 * Only the uniform base quantizer is built (``base_quantizer`` other than
   ``uniform`` raises NotImplementedError).
 """
@@ -35,7 +31,7 @@ class CAREKVAdapter:
                  rv: int = 2, max_rk: int = 4, max_rv: int = 4, bits: int = 3, base_quantizer: str = "uniform",
                  bits_k: int = -1, bits_v: int = -1, max_pages: int = 0, k_store_mode: str = "post_rope",
                  correction_impl: str = "cached", k_channel_group: int = 32, v_token_block: int = 4,
-                 prefill_mode: str = "fp"):
+                 prefill_mode: str = "carekv_stored"):
         if base_quantizer != "uniform":
             raise NotImplementedError(f"base_quantizer={base_quantizer}: only the uniform base is built")
         if mode not in ("fixed", "adaptive"):

@@ -276,6 +276,51 @@ int carekv_decode_attention(const carekv_config_t* cfg, const carekv_cache_t* ca
                           *params, workspace, workspace_bytes_, sketch_proj, as_stream(stream));
 }
 
+int carekv_prefill_workspace_bytes(const carekv_config_t* cfg, int32_t n_pos, int32_t max_pages_used,
+                                   size_t* bytes) {
+  CHECK(validate_config(cfg));
+  if (!bytes || n_pos < 0 || max_pages_used < 1 || max_pages_used > cfg->max_pages) return CAREKV_ERR_INVALID_ARG;
+  *bytes = prefill_workspace_bytes(*cfg, n_pos, max_pages_used);
+  return CAREKV_OK;
+}
+
+int carekv_prefill_correction(const carekv_config_t* cfg, const carekv_cache_t* cache, int32_t layer, int32_t seq,
+                              int32_t n_pos, int32_t max_pages_used, const void* q, const float* logits,
+                              const float* row_max, const float* attn, const float* attn_sum,
+                              const float* o_base, const float* o_exact, const float* v_rows,
+                              const float* v_pnorm, void* out,
+                              int32_t dtype, const carekv_route_params_t* params, const float* sketch_proj,
+                              void* workspace,
+                              size_t workspace_bytes_, void* stream) {
+  CHECK(validate_config(cfg));
+  CHECK(validate_cache(cfg, cache));
+  CHECK(validate_range(cache, layer, seq, 1, cfg));
+  CHECK(validate_dtype(dtype));
+  if (!params || !q || !attn || !o_base || !out || !workspace) return CAREKV_ERR_INVALID_ARG;
+  if (n_pos < 0 || max_pages_used < 1 || max_pages_used > cfg->max_pages) return CAREKV_ERR_INVALID_ARG;
+  if (params->kind < CAREKV_KIND_BOTH || params->kind > CAREKV_KIND_NONE) return CAREKV_ERR_INVALID_ARG;
+  // the sketch proxy reads the logits and their row maxima (and the sketches)
+  if (params->kind != CAREKV_KIND_NONE && !params->kscore_live &&
+      (!logits || !row_max || !cache->k_sketch || cfg->sketch_dim <= 0 || !sketch_proj))
+    return CAREKV_ERR_INVALID_ARG;
+  if (params->kind != CAREKV_KIND_NONE) {
+    if (params->budget_mode == 0) {
+      if (params->read_k < 0 || params->read_v < 0 || params->read_k + params->read_v > kMaxSelHost)
+        return CAREKV_ERR_UNSUPPORTED;
+    } else {
+      const double nk = static_cast<double>(max_pages_used) * cfg->k_slots_per_page;
+      const double nv = static_cast<double>(max_pages_used) * cfg->v_slots_per_page;
+      const int bk = params->ratio_k > 0 ? std::max(1, static_cast<int>(nk * params->ratio_k)) : 0;
+      const int bv = params->ratio_v > 0 ? std::max(1, static_cast<int>(nv * params->ratio_v)) : 0;
+      if (bk + bv > kMaxSelHost) return CAREKV_ERR_UNSUPPORTED;
+    }
+  }
+  if (n_pos == 0) return CAREKV_OK;
+  return prefill_correction(*cfg, *cache, layer, seq, n_pos, max_pages_used, q, logits, row_max, attn, attn_sum,
+                            o_base, o_exact, v_rows, v_pnorm, out, dtype, *params, sketch_proj, workspace,
+                            workspace_bytes_, as_stream(stream));
+}
+
 int carekv_check_device_errors(const carekv_cache_t* cache, int32_t* flags_out, void* stream) {
   if (!cache || !cache->error_flag) return CAREKV_ERR_INVALID_ARG;
   int32_t h = 0;

@@ -203,6 +203,12 @@ size_t workspace_bytes(const carekv_config_t& c, int seq_count, int p_used) {
   return static_cast<size_t>(ws_layout(c, seq_count, p_used).total);
 }
 
+// The prefill correction reads its logits and partials from the caller:
+// only the selection readback and the scores live in the workspace.
+size_t prefill_workspace_bytes(const carekv_config_t& c, int n_pos, int p_used) {
+  return static_cast<size_t>(ws_layout(c, n_pos, p_used).S);
+}
+
 template <int QN>
 static cudaError_t launch_qn(DecodeArgs& a, cudaStream_t st, int n_bh) {
   dim3 g1(n_bh, a.n_splits);
@@ -281,12 +287,74 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
   a.sketch_proj = sketch_proj;
   a.rp = rp;
   a.force_generic = 0;
+  a.seq_fixed = -1;
+  a.attn = nullptr;
+  a.o_exact = nullptr;
+  a.v_rows = nullptr;
+  a.v_pnorm = nullptr;
   cudaError_t e;
   switch (a.qn) {
     case 1: e = launch_qn<1>(a, st, n_bh); break;
     case 2: e = launch_qn<2>(a, st, n_bh); break;
     case 4: e = launch_qn<4>(a, st, n_bh); break;
     case 8: e = launch_qn<8>(a, st, n_bh); break;
+    default: return CAREKV_ERR_UNSUPPORTED;
+  }
+  return e == cudaSuccess ? CAREKV_OK : CAREKV_ERR_CUDA;
+}
+
+// Stored-slot prefill correction (layer.py:458-637 with the vectorized
+// router, attention.py:576-957): the route kernel over n_pos x H grid rows,
+// row (t, h) holding the QN query heads of kv head h at prefill position t.
+// The caller supplies the attention weights A (causally masked, as the
+// prefill attention produced them) with their row sums, the masked logits
+// and their row maxima (read by the sketch proxy score only), the base
+// output O and sum_t A V (the exact renormalisation's starting point), and
+// optionally the prefill's base V rows and their page norms.
+int prefill_correction(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, int seq, int n_pos,
+                       int p_used, const void* q, const float* logits, const float* row_max, const float* A,
+                       const float* A_sum, const float* O, const float* O_exact, const float* v_rows,
+                       const float* v_pnorm, void* out, int dtype, const carekv_route_params_t& rp,
+                       const float* sketch_proj, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (ws_bytes < prefill_workspace_bytes(cfg, n_pos, p_used)) return CAREKV_ERR_WORKSPACE;
+  DecodeArgs a{};
+  a.cfg = cfg;
+  a.cache = cache;
+  a.layer = layer;
+  a.q = q;
+  a.out = out;
+  a.dt = dtype;
+  a.seq_begin = 0;
+  a.qn = cfg.num_heads / cfg.num_kv_heads;
+  a.pps = p_used;
+  a.n_splits = 0;
+  a.p_used = p_used;
+  a.sf = static_cast<float>(1.0 / std::sqrt(static_cast<double>(cfg.head_dim)));
+  a.sqrt_d = static_cast<float>(std::sqrt(static_cast<double>(cfg.head_dim)));
+  const WsLayout wl = ws_layout(cfg, n_pos, p_used);
+  char* w = static_cast<char*>(ws);
+  a.sel_out = reinterpret_cast<int*>(w + wl.sel);
+  a.scores = reinterpret_cast<float*>(w + wl.scores);
+  a.S = const_cast<float*>(logits);
+  a.pm = const_cast<float*>(row_max);
+  a.po = const_cast<float*>(O);
+  a.attn = A;
+  a.pl = const_cast<float*>(A_sum);
+  a.o_exact = O_exact;
+  a.sketch_proj = sketch_proj;
+  a.kw = nullptr;
+  a.s_perm = 0;
+  a.rp = rp;
+  a.seq_fixed = seq;
+  a.v_rows = v_rows;
+  a.v_pnorm = v_pnorm;
+  const int n_bh = n_pos * cfg.num_kv_heads;
+  cudaError_t e;
+  switch (a.qn) {
+    case 1: e = launch_route<1>(a, st, n_bh); break;
+    case 2: e = launch_route<2>(a, st, n_bh); break;
+    case 4: e = launch_route<4>(a, st, n_bh); break;
+    case 8: e = launch_route<8>(a, st, n_bh); break;
     default: return CAREKV_ERR_UNSUPPORTED;
   }
   return e == cudaSuccess ? CAREKV_OK : CAREKV_ERR_CUDA;

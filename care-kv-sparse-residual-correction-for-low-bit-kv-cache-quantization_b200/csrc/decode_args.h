@@ -36,6 +36,16 @@ struct DecodeArgs {
   const float* sketch_proj;
   carekv_route_params_t rp;
   int force_generic;  // 1: use the generic split-K pass (tests)
+  // prefill correction (route kernel only): every grid row reads cache
+  // sequence seq_fixed (>= 0), the attention weights come from attn (laid
+  // out like S) instead of exp(S - M) / L, and optional base V rows / page
+  // norms replace the cache's dequantised V (the prefill's V_hat with
+  // activation-dtype scales)
+  int seq_fixed;       // -1: sequence seq_begin + row / H
+  const float* attn;   // [bh][qn][p_used*16] attention weights, or null
+  const float* o_exact;  // [bh][qn][D] sum_t A V for the exact form (prefill), or null
+  const float* v_rows;   // [H][p_used*16][D] or null
+  const float* v_pnorm;  // [H][p_used] Frobenius norm of each page's rows, or null
 };
 
 // Position of token t (0..15) inside a page's 16 logits: the narrow pass

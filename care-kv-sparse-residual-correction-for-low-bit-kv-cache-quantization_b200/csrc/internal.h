@@ -26,5 +26,11 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
                      const carekv_route_params_t& rp, void* ws, size_t ws_bytes, const float* sketch_proj,
                      cudaStream_t st);
 size_t workspace_bytes(const carekv_config_t& c, int seq_count, int p_used);
+size_t prefill_workspace_bytes(const carekv_config_t& c, int n_pos, int p_used);
+int prefill_correction(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, int seq, int n_pos,
+                       int p_used, const void* q, const float* logits, const float* row_max, const float* A,
+                       const float* A_sum, const float* O, const float* O_exact, const float* v_rows,
+                       const float* v_pnorm, void* out, int dtype, const carekv_route_params_t& rp,
+                       const float* sketch_proj, void* ws, size_t ws_bytes, cudaStream_t st);
 constexpr int kMaxSelHost = 32;
 }  // namespace carekv

@@ -179,7 +179,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   const Dims d = make_dims(a.cfg);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int s = bh / d.H, h = bh % d.H;
-  const int b = a.seq_begin + s;
+  const int b = a.seq_fixed >= 0 ? a.seq_fixed : a.seq_begin + s;
   const int D = d.D;
   const int Hq = d.H * QN;
   const int64_t lhp = d.lhp(b, a.layer, h);
@@ -197,6 +197,16 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   for (int idx = tid; idx < QN * D; idx += NT) {
     const int i = idx / D, c = idx % D;
     const int64_t base = static_cast<int64_t>(bh) * a.n_splits * QN + i;
+    if (a.n_splits == 0) {   // po holds the base output itself, pm the logit row maxima (prefill)
+      sm.O[i][c] = a.po[(static_cast<int64_t>(bh) * QN + i) * D + c];
+      if (c == 0) {
+        sm.M[i] = a.pm ? a.pm[static_cast<int64_t>(bh) * QN + i] : 0.f;
+        sm.L[i] = 1.f;
+        sm.invL[i] = 1.f;
+        sm.mlb[i] = 0.f;
+      }
+      continue;
+    }
     float M = -INFINITY;
     for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, a.pm[base + sp * QN]);
     float L = 0.f, O = 0.f;
@@ -219,6 +229,9 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
     }
   }
   __syncthreads();
+
+  // attention weight of a logit of query i (the weight itself when a.S holds A)
+  auto attw = [&](float sv, int i) -> float { return a.attn ? sv : rex2((sv - sm.M[i]) * kRL2e) * sm.invL[i]; };
 
   // A fragments for the slot dots: rows gid = q_hi, gid+8 = q_lo of query gid;
   // k-step ks of group g covers channels g*32 + 8*tig + 4*ks + {0..3}
@@ -255,6 +268,8 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   const int NG = KG + VG;
   float* sc = scores_in_smem ? dyn : a.scores + static_cast<int64_t>(bh) * QN * NG;
   const float* Sb = a.S + static_cast<int64_t>(bh) * QN * a.p_used * kPage;
+  // weights source: A itself when given (read through attw), else the logits
+  const float* Wb = a.attn ? a.attn + static_cast<int64_t>(bh) * QN * a.p_used * kPage : Sb;
   const int64_t sst = static_cast<int64_t>(a.p_used) * kPage;
   const bool kind_k = rp.kind == CAREKV_KIND_BOTH || rp.kind == CAREKV_KIND_K;
   const bool kind_v = rp.kind == CAREKV_KIND_BOTH || rp.kind == CAREKV_KIND_V;
@@ -274,14 +289,14 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       // every load of the page is issued before any result is used (the
       // workspace rows exist for every page, so no load waits on a check)
       const int nv = live ? a.cache.valid[pg] : 0;
-      const float vc = live ? sqrtf(a.cache.v_norm2[pg]) : 0.f;
+      const float vc = live ? (a.v_pnorm ? a.v_pnorm[h * a.p_used + p] : sqrtf(a.cache.v_norm2[pg])) : 0.f;
       // the page's 4 V block errors in one load (NV == 4), so the error of a
       // kept block does not wait for the block index
       uint2 ve4 = make_uint2(0u, 0u);
       if (live && d.NV == 4) ve4 = *reinterpret_cast<const uint2*>(a.cache.v_err + pg * 4);
       ntok += nv;
       for (int i = 0; i < QN; ++i) {
-        const float4* srow = reinterpret_cast<const float4*>(Sb + i * sst + p * kPage);
+        const float4* srow = reinterpret_cast<const float4*>(Wb + i * sst + p * kPage);
         float sv[16];
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
@@ -293,7 +308,8 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         float A[16];
         const float mlb = sm.mlb[i];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) A[j] = pos_tok(j, a.s_perm) < nv ? rex2(fmaf(sv[j], kRL2e, -mlb)) : 0.f;
+        for (int j = 0; j < 16; ++j)
+          A[j] = pos_tok(j, a.s_perm) < nv ? (a.attn ? sv[j] : rex2(fmaf(sv[j], kRL2e, -mlb))) : 0.f;
         // attention mass of each 4-token V block (positions in ascending order)
         float bm[4] = {0.f, 0.f, 0.f, 0.f};
         if (d.vtb == 4) {
@@ -391,10 +407,10 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       const uint32_t w0 = *reinterpret_cast<const uint32_t*>(pay + gid * 16 + 4 * tig);
       const uint32_t w1 = *reinterpret_cast<const uint32_t*>(pay + (gid + 8) * 16 + 4 * tig);
       const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
-      const float vc = sqrtf(a.cache.v_norm2[pg]);
+      const float vc = a.v_pnorm ? a.v_pnorm[h * a.p_used + p] : sqrtf(a.cache.v_norm2[pg]);
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
       if (gid < QN) {
-        const float* srow = Sb + gid * sst + p * kPage;
+        const float* srow = Wb + gid * sst + p * kPage;
         s4[0] = srow[tok_pos(2 * tig, a.s_perm)];
         s4[1] = srow[tok_pos(2 * tig + 1, a.s_perm)];
         s4[2] = srow[tok_pos(8 + 2 * tig, a.s_perm)];
@@ -416,7 +432,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         for (int u = 0; u < 4; ++u) {
           if (toks[u] < nv) {
             const float dS = __fdiv_rn(__fmul_rn(dots[u], rs), a.sqrt_d);
-            const float A = rex2((s4[u] - sm.M[gid]) * kRL2e) * sm.invL[gid];
+            const float A = attw(s4[u], gid);
             const float term = dS * (A * (1.f - A));
             ss = fmaf(term, term, ss);
           }
@@ -456,10 +472,13 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       const uint8_t* pay = a.cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes;
       const uint4 raw = *reinterpret_cast<const uint4*>(pay + t * 16);
       const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
-      float sv[QN];
+      float sv[QN], wv[QN];   // logits and attention weights
 #pragma unroll
-      for (int i = 0; i < QN; ++i) sv[i] = t < nv ? Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] : 0.f;
-      const float vn2 = a.cache.v_norm2[pg];
+      for (int i = 0; i < QN; ++i) {
+        sv[i] = t < nv && a.S ? Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] : 0.f;
+        wv[i] = t < nv ? (a.attn ? Wb[i * sst + p * kPage + tok_pos(t, a.s_perm)] : attw(sv[i], i)) : 0.f;
+      }
+      const float vn2 = a.v_pnorm ? a.v_pnorm[h * a.p_used + p] * a.v_pnorm[h * a.p_used + p] : a.cache.v_norm2[pg];
       const uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
       float r[32];
 #pragma unroll
@@ -479,7 +498,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           float term = 0.f;
           if (t < nv) {
             const float dS = __fdiv_rn(dot, a.sqrt_d);
-            const float A = rex2((sv[i] - sm.M[i]) * kRL2e) * sm.invL[i];
+            const float A = wv[i];
             term = dS * (A * (1.f - A));
           }
           float ss = term * term;
@@ -497,12 +516,17 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         for (int i = 0; i < QN; ++i) {
           float A = 0.f, inv = 0.f, vd = 0.f;
           if (t < nv) {
-            A = rex2((sv[i] - sm.M[i]) * kRL2e) * sm.invL[i];
+            A = wv[i];
             inv = __fdiv_rn(1.f, fmaxf(sm.M[i] - sv[i], kREps));
             float acc = 0.f;
             for (int c = 0; c < D; ++c) {
-              const float svv = read_scale(a.cache.v_scale, (pg * kPage + t) * d.G + c / d.gsize, d.scale_mode, mv);
-              const float vh = f16r(__fmul_rn(static_cast<float>(unpack_code(a.cache.v_codes + (pg * kPage + t) * d.R, c, d.bits)), svv));
+              float vh;
+              if (a.v_rows) {
+                vh = a.v_rows[((static_cast<int64_t>(h) * a.p_used + p) * kPage + t) * D + c];
+              } else {
+                const float svv = read_scale(a.cache.v_scale, (pg * kPage + t) * d.G + c / d.gsize, d.scale_mode, mv);
+                vh = f16r(__fmul_rn(static_cast<float>(unpack_code(a.cache.v_codes + (pg * kPage + t) * d.R, c, d.bits)), svv));
+              }
               const float df = vh - sm.O[i][c];
               acc = fmaf(df, df, acc);
             }
@@ -549,7 +573,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         for (int i = 0; i < QN; ++i) {
           float mass = 0.f;
           for (int t = t0; t < t1; ++t)
-            mass += rex2((Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
+            mass += attw(Wb[i * sst + p * kPage + tok_pos(t, a.s_perm)], i);
           sc[i * NG + KG + e] = __fmul_rn(__fmul_rn(mass, err), rp.sensitivity);
         }
       } else {
@@ -775,8 +799,8 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   const int k_item_b = k_codes_b + k_sc_b + kPage * 4;
   const int v_item_b = d.vslot_bytes + kPage * 4;
   const bool bulk = ((reinterpret_cast<uintptr_t>(a.cache.v_codes) | reinterpret_cast<uintptr_t>(a.cache.v_scale) |
-                      reinterpret_cast<uintptr_t>(a.cache.v_slot_data) | reinterpret_cast<uintptr_t>(a.S)) & 15) == 0 &&
-                    k_codes_b % 16 == 0 && k_sc_b % 16 == 0 && d.vslot_bytes % 16 == 0;
+                      reinterpret_cast<uintptr_t>(a.cache.v_slot_data) | reinterpret_cast<uintptr_t>(Wb)) & 15) == 0 &&
+                    k_codes_b % 16 == 0 && k_sc_b % 16 == 0 && d.vslot_bytes % 16 == 0 && a.v_rows == nullptr;
   if (tid == 0) {
     mbar_init(&sm.stg_bar, 1);
     fence_mbar_init();
@@ -868,13 +892,13 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           const int64_t pg = lhp * d.P + p;
           bulk_g2s(dst, a.cache.v_codes + pg * k_codes_b, k_codes_b, &sm.stg_bar);
           bulk_g2s(dst + k_codes_b, reinterpret_cast<const uint8_t*>(a.cache.v_scale) + pg * k_sc_b, k_sc_b, &sm.stg_bar);
-          bulk_g2s(dst + k_codes_b + k_sc_b, Sb + i * sst + p * kPage, kPage * 4, &sm.stg_bar);
+          bulk_g2s(dst + k_codes_b + k_sc_b, Wb + i * sst + p * kPage, kPage * 4, &sm.stg_bar);
         } else {
           const int ev = sm.vsel[it - nkp];
           const int pv = ev / d.SV, j = ev % d.SV;
           const int64_t pg = lhp * d.P + pv;
           bulk_g2s(dst, a.cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes, d.vslot_bytes, &sm.stg_bar);
-          bulk_g2s(dst + d.vslot_bytes, Sb + i * sst + pv * kPage, kPage * 4, &sm.stg_bar);
+          bulk_g2s(dst + d.vslot_bytes, Wb + i * sst + pv * kPage, kPage * 4, &sm.stg_bar);
         }
       }
     };
@@ -942,21 +966,22 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           const int u = item, p = sm.kp_page[u];
           const int64_t pg = lhp * d.P + p;
           const int nv = sm.kp_nv[u];
+          const float* vrow = a.v_rows ? a.v_rows + (static_cast<int64_t>(h) * a.p_used + p) * kPage * D : nullptr;
           if (!bulk) {
-            for (int w = lane; w < k_codes_b / 4; w += 32)
+            for (int w = lane; w < (vrow ? 0 : k_codes_b / 4); w += 32)
               reinterpret_cast<uint32_t*>(stg)[w] = reinterpret_cast<const uint32_t*>(a.cache.v_codes + pg * k_codes_b)[w];
-            for (int w = lane; w < k_sc_b; w += 32)
+            for (int w = lane; w < (vrow ? 0 : k_sc_b); w += 32)
               stg[k_codes_b + w] = reinterpret_cast<const uint8_t*>(a.cache.v_scale)[pg * k_sc_b + w];
             if (lane < kPage)
-              reinterpret_cast<float*>(stg + k_codes_b + k_sc_b)[lane] = Sb[i * sst + p * kPage + lane];
+              reinterpret_cast<float*>(stg + k_codes_b + k_sc_b)[lane] = Wb[i * sst + p * kPage + lane];
             __syncwarp();
           }
           const float* srow = reinterpret_cast<const float*>(stg + k_codes_b + k_sc_b);
-          for (int x = lane; x < kPage * G; x += 32)
+          for (int x = lane; x < (vrow ? 0 : kPage * G); x += 32)
             sm.stage_sc[warp][x] = read_scale(stg + k_codes_b, x, d.scale_mode, sm.kp_vm[u]);
           float cf = 0.f;
           if (lane < kPage && lane < nv) {
-            const float A = rex2((srow[tok_pos(lane, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
+            const float A = attw(srow[tok_pos(lane, a.s_perm)], i);
             const float wk = sm.ds[u][lane];
             if (exact) {
               const float dsv = __fdiv_rn(wk, a.sqrt_d);
@@ -968,7 +993,16 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           if (lane < kPage) sm.coef[warp][lane] = cf;
           zp += warp_sum(cf);
           __syncwarp();
-          if (fast3) {
+          if (vrow) {   // base V rows given by the caller
+            for (int t = 0; t < nv; ++t) {
+              const float c = sm.coef[warp][t];
+#pragma unroll
+              for (int jj = 0; jj < 4; ++jj) {
+                const int ch = lane + 32 * jj;
+                if (ch < D) num[jj] = fmaf(c, vrow[t * D + ch], num[jj]);
+              }
+            }
+          } else if (fast3) {
             for (int t = rg; t < nv; t += RG) {
               const float sg = sm.stage_sc[warp][t * G + (8 * wl) / d.gsize];
               acc_int3_word(stg + t * R, wl, pack_h2(sg, sg), sm.coef[warp][t], acc8);
@@ -997,7 +1031,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
             const uint32_t* src = reinterpret_cast<const uint32_t*>(a.cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes);
             for (int w = lane; w < d.vslot_bytes / 4; w += 32) reinterpret_cast<uint32_t*>(stg)[w] = src[w];
             if (lane < kPage)
-              reinterpret_cast<float*>(stg + d.vslot_bytes)[lane] = Sb[i * sst + p * kPage + lane];
+              reinterpret_cast<float*>(stg + d.vslot_bytes)[lane] = Wb[i * sst + p * kPage + lane];
             __syncwarp();
           }
           const float* srow = reinterpret_cast<const float*>(stg + d.vslot_bytes);
@@ -1008,7 +1042,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
             const int t = t0 + lane;
             float cf = 0.f;
             if (t < t1) {
-              const float A = rex2((srow[tok_pos(t, a.s_perm)] - sm.M[i]) * kRL2e) * sm.invL[i];
+              const float A = attw(srow[tok_pos(t, a.s_perm)], i);
               float w = 1.f;
               if (exact) {
                 const float dsv = u >= 0 ? __fdiv_rn(sm.ds[u][t], a.sqrt_d) : 0.f;
@@ -1056,7 +1090,12 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       float n = 0.f, z = 0.f;
       for (int w = 0; w < NW; ++w) { n += sm.acc[w][tid]; z += sm.z[w]; }
       const float ob = sm.O[i][tid];
-      const float delta = exact ? (__fdiv_rn(fmaf(cbase, ob, n), cbase + z) - ob) : (n - z * ob);
+      // exact form: a_new @ V = (cbase * sum_t A V + num) / (cbase * sum_t A + z); sum_t A V and
+      // sum_t A are O and 1 in decode, given by the caller in the prefill correction
+      const int64_t row = static_cast<int64_t>(bh) * QN + i;
+      const float oe = a.o_exact ? a.o_exact[row * D + tid] : ob;
+      const float as = (a.n_splits == 0 && a.pl) ? a.pl[row] : 1.f;
+      const float delta = exact ? (__fdiv_rn(fmaf(cbase, oe, n), fmaf(cbase, as, z)) - ob) : (n - z * ob);
       store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + tid, ob + delta, a.dt);
     }
     __syncthreads();

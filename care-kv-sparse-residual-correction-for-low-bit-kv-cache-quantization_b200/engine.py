@@ -134,6 +134,59 @@ class DecodeEngine:
             self._stream()), "carekv_decode_attention")
         return out
 
+    def prefill_correct(self, layer: int, seq: int, q: torch.Tensor, attn: torch.Tensor, o_base: torch.Tensor,
+                        o_exact: Optional[torch.Tensor] = None, attn_sum: Optional[torch.Tensor] = None,
+                        logits: Optional[torch.Tensor] = None, row_max: Optional[torch.Tensor] = None,
+                        v_rows: Optional[torch.Tensor] = None, v_pnorm: Optional[torch.Tensor] = None,
+                        out: Optional[torch.Tensor] = None, kind: Optional[str] = None, score_normalize=None,
+                        k_corr_scale=None) -> torch.Tensor:
+        """Stored-slot correction of a prefill (layer.py:458-637): one route /
+        correct pass per (prefill position, kv head) over the slots of
+        sequence `seq`.  With P = the sequence's pages and QN = Hq / Hkv:
+        q [T, Hq, D]; attn, logits [T, Hkv, QN, P*16] fp32; attn_sum, row_max
+        [T, Hkv, QN] fp32; o_base, o_exact [T, Hkv, QN, D] fp32; v_rows
+        [Hkv, P*16, D] fp32; v_pnorm [Hkv, P] fp32.  Returns [T, Hq, D]."""
+        cfg = self.cfg
+        T = q.shape[0]
+        H, QN, D = cfg.num_kv_heads, cfg.num_heads // cfg.num_kv_heads, cfg.head_dim
+        P = self._pages(seq, layer)
+        if P == 0:
+            raise ValueError("prefill_correct: the sequence holds no pages")
+        q = self._check_tensor(q, (T, cfg.num_heads, D), "prefill q")
+
+        def f32(t, shape, what, optional=True):
+            if t is None:
+                if optional:
+                    return None
+                raise ValueError(f"{what} is required")
+            if t.dtype != torch.float32:
+                raise ValueError(f"{what}: expected float32, got {t.dtype}")
+            return self._check_tensor(t, shape, what)
+        attn = f32(attn, (T, H, QN, P * cfg.page_size), "attn", optional=False)
+        o_base = f32(o_base, (T, H, QN, D), "o_base", optional=False)
+        o_exact = f32(o_exact, (T, H, QN, D), "o_exact")
+        attn_sum = f32(attn_sum, (T, H, QN), "attn_sum")
+        logits = f32(logits, (T, H, QN, P * cfg.page_size), "logits")
+        row_max = f32(row_max, (T, H, QN), "row_max")
+        v_rows = f32(v_rows, (H, P * cfg.page_size, D), "v_rows")
+        v_pnorm = f32(v_pnorm, (H, P), "v_pnorm")
+        if out is None:
+            out = torch.empty_like(q)
+        rp = resolve_route_params(cfg, layer, kind=kind, score_normalize=score_normalize, k_corr_scale=k_corr_scale)
+        n = ctypes.c_size_t(0)
+        _lib.check(_lib.lib().carekv_prefill_workspace_bytes(ctypes.byref(self.cache.ccfg), T, P, ctypes.byref(n)),
+                   "carekv_prefill_workspace_bytes")
+        ws = self.workspace(int(n.value))
+
+        def ptr(t):
+            return t.data_ptr() if t is not None else None
+        _lib.check(_lib.lib().carekv_prefill_correction(
+            ctypes.byref(self.cache.ccfg), ctypes.byref(self.cache.c), layer, seq, T, P, q.data_ptr(), ptr(logits),
+            ptr(row_max), attn.data_ptr(), ptr(attn_sum), o_base.data_ptr(), ptr(o_exact), ptr(v_rows),
+            ptr(v_pnorm), out.data_ptr(), _DT[q.dtype], ctypes.byref(rp), self._sketch_ptr(), ws.data_ptr(),
+            ws.numel(), self._stream()), "carekv_prefill_correction")
+        return out
+
     # ── host mirror of the page state ─────────────────────────────────
     # The device keeps num_pages / valid; the host mirrors them per
     # (sequence, layer) as (pages, valid rows of the last page).
@@ -163,12 +216,14 @@ class DecodeEngine:
     # ── parity readback (tests) ───────────────────────────────────────
     MAX_SEL = 32
 
-    def last_selection(self, layer: int, seq_begin: int, seq_count: int, pages: int):
+    def last_selection(self, layer: int, seq_begin: int, seq_count: int, pages: int, cache_seq: Optional[int] = None):
         """Selected slots of the last attend(): {(seq, kv_head, query): [(kind, page, group), ...]}.
 
         Reads the workspace region the route kernel publishes and maps grid
         indices back to (\"K\", page, channel group) / (\"V\", page, token block)
-        through the cache's slot tables.  Synchronizes the device.
+        through the cache's slot tables.  Synchronizes the device.  After
+        prefill_correct, pass seq_count = the prefill positions and cache_seq =
+        the sequence: rows are then (position, kv_head, query).
         """
         cfg = self.cache.ccfg
         qn = cfg.num_heads // cfg.num_kv_heads
@@ -182,7 +237,7 @@ class DecodeEngine:
         out = {}
         for bh in range(n_bh):
             s, h = divmod(bh, cfg.num_kv_heads)
-            b = seq_begin + s
+            b = seq_begin + s if cache_seq is None else cache_seq
             for i in range(qn):
                 n = int(sel[bh, i, 0])
                 items = []
@@ -193,7 +248,7 @@ class DecodeEngine:
                     else:
                         p, j = divmod(e - KG, SV)
                         items.append(("V", p, int(vb[b, layer, h, p, j])))
-                out[(b, h, i)] = items
+                out[(seq_begin + s, h, i)] = items
         return out
 
     def last_scores(self, seq_count: int, pages: int):

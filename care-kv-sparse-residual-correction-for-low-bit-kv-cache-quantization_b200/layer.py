@@ -15,9 +15,14 @@ kernel.
 
 Prefill attention follows ``CAREKV_PREFILL_MODE`` (layer.py:129-141, default
 ``fp``): ``fp`` attends over the full-precision post-RoPE K / V, ``base_quant``
-over their per-group quantize-dequantize (scales in the activation dtype).  The prefill stored-slot
-correction modes (``carekv_eval``, ``carekv_stored``; layer.py:363-637) are
-not built and raise NotImplementedError.
+over their per-group quantize-dequantize (scales in the activation dtype),
+and ``carekv_stored`` adds the stored-slot correction
+(_apply_sparse_prefill_correction_stored, layer.py:458-637, with the
+vectorized router) to that base attention: the attention weights, logits and
+base output come from PyTorch, the routing and correction of every prefill
+position run in the CUDA route kernel over the slots the prefill just
+stored.  ``carekv_eval`` (the in-memory residual upper bound,
+layer.py:363-453) is not built and raises NotImplementedError.
 """
 
 from __future__ import annotations
@@ -30,7 +35,7 @@ import torch
 from torch import Tensor, nn
 
 from .cache import CAREKVCache
-from .config import CacheConfig
+from .config import CacheConfig, any_read_budget
 from .engine import DecodeEngine
 from .quantizer import QuantConfig, dequantize, quantize
 
@@ -142,11 +147,11 @@ class CAREKVLayer(nn.Module):
                       token_start_abs: int = 0, seq_begin: int = 0) -> Tensor:
         """hidden [B, T, dm] of sequences seq_begin .. seq_begin+B -> [B, T, dm]."""
         mode = resolve_prefill_mode()
-        if mode in ("carekv_eval", "carekv_stored"):
+        if mode == "carekv_eval":
             raise NotImplementedError(
-                f"CAREKV_PREFILL_MODE={mode}: the prefill residual correction (layer.py:363-637) is not "
-                "built in this library; use fp or base_quant")
-        if mode not in ("fp", "base_quant"):
+                "CAREKV_PREFILL_MODE=carekv_eval: the in-memory residual upper bound (layer.py:363-453) is not "
+                "built in this library; use fp, base_quant or carekv_stored")
+        if mode not in ("fp", "base_quant", "carekv_stored"):
             raise ValueError(f"Unknown CAREKV_PREFILL_MODE={mode}")
         cfg = self.cfg
         B, T, _ = hidden.shape
@@ -160,11 +165,84 @@ class CAREKVLayer(nn.Module):
             K_att, V_att = k_post, v
         else:
             K_att, V_att = self._quantize_dequantize(k_post), self._quantize_dequantize(v)
+        if mode == "carekv_stored" and any_read_budget(cfg):
+            O = self._stored_correction(eng, q_post, K_att, V_att, attention_mask, seq_begin)
+            return self._out(O)
         if g > 1:
             K_att = K_att.repeat_interleave(g, dim=1)
             V_att = V_att.repeat_interleave(g, dim=1)
         O = causal_attention(q_post, K_att, V_att, attention_mask)
         return self._out(O)
+
+    def _stored_correction(self, eng: DecodeEngine, q: Tensor, K_hat: Tensor, V_hat: Tensor,
+                           attention_mask: Optional[Tensor], seq_begin: int, chunk: int = 256) -> Tensor:
+        """Base attention over K_hat / V_hat plus the stored-slot correction
+        (layer.py:458-637): q [B, Hq, T, D]; K_hat, V_hat [B, Hkv, T, D] in the
+        activation dtype.  Returns the corrected attention output [B, Hq, T, D].
+
+        Per sequence and chunk of positions the causal attention runs in
+        PyTorch as layer.py:936-972 does (fp32 logits and softmax, weights cast
+        to the activation dtype, output in the activation dtype); the weights,
+        logits, base output and the fp32 attn @ V_hat feed the route kernel,
+        which reads V_hat and its page norms instead of the cache's int8-scale
+        dequantisation, as the reference passes V_hat_stack."""
+        cfg = self.cfg
+        B, Hq, T, D = q.shape
+        H, QN, PS = cfg.num_kv_heads, Hq // cfg.num_kv_heads, cfg.page_size
+        dt = q.dtype
+        out = torch.empty_like(q)
+        for b in range(B):
+            seq = seq_begin + b
+            P = eng._pages(seq, self.layer_id)
+            if eng.cache.lengths[seq][self.layer_id] != T:
+                raise NotImplementedError("carekv_stored prefill correction: the sequence must hold exactly this "
+                                          "prefill (a prompt written in one call)")
+            N = P * PS
+            Kb, Vb = K_hat[b], V_hat[b]                                   # [H, T, D]
+            if QN > 1:
+                Kq, Vq = Kb.repeat_interleave(QN, dim=0), Vb.repeat_interleave(QN, dim=0)
+            else:
+                Kq, Vq = Kb, Vb
+            v_rows = torch.zeros(H, N, D, dtype=torch.float32, device=q.device)
+            v_rows[:, :T] = Vb.float()
+            v_pnorm = v_rows.view(H, P, PS * D).norm(dim=-1).contiguous()
+            mask_b = None
+            if attention_mask is not None:
+                am = attention_mask
+                if am.dim() == 4:
+                    am = am[b if am.shape[0] > 1 else 0, 0]
+                elif am.dim() == 3:
+                    am = am[b if am.shape[0] > 1 else 0]
+                mask_b = am
+            for t0 in range(0, T, chunk):
+                t1 = min(T, t0 + chunk)
+                tc = t1 - t0
+                scores = torch.einsum("hid,hjd->hij", q[b, :, t0:t1].float(), Kq.float()) / math.sqrt(D)
+                if mask_b is not None:
+                    scores = scores + mask_b[t0:t1, :T].to(device=scores.device, dtype=scores.dtype).unsqueeze(0)
+                else:
+                    rows = torch.arange(t0, t1, device=q.device).unsqueeze(1)
+                    cols = torch.arange(T, device=q.device).unsqueeze(0)
+                    scores = scores.masked_fill(cols > rows, torch.finfo(torch.float32).min)
+                attn_w = torch.softmax(scores, dim=-1, dtype=torch.float32).to(dt)
+                o_base = torch.einsum("hij,hjd->hid", attn_w, Vq)             # [Hq, tc, D], activation dtype
+                A = attn_w.float()
+                o_exact = torch.einsum("hij,hjd->hid", A, Vq.float())
+
+                def rows_of(x, fill):                                       # [Hq, tc, T] -> [tc, H, QN, N]
+                    y = torch.full((Hq, tc, N), fill, dtype=torch.float32, device=q.device)
+                    y[..., :T] = x
+                    return y.view(H, QN, tc, N).permute(2, 0, 1, 3).contiguous()
+
+                def per_row(x):                                             # [Hq, tc, ...] -> [tc, H, QN, ...]
+                    return x.reshape(H, QN, tc, *x.shape[2:]).movedim(2, 0).contiguous()
+                res = eng.prefill_correct(
+                    self.layer_id, seq, q[b, :, t0:t1].transpose(0, 1).contiguous(), attn=rows_of(A, 0.0),
+                    o_base=per_row(o_base.float()), o_exact=per_row(o_exact), attn_sum=per_row(A.sum(-1)),
+                    logits=rows_of(scores, torch.finfo(torch.float32).min), row_max=per_row(scores.amax(-1)),
+                    v_rows=v_rows, v_pnorm=v_pnorm)
+                out[b, :, t0:t1] = res.transpose(0, 1)
+        return out
 
     def _quantize_dequantize(self, x: Tensor) -> Tensor:
         """x [..., D] -> per-group quantize then dequantize with scales in x's

@@ -20,6 +20,8 @@
  *   attention.py:979-1039 (base decode) + attention.py:576-957
  *   (vectorized_joint_correction) + residual_router.py:37-76
  *                                   -> carekv_decode_attention
+ *   layer.py:458-637 (_apply_sparse_prefill_correction_stored, vectorized
+ *   router) + attention.py:576-957  -> carekv_prefill_correction
  */
 #ifndef CAREKV_B200_H
 #define CAREKV_B200_H
@@ -252,6 +254,44 @@ int carekv_decode_attention_noalloc(const carekv_config_t *cfg, const carekv_cac
                                     int32_t seq_begin, int32_t seq_count, int32_t max_pages_used,
                                     const carekv_route_params_t *params, const float *sketch_proj,
                                     void *stream);
+
+/* Stored-slot correction of a prefill (CAREKV_PREFILL_MODE=carekv_stored):
+ * for every prefill position t of cache sequence `seq` and every query head,
+ * route over the slots the prefill just stored and add the correction to the
+ * base output, as _apply_sparse_prefill_correction_stored (layer.py:458-637)
+ * does with vectorized_joint_correction per kv head.  Inputs, with
+ * P = max_pages_used and QN = num_heads / num_kv_heads:
+ *   q       [n_pos][num_heads][D] post-RoPE queries in `dtype`
+ *   logits  [n_pos][num_kv_heads][QN][P * 16] fp32 masked logits, token j of
+ *           page p at p*16+j; read by the sketch proxy score only
+ *           (params->kscore_live == 0), may be NULL otherwise
+ *   row_max [n_pos][num_kv_heads][QN] fp32 maximum of each logit row (same
+ *           condition)
+ *   attn    [n_pos][num_kv_heads][QN][P * 16] fp32 attention weights of the
+ *           (causally masked) prefill attention, laid out like logits
+ *   attn_sum [n_pos][num_kv_heads][QN] fp32 row sums of attn, or NULL for 1
+ *   o_base  [n_pos][num_kv_heads][QN][D] fp32 base output: the result where
+ *           nothing is corrected, the start of the linear correction and
+ *           of the sketch proxy's value distances
+ *   o_exact [n_pos][num_kv_heads][QN][D] fp32 attn @ V in fp32, the start
+ *           of the exact renormalisation a_new @ V, or NULL for o_base
+ *   v_rows  [num_kv_heads][P * 16][D] fp32 base V rows the correction reads,
+ *           or NULL for the cache's dequantised V
+ *   v_pnorm [num_kv_heads][P] fp32 Frobenius norm of each page of v_rows, or
+ *           NULL for the cache's page norms
+ * out: [n_pos][num_heads][D] in `dtype`.  The workspace must hold
+ * carekv_prefill_workspace_bytes(cfg, n_pos, max_pages_used).  The router
+ * computes q . R_K from the slot payloads itself. */
+int carekv_prefill_workspace_bytes(const carekv_config_t *cfg, int32_t n_pos, int32_t max_pages_used,
+                                   size_t *bytes);
+int carekv_prefill_correction(const carekv_config_t *cfg, const carekv_cache_t *cache, int32_t layer,
+                              int32_t seq, int32_t n_pos, int32_t max_pages_used, const void *q,
+                              const float *logits, const float *row_max, const float *attn,
+                              const float *attn_sum, const float *o_base, const float *o_exact,
+                              const float *v_rows, const float *v_pnorm, void *out,
+                              int32_t dtype, const carekv_route_params_t *params,
+                              const float *sketch_proj, void *workspace, size_t workspace_bytes,
+                              void *stream);
 
 /* Copy the device error flag to the host and clear it (synchronizes the
  * stream).  Returns CAREKV_OK when no device check tripped. */

@@ -64,7 +64,8 @@ def test_prefill_mode_resolution_and_unbuilt_modes():
     cfg = care_cfg(pkg)
     W = torch.zeros(256, 256)
     layer = pkg.CAREKVLayer(cfg, 0, W, W[:128], W[:128], W)
-    with env(CAREKV_PREFILL_MODE="carekv_stored"):
+    # the in-memory residual upper bound (layer.py:363-453) is the one prefill mode not built
+    with env(CAREKV_PREFILL_MODE="carekv_eval"):
         with pytest.raises(NotImplementedError):
             layer.prefill(None, torch.zeros(4, 256))
 
@@ -108,7 +109,7 @@ def test_adapter_env_config_and_patch():
     ad = ad_mod.CAREKVAdapter(sk=1, sv=1, rk=2, rv=3, max_pages=16)
     e = ad.env()
     assert e["CAREKV_STORE_ABS_K"] == "1" and e["CAREKV_READ_ABS_V"] == "3"
-    assert e["CAREKV_READ_BUDGET_MODE"] == "absolute" and e["CAREKV_PREFILL_MODE"] == "fp"
+    assert e["CAREKV_READ_BUDGET_MODE"] == "absolute" and e["CAREKV_PREFILL_MODE"] == "carekv_stored"
     with pytest.raises(NotImplementedError):
         ad_mod.CAREKVAdapter(base_quantizer="kivi_style")
     keys = list(e)
