@@ -10,11 +10,13 @@ namespace carekv {
 
 constexpr int kRouteWarps = 4;
 
-template <int QN>
+// PF: prefill correction (caller attention weights, base V rows, one cache
+// sequence for every row); the decode instantiation carries none of it.
+template <int QN, bool PF>
 __global__ void __launch_bounds__(kRouteWarps * 32, 8) route_kernel2(DecodeArgs a, int scores_in_smem) {
   __shared__ RouteSmem<QN, kRouteWarps> sm;
   extern __shared__ float dyn[];
-  route_body<QN, kRouteWarps>(a, blockIdx.x, sm, dyn, scores_in_smem);
+  route_body<QN, kRouteWarps, PF>(a, blockIdx.x, sm, dyn, scores_in_smem);
 }
 
 template <int QN>
@@ -22,7 +24,10 @@ cudaError_t launch_route(DecodeArgs& a, cudaStream_t st, int n_bh) {
   const int NG = a.p_used * (a.cfg.k_slots_per_page + a.cfg.v_slots_per_page);
   const size_t sc_bytes = static_cast<size_t>(QN) * NG * sizeof(float);
   const int in_smem = sc_bytes + sizeof(RouteSmem<QN, kRouteWarps>) <= 46 * 1024 ? 1 : 0;
-  route_kernel2<QN><<<n_bh, kRouteWarps * 32, in_smem ? sc_bytes : 0, st>>>(a, in_smem);
+  if (a.attn != nullptr)
+    route_kernel2<QN, true><<<n_bh, kRouteWarps * 32, in_smem ? sc_bytes : 0, st>>>(a, in_smem);
+  else
+    route_kernel2<QN, false><<<n_bh, kRouteWarps * 32, in_smem ? sc_bytes : 0, st>>>(a, in_smem);
   return cudaGetLastError();
 }
 

@@ -172,14 +172,20 @@ struct RouteSmem {
 // Route + correct one (sequence, kv head) `bh` with the NW warps of the
 // calling CTA.  `sm` is the CTA's scratch; the scores live in `dyn` when
 // scores_in_smem, else in the workspace.  Every thread of the CTA calls it.
-template <int QN, int NW>
+template <int QN, int NW, bool PF>
 __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSmem<QN, NW>& sm, float* dyn,
                                            int scores_in_smem) {
   constexpr int NT = NW * 32;
   const Dims d = make_dims(a.cfg);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // prefill-correction inputs (PF): compiled out of the decode instantiation
+  const float* const A_in = PF ? a.attn : nullptr;
+  const float* const v_rows = PF ? a.v_rows : nullptr;
+  const float* const v_pnorm = PF ? a.v_pnorm : nullptr;
+  const float* const o_exact = PF ? a.o_exact : nullptr;
+  const bool po_direct = PF && a.n_splits == 0;
   const int s = bh / d.H, h = bh % d.H;
-  const int b = a.seq_fixed >= 0 ? a.seq_fixed : a.seq_begin + s;
+  const int b = PF && a.seq_fixed >= 0 ? a.seq_fixed : a.seq_begin + s;
   const int D = d.D;
   const int Hq = d.H * QN;
   const int64_t lhp = d.lhp(b, a.layer, h);
@@ -197,7 +203,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   for (int idx = tid; idx < QN * D; idx += NT) {
     const int i = idx / D, c = idx % D;
     const int64_t base = static_cast<int64_t>(bh) * a.n_splits * QN + i;
-    if (a.n_splits == 0) {   // po holds the base output itself, pm the logit row maxima (prefill)
+    if (po_direct) {   // po holds the base output itself, pm the logit row maxima (prefill)
       sm.O[i][c] = a.po[(static_cast<int64_t>(bh) * QN + i) * D + c];
       if (c == 0) {
         sm.M[i] = a.pm ? a.pm[static_cast<int64_t>(bh) * QN + i] : 0.f;
@@ -231,7 +237,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   __syncthreads();
 
   // attention weight of a logit of query i (the weight itself when a.S holds A)
-  auto attw = [&](float sv, int i) -> float { return a.attn ? sv : rex2((sv - sm.M[i]) * kRL2e) * sm.invL[i]; };
+  auto attw = [&](float sv, int i) -> float { return A_in ? sv : rex2((sv - sm.M[i]) * kRL2e) * sm.invL[i]; };
 
   // A fragments for the slot dots: rows gid = q_hi, gid+8 = q_lo of query gid;
   // k-step ks of group g covers channels g*32 + 8*tig + 4*ks + {0..3}
@@ -269,7 +275,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   float* sc = scores_in_smem ? dyn : a.scores + static_cast<int64_t>(bh) * QN * NG;
   const float* Sb = a.S + static_cast<int64_t>(bh) * QN * a.p_used * kPage;
   // weights source: A itself when given (read through attw), else the logits
-  const float* Wb = a.attn ? a.attn + static_cast<int64_t>(bh) * QN * a.p_used * kPage : Sb;
+  const float* Wb = A_in ? A_in + static_cast<int64_t>(bh) * QN * a.p_used * kPage : Sb;
   const int64_t sst = static_cast<int64_t>(a.p_used) * kPage;
   const bool kind_k = rp.kind == CAREKV_KIND_BOTH || rp.kind == CAREKV_KIND_K;
   const bool kind_v = rp.kind == CAREKV_KIND_BOTH || rp.kind == CAREKV_KIND_V;
@@ -289,7 +295,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       // every load of the page is issued before any result is used (the
       // workspace rows exist for every page, so no load waits on a check)
       const int nv = live ? a.cache.valid[pg] : 0;
-      const float vc = live ? (a.v_pnorm ? a.v_pnorm[h * a.p_used + p] : sqrtf(a.cache.v_norm2[pg])) : 0.f;
+      const float vc = live ? (v_pnorm ? v_pnorm[h * a.p_used + p] : sqrtf(a.cache.v_norm2[pg])) : 0.f;
       // the page's 4 V block errors in one load (NV == 4), so the error of a
       // kept block does not wait for the block index
       uint2 ve4 = make_uint2(0u, 0u);
@@ -309,7 +315,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         const float mlb = sm.mlb[i];
 #pragma unroll
         for (int j = 0; j < 16; ++j)
-          A[j] = pos_tok(j, a.s_perm) < nv ? (a.attn ? sv[j] : rex2(fmaf(sv[j], kRL2e, -mlb))) : 0.f;
+          A[j] = pos_tok(j, a.s_perm) < nv ? (A_in ? sv[j] : rex2(fmaf(sv[j], kRL2e, -mlb))) : 0.f;
         // attention mass of each 4-token V block (positions in ascending order)
         float bm[4] = {0.f, 0.f, 0.f, 0.f};
         if (d.vtb == 4) {
@@ -407,7 +413,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       const uint32_t w0 = *reinterpret_cast<const uint32_t*>(pay + gid * 16 + 4 * tig);
       const uint32_t w1 = *reinterpret_cast<const uint32_t*>(pay + (gid + 8) * 16 + 4 * tig);
       const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
-      const float vc = a.v_pnorm ? a.v_pnorm[h * a.p_used + p] : sqrtf(a.cache.v_norm2[pg]);
+      const float vc = v_pnorm ? v_pnorm[h * a.p_used + p] : sqrtf(a.cache.v_norm2[pg]);
       float s4[4] = {0.f, 0.f, 0.f, 0.f};
       if (gid < QN) {
         const float* srow = Wb + gid * sst + p * kPage;
@@ -476,9 +482,9 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
 #pragma unroll
       for (int i = 0; i < QN; ++i) {
         sv[i] = t < nv && a.S ? Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] : 0.f;
-        wv[i] = t < nv ? (a.attn ? Wb[i * sst + p * kPage + tok_pos(t, a.s_perm)] : attw(sv[i], i)) : 0.f;
+        wv[i] = t < nv ? (A_in ? Wb[i * sst + p * kPage + tok_pos(t, a.s_perm)] : attw(sv[i], i)) : 0.f;
       }
-      const float vn2 = a.v_pnorm ? a.v_pnorm[h * a.p_used + p] * a.v_pnorm[h * a.p_used + p] : a.cache.v_norm2[pg];
+      const float vn2 = v_pnorm ? v_pnorm[h * a.p_used + p] * v_pnorm[h * a.p_used + p] : a.cache.v_norm2[pg];
       const uint32_t wds[4] = {raw.x, raw.y, raw.z, raw.w};
       float r[32];
 #pragma unroll
@@ -521,8 +527,8 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
             float acc = 0.f;
             for (int c = 0; c < D; ++c) {
               float vh;
-              if (a.v_rows) {
-                vh = a.v_rows[((static_cast<int64_t>(h) * a.p_used + p) * kPage + t) * D + c];
+              if (v_rows) {
+                vh = v_rows[((static_cast<int64_t>(h) * a.p_used + p) * kPage + t) * D + c];
               } else {
                 const float svv = read_scale(a.cache.v_scale, (pg * kPage + t) * d.G + c / d.gsize, d.scale_mode, mv);
                 vh = f16r(__fmul_rn(static_cast<float>(unpack_code(a.cache.v_codes + (pg * kPage + t) * d.R, c, d.bits)), svv));
@@ -800,7 +806,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   const int v_item_b = d.vslot_bytes + kPage * 4;
   const bool bulk = ((reinterpret_cast<uintptr_t>(a.cache.v_codes) | reinterpret_cast<uintptr_t>(a.cache.v_scale) |
                       reinterpret_cast<uintptr_t>(a.cache.v_slot_data) | reinterpret_cast<uintptr_t>(Wb)) & 15) == 0 &&
-                    k_codes_b % 16 == 0 && k_sc_b % 16 == 0 && d.vslot_bytes % 16 == 0 && a.v_rows == nullptr;
+                    k_codes_b % 16 == 0 && k_sc_b % 16 == 0 && d.vslot_bytes % 16 == 0 && v_rows == nullptr;
   if (tid == 0) {
     mbar_init(&sm.stg_bar, 1);
     fence_mbar_init();
@@ -966,7 +972,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           const int u = item, p = sm.kp_page[u];
           const int64_t pg = lhp * d.P + p;
           const int nv = sm.kp_nv[u];
-          const float* vrow = a.v_rows ? a.v_rows + (static_cast<int64_t>(h) * a.p_used + p) * kPage * D : nullptr;
+          const float* vrow = v_rows ? v_rows + (static_cast<int64_t>(h) * a.p_used + p) * kPage * D : nullptr;
           if (!bulk) {
             for (int w = lane; w < (vrow ? 0 : k_codes_b / 4); w += 32)
               reinterpret_cast<uint32_t*>(stg)[w] = reinterpret_cast<const uint32_t*>(a.cache.v_codes + pg * k_codes_b)[w];
@@ -1093,8 +1099,8 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       // exact form: a_new @ V = (cbase * sum_t A V + num) / (cbase * sum_t A + z); sum_t A V and
       // sum_t A are O and 1 in decode, given by the caller in the prefill correction
       const int64_t row = static_cast<int64_t>(bh) * QN + i;
-      const float oe = a.o_exact ? a.o_exact[row * D + tid] : ob;
-      const float as = (a.n_splits == 0 && a.pl) ? a.pl[row] : 1.f;
+      const float oe = o_exact ? o_exact[row * D + tid] : ob;
+      const float as = (po_direct && a.pl) ? a.pl[row] : 1.f;
       const float delta = exact ? (__fdiv_rn(fmaf(cbase, oe, n), fmaf(cbase, as, z)) - ob) : (n - z * ob);
       store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + tid, ob + delta, a.dt);
     }
