@@ -135,6 +135,7 @@ int carekv_cache_init(const carekv_config_t* cfg, const carekv_cache_t* cache, v
   const bool minus_one[CAREKV_NUM_BUFFERS] = {false, false, false, false, false, false, false, false,
                                               false, true,  false, false, true,  true,  false, false,
                                               true,  false, false, false, false, false, false};
+  prepare_decode_streams();
   cudaStream_t st = as_stream(stream);
   for (int i = 0; i < CAREKV_NUM_BUFFERS; ++i) {
     if (ptrs[i] == nullptr || sz[i] == 0) continue;

@@ -19,6 +19,9 @@
 #include "internal.h"
 #include "decode_args.h"
 #include "ptx.cuh"
+#include <algorithm>
+#include <cstdlib>
+#include <mutex>
 
 namespace carekv {
 
@@ -175,8 +178,18 @@ inline Pass choose_pass(const carekv_config_t& c) {
 }
 inline int pass_slots(Pass p) { return p == Pass::NARROW ? 4 * 148 : 2 * 148; }
 
+namespace {
+int attend_chunks();
+}
+// Sequences per chunk of a decode attention call (see decode_attention).
+inline int chunk_size(int seq_count) {
+  const int chunks = std::max(1, std::min(attend_chunks(), seq_count));
+  return (seq_count + chunks - 1) / chunks;
+}
+
 // Workspace regions, each 256-byte aligned: selection readback, scores,
 // logits, split partials m / l / O, and (narrow pass) q . R_K per K slot.
+// The split plan is the one of a chunk (chunk_size sequences).
 struct WsLayout {
   int64_t sel, scores, S, pm, pl, po, kw, total;
 };
@@ -184,7 +197,7 @@ inline WsLayout ws_layout(const carekv_config_t& c, int seq_count, int p_used) {
   const int64_t qn = c.num_heads / c.num_kv_heads;
   const int64_t n_bh = static_cast<int64_t>(seq_count) * c.num_kv_heads;
   const Pass pass = choose_pass(c);
-  const SplitPlan sp = split_plan(static_cast<int>(n_bh), p_used, pass_slots(pass));
+  const SplitPlan sp = split_plan(chunk_size(seq_count) * c.num_kv_heads, p_used, pass_slots(pass));
   WsLayout w;
   int64_t o = 0;
   w.sel = o;    o = align256(o + n_bh * qn * (kMaxSel + 1) * 4);
@@ -234,6 +247,63 @@ static cudaError_t launch_qn(DecodeArgs& a, cudaStream_t st, int n_bh) {
   return launch_route<QN>(a, st, n_bh);
 }
 
+// Batch chunking of decode attention.  The split-K pass is issue-bound and
+// the router latency-bound, so the batch is cut into `chunks` ranges of
+// sequences that run on separate streams: chunk c (c < chunks - 1) on an
+// internal stream of higher priority than chunk c + 1, the last chunk on
+// the caller's stream.  Routing a chunk then overlaps the split-K pass of the
+// later chunks, whose CTAs fill the SMs the router leaves idle.  Every chunk
+// uses the split plan of one chunk and its slice of the one workspace layout
+// (all regions are indexed by (sequence, kv head)), so the workspace size
+// and the selection readback do not depend on the chunking.
+// Fork and join go through events, which stream capture records as graph
+// edges.  CAREKV_ATTEND_CHUNKS (1, 2 or 4; default 2) sets the count.
+namespace {
+constexpr int kMaxDev = 64, kMaxChunks = 4;
+struct ChunkStreams {
+  bool ready = false;
+  cudaStream_t st[kMaxChunks - 1] = {};
+  cudaEvent_t fork = nullptr, join[kMaxChunks - 1] = {};
+};
+ChunkStreams g_chunk[kMaxDev];
+std::mutex g_chunk_mu;
+
+int attend_chunks() {
+  static const int n = [] {
+    const char* e = std::getenv("CAREKV_ATTEND_CHUNKS");
+    const int v = e ? std::atoi(e) : 2;
+    return v == 1 || v == 2 || v == 4 ? v : 2;
+  }();
+  return n;
+}
+
+// Streams and events of the current device, created on first use outside
+// stream capture; null while they do not exist (the caller then runs
+// unchunked).
+ChunkStreams* chunk_streams(cudaStream_t caller) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
+  std::lock_guard<std::mutex> lock(g_chunk_mu);
+  ChunkStreams& cs = g_chunk[dev];
+  if (cs.ready) return &cs;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(caller, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return nullptr;
+  int least = 0, greatest = 0;
+  if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) return nullptr;
+  for (int i = 0; i < kMaxChunks - 1; ++i) {
+    // chunk 0 gets the greatest priority, later chunks step down towards the caller's
+    const int prio = std::min(least, greatest + i);
+    if (cudaStreamCreateWithPriority(&cs.st[i], cudaStreamNonBlocking, prio) != cudaSuccess) return nullptr;
+    if (cudaEventCreateWithFlags(&cs.join[i], cudaEventDisableTiming) != cudaSuccess) return nullptr;
+  }
+  if (cudaEventCreateWithFlags(&cs.fork, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+  cs.ready = true;
+  return &cs;
+}
+}  // namespace
+
+void prepare_decode_streams() { (void)chunk_streams(nullptr); }
+
 int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* q,
                      void* out, int dtype, int seq_begin, int seq_count, int p_used,
                      const carekv_route_params_t& rp, void* ws, size_t ws_bytes, const float* sketch_proj,
@@ -248,8 +318,8 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
   a.dt = dtype;
   a.seq_begin = seq_begin;
   a.qn = cfg.num_heads / cfg.num_kv_heads;
-  const int n_bh = seq_count * cfg.num_kv_heads;
-  const SplitPlan sp = split_plan(n_bh, p_used, pass_slots(choose_pass(cfg)));
+  const int H = cfg.num_kv_heads;
+  const SplitPlan sp = split_plan(chunk_size(seq_count) * H, p_used, pass_slots(choose_pass(cfg)));
   a.pps = sp.pps;
   a.n_splits = sp.n_splits;
   a.p_used = p_used;
@@ -292,15 +362,51 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
   a.o_exact = nullptr;
   a.v_rows = nullptr;
   a.v_pnorm = nullptr;
-  cudaError_t e;
-  switch (a.qn) {
-    case 1: e = launch_qn<1>(a, st, n_bh); break;
-    case 2: e = launch_qn<2>(a, st, n_bh); break;
-    case 4: e = launch_qn<4>(a, st, n_bh); break;
-    case 8: e = launch_qn<8>(a, st, n_bh); break;
-    default: return CAREKV_ERR_UNSUPPORTED;
+  if (a.qn != 1 && a.qn != 2 && a.qn != 4 && a.qn != 8) return CAREKV_ERR_UNSUPPORTED;
+
+  const int per = chunk_size(seq_count);
+  int chunks = (seq_count + per - 1) / per;
+  ChunkStreams* cs = chunks > 1 ? chunk_streams(st) : nullptr;
+  // without the streams (first call under capture) the chunks run in order on
+  // the caller's stream: same plan, same workspace slices, no overlap
+
+  if (cs && cudaEventRecord(cs->fork, st) != cudaSuccess) return CAREKV_ERR_CUDA;
+  const int64_t qn = a.qn, D = cfg.head_dim, NGs = static_cast<int64_t>(p_used) * (cfg.k_slots_per_page + cfg.v_slots_per_page);
+  const int64_t es = dtype == CAREKV_F32 ? 4 : 2;
+  for (int c = 0; c < chunks; ++c) {
+    const int s0 = c * per, n = std::min(per, seq_count - s0);
+    const int64_t bh0 = static_cast<int64_t>(s0) * H;
+    DecodeArgs ac = a;
+    ac.seq_begin = seq_begin + s0;
+    ac.q = static_cast<const char*>(q) + bh0 * qn * D * es;
+    ac.out = static_cast<char*>(out) + bh0 * qn * D * es;
+    ac.sel_out = a.sel_out + bh0 * qn * (kMaxSel + 1);
+    ac.scores = a.scores + bh0 * qn * NGs;
+    ac.S = a.S + bh0 * qn * p_used * kPage;
+    ac.pm = a.pm + bh0 * a.n_splits * qn;
+    ac.pl = a.pl + bh0 * a.n_splits * qn;
+    ac.po = a.po + bh0 * a.n_splits * qn * D;
+    if (a.kw) ac.kw = a.kw + bh0 * qn * p_used * cfg.k_slots_per_page * kPage;
+    cudaStream_t sc = st;
+    if (cs && c < chunks - 1) {
+      sc = cs->st[c];
+      if (cudaStreamWaitEvent(sc, cs->fork, 0) != cudaSuccess) return CAREKV_ERR_CUDA;
+    }
+    cudaError_t e;
+    switch (a.qn) {
+      case 1: e = launch_qn<1>(ac, sc, n * H); break;
+      case 2: e = launch_qn<2>(ac, sc, n * H); break;
+      case 4: e = launch_qn<4>(ac, sc, n * H); break;
+      default: e = launch_qn<8>(ac, sc, n * H); break;
+    }
+    if (e != cudaSuccess) return CAREKV_ERR_CUDA;
+    if (cs && c < chunks - 1) {
+      if (cudaEventRecord(cs->join[c], sc) != cudaSuccess) return CAREKV_ERR_CUDA;
+    }
   }
-  return e == cudaSuccess ? CAREKV_OK : CAREKV_ERR_CUDA;
+  for (int c = 0; cs && c < chunks - 1; ++c)
+    if (cudaStreamWaitEvent(st, cs->join[c], 0) != cudaSuccess) return CAREKV_ERR_CUDA;
+  return CAREKV_OK;
 }
 
 // Stored-slot prefill correction (layer.py:458-637 with the vectorized
