@@ -265,22 +265,21 @@ def run_gpu(args, rank, world):
     att_ms = [a.elapsed_time(b_) for a, b_ in ev]
 
     # e2e through the public API: per step, pinned host inputs -> device,
-    # step, output -> pinned host
+    # step, output -> pinned host; DecodeStepGraph(host_io=...) keeps the
+    # transfers in the step graph, layer l's copies overlapping other layers
     hq = torch.empty_like(q, device="cpu").pin_memory()
     hk = torch.empty_like(k, device="cpu").pin_memory()
     hv = torch.empty_like(v, device="cpu").pin_memory()
     ho = torch.empty_like(out, device="cpu").pin_memory()
     hq.copy_(q.cpu()); hk.copy_(k.cpu()); hv.copy_(v.cpu())
+    step_io = pkg.engine.DecodeStepGraph(eng, q, k, v, out, pages_bound, host_io=(hq, hk, hv, ho))
+    step_io.replay()   # first replay uploads the graph
     torch.cuda.synchronize()
     barrier()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
     for _ in range(args.e2e_steps):
-        q.copy_(hq, non_blocking=True)
-        k.copy_(hk, non_blocking=True)
-        v.copy_(hv, non_blocking=True)
-        step.replay()
-        ho.copy_(out, non_blocking=True)
+        step_io.replay()
     f1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = f0.elapsed_time(f1)
@@ -290,7 +289,7 @@ def run_gpu(args, rank, world):
                clocks=parse_clocks(clk_path, dev.index) if rank == 0 else None,
                out_finite=bool(torch.isfinite(out.float()).all().item()),
                h2d=int(hq.numel() * 2 + hk.numel() * 2 + hv.numel() * 2), d2h=int(ho.numel() * 2))
-    del step
+    del step, step_io
     return res
 
 

@@ -83,6 +83,7 @@ SIGNATURES = [
     ("carekv_decode_attention", i32, [ctypes.POINTER(Config), ctypes.POINTER(Cache), i32, vp, vp, i32, i32, i32,
                                       i32, ctypes.POINTER(RouteParams), vp, vp, ctypes.c_size_t, vp]),
     ("carekv_check_device_errors", i32, [ctypes.POINTER(Cache), ctypes.POINTER(i32), vp]),
+    ("carekv_decode_attention_launches", i32, [ctypes.POINTER(Config), i32, ctypes.POINTER(i32)]),
     ("carekv_prefill_workspace_bytes", i32, [ctypes.POINTER(Config), i32, i32, ctypes.POINTER(ctypes.c_size_t)]),
     ("carekv_prefill_correction", i32, [ctypes.POINTER(Config), ctypes.POINTER(Cache), i32, i32, i32, i32, vp, vp,
                                         vp, vp, vp, vp, vp, vp, vp, vp, i32, ctypes.POINTER(RouteParams), vp, vp,

@@ -322,6 +322,13 @@ int carekv_prefill_correction(const carekv_config_t* cfg, const carekv_cache_t* 
                             workspace_bytes_, as_stream(stream));
 }
 
+int carekv_decode_attention_launches(const carekv_config_t* cfg, int32_t seq_count, int32_t* launches) {
+  CHECK(validate_config(cfg));
+  if (!launches || seq_count < 0) return CAREKV_ERR_INVALID_ARG;
+  *launches = 2 * decode_attention_chunks(seq_count);
+  return CAREKV_OK;
+}
+
 int carekv_check_device_errors(const carekv_cache_t* cache, int32_t* flags_out, void* stream) {
   if (!cache || !cache->error_flag) return CAREKV_ERR_INVALID_ARG;
   int32_t h = 0;

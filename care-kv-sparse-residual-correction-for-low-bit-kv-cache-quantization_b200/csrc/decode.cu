@@ -304,6 +304,12 @@ ChunkStreams* chunk_streams(cudaStream_t caller) {
 
 void prepare_decode_streams() { (void)chunk_streams(nullptr); }
 
+int decode_attention_chunks(int seq_count) {
+  if (seq_count <= 0) return 0;
+  const int per = chunk_size(seq_count);
+  return (seq_count + per - 1) / per;
+}
+
 int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* q,
                      void* out, int dtype, int seq_begin, int seq_count, int p_used,
                      const carekv_route_params_t& rp, void* ws, size_t ws_bytes, const float* sketch_proj,

@@ -26,7 +26,8 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
                      const carekv_route_params_t& rp, void* ws, size_t ws_bytes, const float* sketch_proj,
                      cudaStream_t st);
 size_t workspace_bytes(const carekv_config_t& c, int seq_count, int p_used);
-void prepare_decode_streams();   // creates the chunk streams of the current device (not under capture)
+void prepare_decode_streams();
+int decode_attention_chunks(int seq_count);   // batch chunks one decode attention call runs   // creates the chunk streams of the current device (not under capture)
 size_t prefill_workspace_bytes(const carekv_config_t& c, int n_pos, int p_used);
 int prefill_correction(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, int seq, int n_pos,
                        int p_used, const void* q, const float* logits, const float* row_max, const float* A,

@@ -271,9 +271,16 @@ class DecodeStepGraph:
     steps where the host page mirror says a page completes.  Step inputs
     live in fixed device buffers (q [L,B,Hq,D], k/v [L,B,Hkv,D]) and outputs
     land in out [L,B,Hq,D].
+
+    host_io = (hq, hk, hv, ho), pinned host tensors shaped like q, k, v,
+    out, puts the host transfers in the graph: layer l's inputs are copied in
+    on a copy stream while earlier layers compute, and its output is copied
+    back on a third stream as soon as the layer is done, so only the first
+    layer's inputs and the last layer's output are exposed.
     """
 
-    def __init__(self, engine: DecodeEngine, q, k, v, out, max_pages: int, correction: bool = True):
+    def __init__(self, engine: DecodeEngine, q, k, v, out, max_pages: int, correction: bool = True,
+                 host_io=None):
         self.engine = engine
         self.cache = engine.cache
         self.cfg = engine.cfg
@@ -294,21 +301,50 @@ class DecodeStepGraph:
         nbytes = engine.workspace_bytes(self.B, max_pages)
         self.ws = engine.workspace(nbytes)
         self.sketch = engine._sketch_ptr()
+        self.host_io = host_io
+        if host_io is not None:
+            for h, d_ in zip(host_io, (q, k, v, out)):
+                if h.device.type != "cpu" or not h.is_pinned() or h.shape != d_.shape or h.dtype != d_.dtype:
+                    raise ValueError("host_io: pinned host tensors shaped like q, k, v, out")
+        n = ctypes.c_int32(0)
+        _lib.check(lib.carekv_decode_attention_launches(ctypes.byref(cache.ccfg), self.B, ctypes.byref(n)),
+                   "carekv_decode_attention_launches")
+        attend_launches = int(n.value)
         self.graphs = {}
         self.launches = {}
         stream = torch.cuda.Stream(cache.device)
         for fill in (0, 1):
-            # warm the launch path once outside capture (lazy module loading)
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
-                self._issue(fill, torch.cuda.current_stream(cache.device).cuda_stream)
+                self._issue(fill, torch.cuda.current_stream(cache.device))
             self.graphs[fill] = g
-            self.launches[fill] = self.L * ((3 if fill else 1) + 2)
+            self.launches[fill] = self.L * ((3 if fill else 1) + attend_launches)
 
-    def _issue(self, fill, st):
+    def _issue(self, fill, stream):
         lib = _lib.lib()
         cache = self.cache
+        st = stream.cuda_stream
+        io = self.host_io
+        if io is not None:
+            hq, hk, hv, ho = io
+            dev = cache.device
+            copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+            fork = torch.cuda.Event()
+            fork.record(stream)
+            copy_in.wait_event(fork)
+            copy_out.wait_event(fork)
+            ready = []
+            with torch.cuda.stream(copy_in):
+                for l in range(self.L):
+                    self.q[l].copy_(hq[l], non_blocking=True)
+                    self.k[l].copy_(hk[l], non_blocking=True)
+                    self.v[l].copy_(hv[l], non_blocking=True)
+                    e = torch.cuda.Event()
+                    e.record(copy_in)
+                    ready.append(e)
         for l in range(self.L):
+            if io is not None:
+                stream.wait_event(ready[l])
             _lib.check(lib.carekv_append(ctypes.byref(cache.ccfg), ctypes.byref(cache.c), l, self.k[l].data_ptr(),
                                          self.v[l].data_ptr(), 0, self.B, ctypes.byref(self.store_params[l]),
                                          self.sketch, fill, st), "carekv_append")
@@ -316,6 +352,17 @@ class DecodeStepGraph:
                 ctypes.byref(cache.ccfg), ctypes.byref(cache.c), l, self.q[l].data_ptr(), self.out[l].data_ptr(),
                 _DT[self.q.dtype], 0, self.B, self.max_pages, ctypes.byref(self.route_params[l]), self.sketch,
                 self.ws.data_ptr(), self.ws.numel(), st), "carekv_decode_attention")
+            if io is not None:
+                done = torch.cuda.Event()
+                done.record(stream)
+                copy_out.wait_event(done)
+                with torch.cuda.stream(copy_out):
+                    ho[l].copy_(self.out[l], non_blocking=True)
+        if io is not None:
+            for s_ in (copy_in, copy_out):
+                j = torch.cuda.Event()
+                j.record(s_)
+                stream.wait_event(j)
 
     def next_fill(self) -> int:
         T = self.cfg.page_size

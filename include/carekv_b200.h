@@ -228,6 +228,14 @@ int carekv_decode_attention(const carekv_config_t *cfg, const carekv_cache_t *ca
                             const carekv_route_params_t *params, const float *sketch_proj,
                             void *workspace, size_t workspace_bytes, void *stream);
 
+/* Kernel launches one carekv_decode_attention call over `seq_count`
+ * sequences issues: a split-K pass and a route kernel per batch chunk.  The
+ * batch runs in CAREKV_ATTEND_CHUNKS (environment, 1 / 2 / 4, default 2)
+ * chunks on prioritised streams forked from the caller's stream and joined
+ * back into it (events, so stream capture records them), routing of one
+ * chunk overlapping the split-K pass of the next. */
+int carekv_decode_attention_launches(const carekv_config_t *cfg, int32_t seq_count, int32_t *launches);
+
 /* Decode attention for callers that cannot allocate device memory.
  *
  * No counterpart in the reference.  Same inputs, output and result as
