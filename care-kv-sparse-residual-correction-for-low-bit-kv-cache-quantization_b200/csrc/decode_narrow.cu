@@ -90,12 +90,11 @@ struct Keys {
   uint32_t k0, k3, k6, n0, n4, p10, p43, p76, p22, p11, p44, p77, p55;
 };
 // exact half2 (code_lo, code_hi) * sig2 of two 3-bit fields at mantissa bit S
-// (SC = false: the exact codes, unscaled)
-template <int S, bool SC = true>
+template <int S>
 __device__ __forceinline__ uint32_t i3p(uint32_t t, uint32_t key, uint32_t sig2) {
   uint32_t x;  // (t & mask) ^ key in one LOP3
   asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(x) : "r"(t), "n"(i3_mask2(S, S)), "r"(key));
-  return SC ? h2mul(h2sub(x, key), sig2) : h2sub(x, key);
+  return h2mul(h2sub(x, key), sig2);
 }
 
 // exact half2 (code_lo, code_hi) * sig2 of a 3-bit field at mantissa bit SL
@@ -169,13 +168,13 @@ __device__ __forceinline__ VSrc v_src(uint32_t Wa, uint32_t Wb) {
   v.r[2] = prmt(Wa, Wb, 0x7632);
   return v;
 }
-template <int F, bool SC = true>
+template <int F>
 __device__ __forceinline__ uint32_t v_field(const VSrc& v, const Keys& K, uint32_t sig2) {
   // r[0]: f0..f2 at bits 0, 3, 6; r[1]: f3..f5 at 1, 4, 7; r[2]: f6, f7 at 2, 5
   constexpr int S = F < 3 ? 3 * F : (F < 6 ? 3 * (F - 3) + 1 : 3 * (F - 6) + 2);
   const uint32_t key = S == 0 ? K.k0 : S == 3 ? K.k3 : S == 6 ? K.k6 : S == 1 ? K.p11 : S == 4 ? K.p44 : S == 7 ? K.p77
                      : S == 2 ? K.p22 : K.p55;
-  return i3p<S, SC>(v.r[F < 3 ? 0 : (F < 6 ? 1 : 2)], key, sig2);
+  return i3p<S>(v.r[F < 3 ? 0 : (F < 6 ? 1 : 2)], key, sig2);
 }
 
 // 4-bit residual word (nibbles n0..n7) -> exact half2 codes (n0,n4) (n1,n5)
@@ -189,11 +188,11 @@ __device__ __forceinline__ void nib_quads(uint32_t u, const Keys& K, uint32_t (&
 }
 
 // exact half2 (code_lo, code_hi) * sig2 of two 4-bit fields at mantissa bit S (0 or 4)
-template <int S, bool SC = true>
+template <int S>
 __device__ __forceinline__ uint32_t i4p(uint32_t t, uint32_t key, uint32_t sig2) {
   uint32_t x;
   asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(x) : "r"(t), "n"((15u << S) | (15u << (16 + S))), "r"(key));
-  return SC ? h2mul(h2sub(x, key), sig2) : h2sub(x, key);
+  return h2mul(h2sub(x, key), sig2);
 }
 // One packed INT4 K word (nibbles n0..n7, even channel low) -> half2 operands
 // (n0,n4) (n1,n5) (n2,n6) (n3,n7).
@@ -217,9 +216,9 @@ __device__ __forceinline__ VSrc4 v_src4(uint32_t Wa, uint32_t Wb) {
   v.r[3] = prmt(Wa, Wb, 0x7733);
   return v;
 }
-template <int F, bool SC = true>
+template <int F>
 __device__ __forceinline__ uint32_t v_field4(const VSrc4& v, const Keys& K, uint32_t sig2) {
-  return i4p<4 * (F & 1), SC>(v.r[F >> 1], (F & 1) ? K.n4 : K.n0, sig2);
+  return i4p<4 * (F & 1)>(v.r[F >> 1], (F & 1) ? K.n4 : K.n0, sig2);
 }
 
 template <int QN, int D, int BITS>
@@ -230,14 +229,6 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   constexpr int KW = D / 32;   // packed K words per thread and row
   constexpr int G4 = D / 32;   // 32-channel groups (K residual slots)
   static_assert(QN >= 1 && QN <= 4, "narrow pass: at most 4 queries per kv head");
-  // One query head per kv head: the V MMAs take the exact codes and put the
-  // V scales into P^T instead, column n = (scale group n/2, hi / lo half
-  // n%2) of p * scale, so the 32 HMUL2 of a page's V codes drop out; row
-  // group g's output sits in columns 2g, 2g+1 (thread tig = g).  The K
-  // MMAs then repeat the query in every column pair, so every lane holds the
-  // logits and runs the same online softmax as the lanes whose accumulators
-  // it rescales.
-  constexpr bool kVC = QN == 1;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bars[kWarps][kNS];
   __shared__ float sm_m[kWarps][4], sm_l[kWarps][4];
@@ -312,8 +303,8 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   // column n = query n/2, half n%2 (0 = hi, 1 = lo)
   const int qi = gid >> 1, part = gid & 1;
   auto qp = [&](int c) -> float {
-    if (!kVC && qi >= QN) return 0.f;
-    const float x = q_sm[kVC ? 0 : qi][c];
+    if (qi >= QN) return 0.f;
+    const float x = q_sm[qi][c];
     const float hi = __half2float(__float2half_rn(x));
     return part ? x - hi : hi;
   };
@@ -386,13 +377,11 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   const uint32_t vsel_h = (0x3210 + 0x1111 * (voff + 3)) & 0x7777;
   const int gk = (tig * (D / 4)) / d.gsize;              // K scale group of the thread's channels
   const int gv = ((D == 128 ? 16 : 8) * gid) / d.gsize;  // V scale group
-  const int gcol = gid >> 1;                                // scale group of P^T column gid (kVC)
-  const int gsel = kVC ? min(gcol, G - 1) : gv;            // scale group whose codes the thread reads
   const int ra = 2 * tig;                                 // V rows ra, ra+1, ra+8, ra+9
   const int src_a = 8 * tig + qi, src_b = src_a + 4;
   const int ko0 = gid * R + (D / 4) * BITS / 8 * tig, ko8 = ko0 + 8 * R;   // thread's K channel block
   const int kso0 = gid * G + gk, kso8 = (gid + 8) * G + gk;
-  const int vso0 = ra * G + gsel, vso1 = (ra + 1) * G + gsel, vso2 = (ra + 8) * G + gsel, vso3 = (ra + 9) * G + gsel;
+  const int vso0 = ra * G + gv, vso1 = (ra + 1) * G + gv, vso2 = (ra + 8) * G + gv, vso3 = (ra + 9) * G + gv;
 
   // logits of one staged page for rows gid, gid+8
   auto k_side = [&](const uint8_t* st, int pp, uint32_t km2, float& s0, float& s1) {
@@ -472,14 +461,11 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   };
 
   // O^T += V_hat^T . P^T for one staged page
-  // V scales of rows ra, ra+1 (sA) and ra+8, ra+9 (sB) of a staged page, group gsel
-  auto v_scales = [&](const uint8_t* st, int pp, uint32_t vm2, uint32_t& sA, uint32_t& sB) {
-    const uint8_t* vs = st + g.vsOff + pp * kPage * G;
-    sA = i8_scale_pair(static_cast<uint32_t>(vs[vso0]) | (static_cast<uint32_t>(vs[vso1]) << 16), vm2);
-    sB = i8_scale_pair(static_cast<uint32_t>(vs[vso2]) | (static_cast<uint32_t>(vs[vso3]) << 16), vm2);
-  };
-  auto v_side = [&](const uint8_t* st, int pp, uint32_t sA, uint32_t sB, uint32_t pb0, uint32_t pb1) {
+  auto v_side = [&](const uint8_t* st, int pp, uint32_t vm2, uint32_t pb0, uint32_t pb1) {
     const uint8_t* vc = st + g.vOff + pp * kPage * R;
+    const uint8_t* vs = st + g.vsOff + pp * kPage * G;
+    const uint32_t sA = i8_scale_pair(static_cast<uint32_t>(vs[vso0]) | (static_cast<uint32_t>(vs[vso1]) << 16), vm2);
+    const uint32_t sB = i8_scale_pair(static_cast<uint32_t>(vs[vso2]) | (static_cast<uint32_t>(vs[vso3]) << 16), vm2);
     if constexpr (BITS == 4) {
       if constexpr (D == 128) {
         uint32_t wl[4], wh[4];
@@ -492,7 +478,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
         const VSrc4 x0 = v_src4(wl[0], wl[1]), x1 = v_src4(wh[0], wh[1]);
         const VSrc4 x2 = v_src4(wl[2], wl[3]), x3 = v_src4(wh[2], wh[3]);
 #define CK_VF(F) \
-  mma_f16(o[F], v_field4<F, !kVC>(x0, KY, sA), v_field4<F, !kVC>(x1, KY, sA), v_field4<F, !kVC>(x2, KY, sB), v_field4<F, !kVC>(x3, KY, sB), pb0, pb1);
+  mma_f16(o[F], v_field4<F>(x0, KY, sA), v_field4<F>(x1, KY, sA), v_field4<F>(x2, KY, sB), v_field4<F>(x3, KY, sB), pb0, pb1);
         CK_VF(0) CK_VF(1) CK_VF(2) CK_VF(3) CK_VF(4) CK_VF(5) CK_VF(6) CK_VF(7)
 #undef CK_VF
       } else {
@@ -501,7 +487,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
         for (int r = 0; r < 4; ++r) wv[r] = lds32(vc + (ra + (r & 1) + 8 * (r >> 1)) * R + vo);
         const VSrc4 x0 = v_src4(wv[0], wv[1]), x1 = v_src4(wv[2], wv[3]);
 #define CK_VF(F)                                                                                                   \
-  mma_f16(o[F], v_field4<F, !kVC>(x0, KY, sA), v_field4<F + 4, !kVC>(x0, KY, sA), v_field4<F, !kVC>(x1, KY, sB), v_field4<F + 4, !kVC>(x1, KY, sB), \
+  mma_f16(o[F], v_field4<F>(x0, KY, sA), v_field4<F + 4>(x0, KY, sA), v_field4<F>(x1, KY, sB), v_field4<F + 4>(x1, KY, sB), \
           pb0, pb1);
         CK_VF(0) CK_VF(1) CK_VF(2) CK_VF(3)
 #undef CK_VF
@@ -518,7 +504,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
       const VSrc x0 = v_src(wl[0], wl[1]), x1 = v_src(wh[0], wh[1]);
       const VSrc x2 = v_src(wl[2], wl[3]), x3 = v_src(wh[2], wh[3]);
 #define CK_VF(F) \
-  mma_f16(o[F], v_field<F, !kVC>(x0, KY, sA), v_field<F, !kVC>(x1, KY, sA), v_field<F, !kVC>(x2, KY, sB), v_field<F, !kVC>(x3, KY, sB), pb0, pb1);
+  mma_f16(o[F], v_field<F>(x0, KY, sA), v_field<F>(x1, KY, sA), v_field<F>(x2, KY, sB), v_field<F>(x3, KY, sB), pb0, pb1);
       CK_VF(0) CK_VF(1) CK_VF(2) CK_VF(3) CK_VF(4) CK_VF(5) CK_VF(6) CK_VF(7)
 #undef CK_VF
     } else {
@@ -527,7 +513,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
       for (int r = 0; r < 4; ++r) wv[r] = word24_at(vc + (ra + (r & 1) + 8 * (r >> 1)) * R, vo);
       const VSrc x0 = v_src(wv[0], wv[1]), x1 = v_src(wv[2], wv[3]);
 #define CK_VF(F)                                                                                           \
-  mma_f16(o[F], v_field<F, !kVC>(x0, KY, sA), v_field<F + 4, !kVC>(x0, KY, sA), v_field<F, !kVC>(x1, KY, sB), v_field<F + 4, !kVC>(x1, KY, sB), \
+  mma_f16(o[F], v_field<F>(x0, KY, sA), v_field<F + 4>(x0, KY, sA), v_field<F>(x1, KY, sB), v_field<F + 4>(x1, KY, sB), \
           pb0, pb1);
       CK_VF(0) CK_VF(1) CK_VF(2) CK_VF(3)
 #undef CK_VF
@@ -546,26 +532,6 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
     const uint32_t sel = part ? 0x7632u : 0x5410u;
     pb0 = prmt(xa, xb, sel);
     pb1 = prmt(ya, yb, sel);
-  };
-
-  // kVC: P^T scaled per column group -- tokens 2tig, 2tig+1 | 2tig+8, 2tig+9
-  // of the query from the lanes that computed them (tig 0), times the V
-  // scale of group gcol, split into fp16 hi / lo by the column's half
-  auto p_operands_vc = [&](float pr0, float pr1, uint32_t sA, uint32_t sB, uint32_t& pb0, uint32_t& pb1) {
-    const float a0 = __shfl_sync(0xffffffffu, pr0, 8 * tig), a8 = __shfl_sync(0xffffffffu, pr1, 8 * tig);
-    const float b0 = __shfl_sync(0xffffffffu, pr0, 8 * tig + 4), b8 = __shfl_sync(0xffffffffu, pr1, 8 * tig + 4);
-    const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&sA));
-    const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&sB));
-    const float w0 = a0 * fa.x, w1 = b0 * fa.y, w8 = a8 * fb.x, w9 = b8 * fb.y;
-    uint32_t h01 = pack_h2(w0, w1), h89 = pack_h2(w8, w9);
-    if (part) {
-      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&h01));
-      const float2 y = __half22float2(*reinterpret_cast<const __half2*>(&h89));
-      h01 = pack_h2(w0 - x.x, w1 - x.y);
-      h89 = pack_h2(w8 - y.x, w9 - y.y);
-    }
-    pb0 = gcol < G ? h01 : 0u;
-    pb1 = gcol < G ? h89 : 0u;
   };
 
   bool failed = false;
@@ -652,16 +618,12 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
       l_part += (p00 + p01) + (p10 + p11);
 
       // ── values ──
-      uint32_t pb0, pb1, sA, sB;
-      v_scales(st, 0, m_vm[mi], sA, sB);
-      if constexpr (kVC) p_operands_vc(p00, p01, sA, sB, pb0, pb1);
-      else p_operands(p00, p01, pb0, pb1);
-      v_side(st, 0, sA, sB, pb0, pb1);
+      uint32_t pb0, pb1;
+      p_operands(p00, p01, pb0, pb1);
+      v_side(st, 0, m_vm[mi], pb0, pb1);
       if constexpr (two) {
-        v_scales(st, 1, m_vm[mi + 1], sA, sB);
-        if constexpr (kVC) p_operands_vc(p10, p11, sA, sB, pb0, pb1);
-        else p_operands(p10, p11, pb0, pb1);
-        v_side(st, 1, sA, sB, pb0, pb1);
+        p_operands(p10, p11, pb0, pb1);
+        v_side(st, 1, m_vm[mi + 1], pb0, pb1);
       }
     };
     if (pbase + 1 < pb)
@@ -691,8 +653,8 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
     sm_m[warp][tig] = m_run;
     sm_l[warp][tig] = l_part;
   }
-  if (kVC ? tig == gv : q_ok) {   // kVC: row group gv's columns are those of thread tig = gv
-    float* dst = so + (warp * 4 + (kVC ? 0 : tig)) * D;
+  if (q_ok) {
+    float* dst = so + (warp * 4 + tig) * D;
 #pragma unroll
     for (int f = 0; f < KS; ++f) {
       const int c_lo = D == 128 ? 16 * gid + f : 8 * gid + f;
