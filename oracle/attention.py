@@ -174,7 +174,7 @@ def vectorized_joint_correction(cache, l, h, Q, S, A, V_base, O_base, rc: RouteC
     kidx = _k_slot_index(cache, l, h, rc)
     vidx = _v_slot_index(cache, l, h, rc)
     n_k, n_v = len(kidx), len(vidx)
-    info.update(n_k=n_k, n_v=n_v, k_index=kidx, v_index=vidx)
+    info.update(n_k=n_k, n_v=n_v, k_index=kidx, v_index=vidx, A=A)
     want_k = rc.kind in ("k", "both") and n_k > 0
     want_v = rc.kind in ("v", "both") and n_v > 0
     if not want_k and not want_v:

@@ -163,6 +163,20 @@ def compare_cache_state(gpu_cache, oc, b, layer, check_sketch=False, err_ulps=Tr
                     assert float(vscale[b, layer, h, p, j].float().item()) == float(sc), ("V slot scale", h, p)
 
 
+def saturated_attention(info, q, eps=1e-4):
+    """True when query q's attention is saturated in fp32 (1 - max A < eps).
+
+    combined_kvscore weighs every token by A(1 - A); for the dominant token of
+    such a query 1 - A sits at the rounding level of fp32 (one ulp of 1.0 is
+    6e-8), so the K score of its page is rounding noise in the reference as in
+    any other fp32 evaluation, and the selection among the slots it competes
+    with is not determined by the algorithm."""
+    A = info.get("A")
+    if A is None:
+        return False
+    return 1.0 - float(np.max(A[q])) < eps
+
+
 def selection_margin(info, q, qn_total=None):
     """Gap between the last selected and the first unselected normalised
     score of query q (joint list), for tie-aware selection checks."""

@@ -15,7 +15,7 @@ import torch
 import oracle
 from conftest import load_pkg
 from helpers import (PAPER_BEST_ENV, compare_cache_state, env, oracle_cache_for, oracle_selection,
-                     route_cfg_from, selection_margin)
+                     route_cfg_from, saturated_attention, selection_margin)
 
 pytestmark = pytest.mark.gpu
 
@@ -60,7 +60,8 @@ def _check_step(pkg, eng, oc, cfg, q_np, dt, seqs, layer=0, correction=True):
                 for i in range(grp):
                     got = sorted(sel[(b, h, i)])
                     if got != want[i]:
-                        assert selection_margin(info, i) < 1e-5, (b, h, i, got, want[i])
+                        m = selection_margin(info, i)
+                        assert m < 1e-5 or saturated_attention(info, i), (b, h, i, got, want[i], m)
 
 
 CASES = [

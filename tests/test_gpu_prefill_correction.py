@@ -16,7 +16,8 @@ import torch
 
 import oracle
 from conftest import load_pkg
-from helpers import PAPER_BEST_ENV, env, oracle_cache_for, oracle_selection, route_cfg_from, selection_margin
+from helpers import (PAPER_BEST_ENV, env, oracle_cache_for, oracle_selection, route_cfg_from, saturated_attention,
+                     selection_margin)
 
 pytestmark = pytest.mark.gpu
 
@@ -142,7 +143,9 @@ def test_prefill_correction_matches_oracle(pkg, case):
                 for t in range(T):
                     got_s = sorted(sel[(t, h, i)])
                     if got_s != ws[i * T + t]:
-                        assert selection_margin(info, i * T + t) < 1e-5, (h, i, t, got_s, ws[i * T + t])
+                        r = i * T + t
+                        assert selection_margin(info, r) < 1e-5 or saturated_attention(info, r), \
+                            (h, i, t, got_s, ws[r])
         cache.check_errors()
 
 
