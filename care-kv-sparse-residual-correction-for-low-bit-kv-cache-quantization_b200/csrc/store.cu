@@ -451,6 +451,13 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
   __shared__ float scs[2][4];
   __shared__ int sh_p, sh_off;
 
+  // the new rows first: their loads do not depend on the page state
+  const int64_t src = (static_cast<int64_t>(s) * d.H + h) * D;
+  for (int c = lane; c < D; c += 32) {
+    xs[0][c] = load_act(kin, src + c, dt);
+    xs[1][c] = load_act(vin, src + c, dt);
+  }
+  uint32_t masters = 0;   // lane 0: fp16 K | V master of the target page, read early
   if (lane == 0) {
     int np = cache.num_pages[lhp];
     int p = np - 1;
@@ -474,27 +481,62 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
     }
     sh_p = p;
     sh_off = p >= 0 ? cache.valid[lhp * d.P + p] : 0;
+    if (p >= 0 && cfg.scale_mode == CAREKV_SCALE_INT8)
+      masters = cache.k_master[lhp * d.P + p] | (static_cast<uint32_t>(cache.v_master[lhp * d.P + p]) << 16);
   }
   __syncwarp();
   const int p = sh_p;
   if (p < 0) return;
   const int off = sh_off;
   const int64_t pg = lhp * d.P + p;
-  const int64_t src = (static_cast<int64_t>(s) * d.H + h) * D;
-  for (int c = lane; c < D; c += 32) {
-    xs[0][c] = load_act(kin, src + c, dt);
-    xs[1][c] = load_act(vin, src + c, dt);
-  }
-  __syncwarp();
   const int qmax = (1 << (d.bits - 1)) - 1;
-  if (lane < 2 * d.G) {
-    const int kind = lane / d.G, g = lane % d.G;
-    float mx = 0.f;
-    for (int c = g * d.gsize; c < (g + 1) * d.gsize; ++c) mx = fmaxf(mx, fabsf(xs[kind][c]));
-    const float sc = group_scale(mx, qmax, dt);
-    scs[kind][g] = sc;
-    for (int c = g * d.gsize; c < (g + 1) * d.gsize; ++c) cs[kind][c] = quant_code(xs[kind][c], sc, qmax, dt);
+  // per-group max |x| of both rows: every lane folds its channels c = lane +
+  // 32 t into the (kind, group) maxima, then one butterfly per maximum
+  {
+    float mx[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int c = lane + 32 * t;
+      if (c < D) {
+        const int g = c / d.gsize;
+#pragma unroll
+        for (int gg = 0; gg < 4; ++gg) {
+          if (gg == g) {
+            mx[0][gg] = fmaxf(mx[0][gg], fabsf(xs[0][c]));
+            mx[1][gg] = fmaxf(mx[1][gg], fabsf(xs[1][c]));
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int gg = 0; gg < 4; ++gg) {
+        mx[0][gg] = fmaxf(mx[0][gg], __shfl_xor_sync(0xffffffffu, mx[0][gg], o));
+        mx[1][gg] = fmaxf(mx[1][gg], __shfl_xor_sync(0xffffffffu, mx[1][gg], o));
+      }
+    if (lane < 2 * d.G) {
+      const int kind = lane / d.G, g = lane % d.G;
+      float m = mx[0][0];
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk)
+#pragma unroll
+        for (int gg = 0; gg < 4; ++gg)
+          if (kk == kind && gg == g) m = mx[kk][gg];
+      scs[kind][g] = group_scale(m, qmax, dt);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int c = lane + 32 * t;
+      if (c < D) {
+        const int g = c / d.gsize;
+        cs[0][c] = quant_code(xs[0][c], scs[0][g], qmax, dt);
+        cs[1][c] = quant_code(xs[1][c], scs[1][g], qmax, dt);
+      }
+    }
   }
+  masters = __shfl_sync(0xffffffffu, masters, 0);
   __syncwarp();
   for (int j = lane; j < 2 * d.R; j += 32) {
     const int kind = j / d.R, jj = j % d.R;
@@ -506,8 +548,7 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
     void* dst = kind == 0 ? cache.k_scale : cache.v_scale;
     const int64_t idx = (pg * kPage + off) * d.G + g;
     if (d.scale_mode == CAREKV_SCALE_INT8) {
-      const uint16_t* mp = kind == 0 ? cache.k_master : cache.v_master;
-      const float m = f16_bits_to_f32(mp[pg]);
+      const float m = f16_bits_to_f32(static_cast<uint16_t>(kind == 0 ? masters : masters >> 16));
       const float mc = fmaxf(m, 1e-8f);  // master.clamp(min=1e-8) in fp32
       const int8_t c8 = int8_scale_code(scs[kind][g], mc);
       reinterpret_cast<int8_t*>(dst)[idx] = c8;
