@@ -274,11 +274,36 @@ def k_correction_mode() -> str:
     return m
 
 
+# Ablation knobs of vectorized_joint_correction (attention.py:698-810) that
+# change which slots are read or how their scores are formed; none is built
+# here, so a non-default value fails loudly instead of being ignored.
+# (CAREKV_CHUNKED_CORRECTION only bounds the reference's memory: per-query
+# results are unchanged, and this library needs no chunking of that kind.)
+_UNBUILT_ROUTE_KNOBS = (
+    ("CAREKV_ROUTER_PREFILTER_C", "0"), ("CAREKV_K_QDOTR_CLAMP_PCT", "0"), ("CAREKV_K_NORM_GUARD_PCT", "0"),
+    ("CAREKV_RESIDUAL_SCORE", "raw_error"), ("CAREKV_SELECTOR_VARIANT", "current"),
+    ("CAREKV_POSITION_POLICY", "none"),
+)
+
+
+def _check_unbuilt_route_knobs() -> None:
+    for name, default in _UNBUILT_ROUTE_KNOBS:
+        val = os.environ.get(name, default) or default
+        try:
+            same = float(val) == float(default)
+        except ValueError:
+            same = val.lower() == default
+        if not same:
+            raise NotImplementedError(f"{name}={val}: this router ablation (attention.py:698-810) is not built; "
+                                      f"unset it (default {default})")
+
+
 def resolve_route_params(cfg: CacheConfig, layer_id: int, kind: Optional[str] = None,
                          score_normalize: Optional[bool] = None,
                          k_corr_scale: Optional[float] = None) -> "_lib.RouteParams":
     """Budget resolution of residual_router.py:37-76 plus the env knobs of
     vectorized_joint_correction (attention.py:576-957)."""
+    _check_unbuilt_route_knobs()
     if kind is None:
         kind = os.environ.get("CAREKV_PREFILL_RESIDUAL_KIND", "both").lower()
     if kind not in {"v", "k", "both"}:

@@ -148,3 +148,17 @@ def test_layer_budget_multiplier_u_shape():
     cfg = _cfg(pkg, num_layers=5, budget_policy="u_shaped")
     m = [pkg.layer_budget_multiplier(cfg, l) for l in range(5)]
     assert abs(sum(m) / 5 - 1.0) < 1e-12 and m[0] == m[4] > m[2]
+
+
+@pytest.mark.parametrize("knob,value", [("CAREKV_ROUTER_PREFILTER_C", "8"), ("CAREKV_K_QDOTR_CLAMP_PCT", "99"),
+                                        ("CAREKV_K_NORM_GUARD_PCT", "95"),
+                                        ("CAREKV_RESIDUAL_SCORE", "attention_output"),
+                                        ("CAREKV_SELECTOR_VARIANT", "random"), ("CAREKV_POSITION_POLICY", "recent")])
+def test_unbuilt_router_ablations_fail_loudly(knob, value):
+    pkg = load_pkg()
+    cfg = pkg.CacheConfig(num_layers=1, num_heads=4, num_kv_heads=2, head_dim=64, max_pages=4)
+    with env(**{knob: value}):
+        with pytest.raises(NotImplementedError, match=knob):
+            pkg.resolve_route_params(cfg, 0)
+    with env(**{knob: None}):
+        pkg.resolve_route_params(cfg, 0)      # default: accepted
