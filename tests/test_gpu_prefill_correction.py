@@ -65,6 +65,7 @@ CASES = [
      "both"),
     ("gqa4_proxy_fp32", 64, 3, 32, 8, 2, "fp32", 48, (2, 2), "absolute", (2, 2), "joint", False, "exact", "both"),
     ("mha_int2_kind_v", 64, 2, 32, 2, 2, "fp32", 33, (1, 2), "absolute", (0, 2), "joint", True, "exact", "v"),
+    ("gqa8_int3_bf16_ratio", 128, 3, 32, 16, 2, "bf16", 45, (1, 2), "ratio", 0.05, "joint", True, "exact", "both"),
 ]
 
 
