@@ -221,7 +221,10 @@ __device__ __forceinline__ uint32_t v_field4(const VSrc4& v, const Keys& K, uint
   return i4p<4 * (F & 1)>(v.r[F >> 1], (F & 1) ? K.n4 : K.n0, sig2);
 }
 
-template <int QN, int D, int BITS>
+// GC, SKC: scale groups per row and K slots per page fixed at compile time
+// (every stage offset then folds into the instructions), or 0 = read from
+// the configuration.
+template <int QN, int D, int BITS, int GC, int SKC>
 __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   static_assert(BITS == 3 || BITS == 4, "narrow pass: INT3 or INT4 rows");
   constexpr int R = D * BITS / 8;
@@ -249,7 +252,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   const int pa = ca + warp * qv + min(warp, rv);
   const int pb = pa + qv + (warp < rv ? 1 : 0);
   const int Hq = d.H * QN;
-  const int G = d.G, SK = d.SK;
+  const int G = GC > 0 ? GC : d.G, SK = SKC > 0 ? SKC : d.SK;
   const bool kslot = a.kw != nullptr;
   const Geo g = geo(D, G, SK, kslot, BITS);
   const int64_t page0 = lhp * d.P;
@@ -375,8 +378,9 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   const int vbase = vo & ~3, voff = vo & 3;
   const uint32_t vsel_l = 0x3210 + 0x1111 * voff;
   const uint32_t vsel_h = (0x3210 + 0x1111 * (voff + 3)) & 0x7777;
-  const int gk = (tig * (D / 4)) / d.gsize;              // K scale group of the thread's channels
-  const int gv = ((D == 128 ? 16 : 8) * gid) / d.gsize;  // V scale group
+  const int gsz = GC > 0 ? D / GC : d.gsize;
+  const int gk = (tig * (D / 4)) / gsz;                  // K scale group of the thread's channels
+  const int gv = ((D == 128 ? 16 : 8) * gid) / gsz;      // V scale group
   const int ra = 2 * tig;                                 // V rows ra, ra+1, ra+8, ra+9
   const int src_a = 8 * tig + qi, src_b = src_a + 4;
   const int ko0 = gid * R + (D / 4) * BITS / 8 * tig, ko8 = ko0 + 8 * R;   // thread's K channel block
@@ -693,19 +697,29 @@ size_t narrow_smem_bytes(const carekv_config_t& c, bool kslot) {
   return static_cast<size_t>(narrow::geo(c.head_dim, G, c.k_slots_per_page, kslot, c.base_bits).total);
 }
 
-template <int QN, int D, int BITS>
-static cudaError_t launch_narrow_bits(DecodeArgs& a, cudaStream_t st, int n_bh) {
+template <int QN, int D, int BITS, int GC, int SKC>
+static cudaError_t launch_narrow_kernel(DecodeArgs& a, cudaStream_t st, int n_bh) {
   const int smem = static_cast<int>(narrow_smem_bytes(a.cfg, a.kw != nullptr));
   static int attr_bytes = 0;  // per process; the attribute is per function, not per device
   if (smem > attr_bytes) {
-    cudaError_t e = cudaFuncSetAttribute(narrow::decode_narrow<QN, D, BITS>,
+    cudaError_t e = cudaFuncSetAttribute(narrow::decode_narrow<QN, D, BITS, GC, SKC>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr_bytes = smem;
   }
-  a.s_perm = 1;
-  narrow::decode_narrow<QN, D, BITS><<<n_bh * a.n_splits, narrow::kWarps * 32, smem, st>>>(a);
+  narrow::decode_narrow<QN, D, BITS, GC, SKC><<<n_bh * a.n_splits, narrow::kWarps * 32, smem, st>>>(a);
   return cudaGetLastError();
+}
+
+// 32-channel scale groups with one K slot per page (the default store
+// budget at D = 128) take the compile-time layout; other layouts read G and
+// SK from the configuration.
+template <int QN, int D, int BITS>
+static cudaError_t launch_narrow_bits(DecodeArgs& a, cudaStream_t st, int n_bh) {
+  a.s_perm = 1;
+  if (a.cfg.group_size == 32 && a.cfg.k_slots_per_page == 1)
+    return launch_narrow_kernel<QN, D, BITS, D / 32, 1>(a, st, n_bh);
+  return launch_narrow_kernel<QN, D, BITS, 0, 0>(a, st, n_bh);
 }
 
 template <int QN, int D>
