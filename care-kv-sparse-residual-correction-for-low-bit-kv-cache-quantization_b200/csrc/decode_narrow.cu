@@ -711,14 +711,16 @@ static cudaError_t launch_narrow_kernel(DecodeArgs& a, cudaStream_t st, int n_bh
   return cudaGetLastError();
 }
 
-// 32-channel scale groups with one K slot per page (the default store
-// budget at D = 128) take the compile-time layout; other layouts read G and
-// SK from the configuration.
+// 32-channel scale groups with one or two K slots per page (store budgets
+// up to ~6 % at D = 128) take the compile-time layout; other layouts read G
+// and SK from the configuration.
 template <int QN, int D, int BITS>
 static cudaError_t launch_narrow_bits(DecodeArgs& a, cudaStream_t st, int n_bh) {
   a.s_perm = 1;
   if (a.cfg.group_size == 32 && a.cfg.k_slots_per_page == 1)
     return launch_narrow_kernel<QN, D, BITS, D / 32, 1>(a, st, n_bh);
+  if (a.cfg.group_size == 32 && a.cfg.k_slots_per_page == 2)
+    return launch_narrow_kernel<QN, D, BITS, D / 32, 2>(a, st, n_bh);
   return launch_narrow_kernel<QN, D, BITS, 0, 0>(a, st, n_bh);
 }
 
