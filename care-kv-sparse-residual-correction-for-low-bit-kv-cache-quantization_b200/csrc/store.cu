@@ -29,10 +29,28 @@ struct StoreSmem {
   float rscale[2][kPage][4];     // scales as read back (fp16 values)
   float err[8];
   float s4[8];                   // fp32 4-bit slot scale per candidate
-  uint8_t payload[8][256];
+  union {
+    __align__(16) uint8_t packed[2][kPage * 64];  // packed K / V rows before their store
+    __align__(16) uint8_t payload[8][256];        // 4-bit payload per candidate
+  };
   float red[2][32];
   float master[2];
+  int keep_k[8], keep_v[8];      // kept candidates in slot order
 };
+
+constexpr int kStoreThreads = 256;
+
+// 16-byte copy of n bytes (n a multiple of 16, both ends 16-byte aligned)
+// by the CTA's threads, else a byte loop.
+__device__ __forceinline__ void cta_copy(uint8_t* dst, const uint8_t* src, int n, bool vec) {
+  if (vec) {
+    for (int i = threadIdx.x; i < n / 16; i += blockDim.x)
+      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+  }
+}
+__device__ __forceinline__ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
 // Page store.  mode 0: rows come from K/V inputs (prefill).  mode 1: rows are
 // rebuilt from the cache's last page (decode page-full store, layer.py:1087-1146).
@@ -50,6 +68,10 @@ __global__ void __launch_bounds__(256) page_store_kernel(
   const int dt = prm.input_dtype;
   const int D = d.D;
   const int64_t lhp = d.lhp(b, layer, h);
+  // D (64 / 128), the group size, G and the V token block are powers of two
+  // (cache init checks the first and the others divide them), so index
+  // arithmetic below uses shifts
+  const int lgD = __ffs(D) - 1, lgGs = __ffs(d.gsize) - 1, lgG = __ffs(d.G) - 1;
 
   int p, nv;
   if (MODE == 0) {
@@ -63,15 +85,54 @@ __global__ void __launch_bounds__(256) page_store_kernel(
     }
     // stage rows; padded rows are zero (layer.py:262-271)
     const int64_t base = ((static_cast<int64_t>(s) * d.H + h) * T + t0) * D;
-    for (int i = tid; i < kPage * D; i += blockDim.x) {
-      const int r = i / D, c = i % D;
-      float kv = 0.f, vv = 0.f;
-      if (r < nv) {
-        kv = load_act(Kin, base + static_cast<int64_t>(r) * D + c, dt);
-        vv = load_act(Vin, base + static_cast<int64_t>(r) * D + c, dt);
+    const int esz = dt == CAREKV_F32 ? 4 : 2;
+    if (al16(Kin) && al16(Vin) && (D * esz) % 16 == 0 && blockDim.x == kStoreThreads) {
+      // 16-byte chunks of both pages (at most 4 per thread for D <= 128),
+      // every load issued before the first conversion
+      const int per = 16 / esz, nchunk = kPage * D / per, lgN = __ffs(nchunk) - 1;
+      uint4 ld[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = tid + u * kStoreThreads;
+        ld[u] = make_uint4(0u, 0u, 0u, 0u);
+        if (i < 2 * nchunk) {
+          const int e0 = (i & (nchunk - 1)) * per;
+          if ((e0 >> lgD) < nv)
+            ld[u] = *reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(i < nchunk ? Kin : Vin) +
+                                                    (base + e0) * esz);
+        }
       }
-      sm.x[0][r][c] = kv;
-      sm.x[1][r][c] = vv;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = tid + u * kStoreThreads;
+        if (i < 2 * nchunk) {
+          const int kind = i >> lgN, e0 = (i & (nchunk - 1)) * per;
+          float* dst = &sm.x[kind][e0 >> lgD][e0 & (D - 1)];
+          const uint32_t w[4] = {ld[u].x, ld[u].y, ld[u].z, ld[u].w};
+          if (esz == 4) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) dst[k] = __uint_as_float(w[k]);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint16_t lo = static_cast<uint16_t>(w[k]), hi = static_cast<uint16_t>(w[k] >> 16);
+              dst[2 * k] = dt == CAREKV_F16 ? f16_bits_to_f32(lo) : __bfloat162float(__ushort_as_bfloat16(lo));
+              dst[2 * k + 1] = dt == CAREKV_F16 ? f16_bits_to_f32(hi) : __bfloat162float(__ushort_as_bfloat16(hi));
+            }
+          }
+        }
+      }
+    } else {
+      for (int i = tid; i < kPage * D; i += blockDim.x) {
+        const int r = i >> lgD, c = i & (D - 1);
+        float kv = 0.f, vv = 0.f;
+        if (r < nv) {
+          kv = load_act(Kin, base + static_cast<int64_t>(r) * D + c, dt);
+          vv = load_act(Vin, base + static_cast<int64_t>(r) * D + c, dt);
+        }
+        sm.x[0][r][c] = kv;
+        sm.x[1][r][c] = vv;
+      }
     }
   } else {
     p = cache.num_pages[lhp] - 1;
@@ -82,8 +143,8 @@ __global__ void __launch_bounds__(256) page_store_kernel(
     const float mk = cfg.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(cache.k_master[pg]) : 0.f;
     const float mv = cfg.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(cache.v_master[pg]) : 0.f;
     for (int i = tid; i < kPage * D; i += blockDim.x) {
-      const int r = i / D, c = i % D;
-      const int64_t srow = (pg * kPage + r) * d.G + c / d.gsize;
+      const int r = i >> lgD, c = i & (D - 1);
+      const int64_t srow = (pg * kPage + r) * d.G + (c >> lgGs);
       const float sk = read_scale(cache.k_scale, srow, d.scale_mode, mk);
       const float sv = read_scale(cache.v_scale, srow, d.scale_mode, mv);
       const int ck = unpack_code(cache.k_codes + (pg * kPage + r) * d.R, c, d.bits);
@@ -104,31 +165,93 @@ __global__ void __launch_bounds__(256) page_store_kernel(
 
   if (MODE == 0) {
     // ── per-group quantization (quantizer.py:31-64) ──
-    for (int task = tid; task < 2 * kPage * d.G; task += blockDim.x) {
-      const int kind = task / (kPage * d.G);
-      const int r = (task / d.G) % kPage;
-      const int g = task % d.G;
-      float mx = 0.f;
-      for (int c = g * d.gsize; c < (g + 1) * d.gsize; ++c) mx = fmaxf(mx, fabsf(sm.x[kind][r][c]));
-      const float scale = group_scale(mx, qmax, dt);
-      sm.sc[kind][r][g] = scale;
-      for (int c = g * d.gsize; c < (g + 1) * d.gsize; ++c)
-        sm.code[kind][r][c] = quant_code(sm.x[kind][r][c], scale, qmax, dt);
+    const int gs = d.gsize;
+    if ((D == 64 || D == 128) && (gs == 16 || gs == 32 || gs == 64 || gs == 128) && D % gs == 0) {
+      // warp per (kind, row), lane on channels lane + 32k: the group maximum
+      // is a segmented (gs = 16) or whole-warp max combined over the
+      // group's columns; max is order-free, so the scale is the reference's
+      const int KD = D / 32;
+      for (int t = warp; t < 2 * kPage; t += blockDim.x / 32) {
+        const int kind = t / kPage, r = t % kPage;
+        float xv[4], m[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          xv[k] = k < KD ? sm.x[kind][r][lane + 32 * k] : 0.f;
+          m[k] = fmaxf(0.f, fabsf(xv[k]));
+        }
+        if (gs == 16) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) m[k] = fmaxf(m[k], __shfl_xor_sync(0xffffffffu, m[k], o));
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) m[k] = warp_max(m[k]);
+          if (gs >= 64) {
+            m[0] = m[1] = fmaxf(m[0], m[1]);
+            m[2] = m[3] = fmaxf(m[2], m[3]);
+          }
+          if (gs == 128) m[0] = m[1] = m[2] = m[3] = fmaxf(m[0], m[2]);
+        }
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          if (k < KD) {
+            const int c = lane + 32 * k;
+            const float scale = group_scale(m[k], qmax, dt);
+            sm.code[kind][r][c] = quant_code(xv[k], scale, qmax, dt);
+            if (c % gs == 0) sm.sc[kind][r][c / gs] = scale;
+          }
+        }
+      }
+    } else {
+      for (int task = tid; task < 2 * kPage * d.G; task += blockDim.x) {
+        const int kind = task >> (4 + lgG);
+        const int r = (task >> lgG) & (kPage - 1);
+        const int g = task & (d.G - 1);
+        float mx = 0.f;
+        for (int c = g * d.gsize; c < (g + 1) * d.gsize; ++c) mx = fmaxf(mx, fabsf(sm.x[kind][r][c]));
+        const float scale = group_scale(mx, qmax, dt);
+        sm.sc[kind][r][g] = scale;
+        for (int c = g * d.gsize; c < (g + 1) * d.gsize; ++c)
+          sm.code[kind][r][c] = quant_code(sm.x[kind][r][c], scale, qmax, dt);
+      }
     }
     __syncthreads();
-    // ── packed rows, all 16 rows (cache.py:636-640) ──
-    for (int i = tid; i < 2 * kPage * d.R; i += blockDim.x) {
-      const int kind = i / (kPage * d.R);
-      const int r = (i / d.R) % kPage;
-      const int j = i % d.R;
-      uint8_t* dst = (kind == 0 ? cache.k_codes : cache.v_codes) + (pg * kPage + r) * d.R + j;
-      *dst = pack_byte(&sm.code[kind][r][0], j, d.bits);
+    // ── packed rows, all 16 rows (cache.py:636-640), staged then stored ──
+    const int R = d.R;
+    if (d.bits == 3) {
+      const int WPR = D / 8, lgW = lgD - 3;   // 24-bit words (8 codes) per row
+      for (int i = tid; i < 2 * kPage * WPR; i += blockDim.x) {
+        const int kind = i >> (4 + lgW), r = (i >> lgW) & (kPage - 1), w = i & (WPR - 1);
+        const int8_t* cp = &sm.code[kind][r][8 * w];
+        uint32_t word = 0;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) word |= (static_cast<uint32_t>(cp[k]) & 7u) << (3 * k);
+        uint8_t* dst = &sm.packed[kind][r * R + 3 * w];
+        dst[0] = static_cast<uint8_t>(word);
+        dst[1] = static_cast<uint8_t>(word >> 8);
+        dst[2] = static_cast<uint8_t>(word >> 16);
+      }
+    } else {
+      const int lgR = __ffs(R) - 1;   // D/4 or D/2 bytes
+      for (int i = tid; i < 2 * kPage * R; i += blockDim.x) {
+        const int kind = i >> (4 + lgR), r = (i >> lgR) & (kPage - 1), j = i & (R - 1);
+        sm.packed[kind][r * R + j] = pack_byte(&sm.code[kind][r][0], j, d.bits);
+      }
+    }
+    __syncthreads();
+    {
+      uint8_t* kd = cache.k_codes + pg * kPage * R;
+      uint8_t* vd = cache.v_codes + pg * kPage * R;
+      const bool vec = (kPage * R) % 16 == 0 && al16(kd) && al16(vd);
+      cta_copy(kd, sm.packed[0], kPage * R, vec);
+      cta_copy(vd, sm.packed[1], kPage * R, vec);
     }
     // ── page scales (cache.py:592-606) ──
     if (d.scale_mode == CAREKV_SCALE_INT8) {
       for (int kind = 0; kind < 2; ++kind) {
         float mx = 0.f;
-        for (int i = tid; i < kPage * d.G; i += blockDim.x) mx = fmaxf(mx, fabsf(sm.sc[kind][i / d.G][i % d.G]));
+        for (int i = tid; i < kPage * d.G; i += blockDim.x) mx = fmaxf(mx, fabsf(sm.sc[kind][i >> lgG][i & (d.G - 1)]));
         mx = warp_max(mx);
         if (lane == 0) sm.red[kind][warp] = mx;
       }
@@ -143,16 +266,16 @@ __global__ void __launch_bounds__(256) page_store_kernel(
       }
       __syncthreads();
       for (int i = tid; i < 2 * kPage * d.G; i += blockDim.x) {
-        const int kind = i / (kPage * d.G);
-        const int r = (i / d.G) % kPage, g = i % d.G;
+        const int kind = i >> (4 + lgG);
+        const int r = (i >> lgG) & (kPage - 1), g = i & (d.G - 1);
         const int8_t c8 = int8_scale_code(sm.sc[kind][r][g], sm.master[kind]);
         reinterpret_cast<int8_t*>(kind == 0 ? cache.k_scale : cache.v_scale)[(pg * kPage + r) * d.G + g] = c8;
         sm.rscale[kind][r][g] = f16r(__fmul_rn(static_cast<float>(c8), sm.master[kind]));
       }
     } else {
       for (int i = tid; i < 2 * kPage * d.G; i += blockDim.x) {
-        const int kind = i / (kPage * d.G);
-        const int r = (i / d.G) % kPage, g = i % d.G;
+        const int kind = i >> (4 + lgG);
+        const int r = (i >> lgG) & (kPage - 1), g = i & (d.G - 1);
         void* dst = kind == 0 ? cache.k_scale : cache.v_scale;
         const int64_t idx = (pg * kPage + r) * d.G + g;
         write_raw_scale(dst, idx, d.scale_mode, sm.sc[kind][r][g]);
@@ -164,7 +287,7 @@ __global__ void __launch_bounds__(256) page_store_kernel(
     // ── residual in place (residual_store.py:271-285) + V_hat norm ──
     float vn = 0.f;
     for (int i = tid; i < kPage * D; i += blockDim.x) {
-      const int r = i / D, c = i % D, g = c / d.gsize;
+      const int r = i >> lgD, c = i & (D - 1), g = c >> lgGs;
       if (r < nv) {
         const float kh = dequant(sm.code[0][r][c], sm.sc[0][r][g], dt);
         const float vh = dequant(sm.code[1][r][c], sm.sc[1][r][g], dt);
@@ -210,7 +333,7 @@ __global__ void __launch_bounds__(256) page_store_kernel(
       // payload: value index i = t*32 + c, byte i/2 (residual_store.py:127-136)
       for (int j = lane; j < d.kslot_bytes; j += 32) {
         const int i0 = 2 * j;
-        const int t = i0 / d.kcg, c = i0 % d.kcg;
+        const int t = i0 >> 5, c = i0 & 31;   // kcg == 32
         const int lo = nibble_code(sm.x[0][t][c0 + c], sc4);
         const int hi = nibble_code(sm.x[0][t][c0 + c + 1], sc4);
         sm.payload[cand][j] = static_cast<uint8_t>((lo & 15) | ((hi & 15) << 4));
@@ -249,7 +372,7 @@ __global__ void __launch_bounds__(256) page_store_kernel(
       if (lane == 0) sm.s4[cand] = sc4;
       for (int j = lane; j < d.vslot_bytes; j += 32) {
         const int i0 = 2 * j;
-        const int t = t0 + i0 / D, c = i0 % D;
+        const int t = t0 + (i0 >> lgD), c = i0 & (D - 1);
         const int lo = nibble_code(sm.x[1][t][c], sc4);
         const int hi = nibble_code(sm.x[1][t][c + 1], sc4);
         sm.payload[cand][j] = static_cast<uint8_t>((lo & 15) | ((hi & 15) << 4));
@@ -327,20 +450,20 @@ __global__ void __launch_bounds__(256) page_store_kernel(
     for (int vb = 0; vb < d.NV; ++vb) cache.v_err[pg * d.NV + vb] = f32_to_f16_bits(sm.err[d.C + vb]);
     sm.red[1][0] = __int_as_float(nk);
     sm.red[1][1] = __int_as_float(nvk);
+    for (int j = 0; j < nk; ++j) sm.keep_k[j] = kr[j] & 0xFF;
+    for (int j = 0; j < nvk; ++j) sm.keep_v[j] = vr[j] & 0xFF;
   }
   __syncthreads();
   // payload copies of the kept slots
   const int nk = __float_as_int(sm.red[1][0]);
   const int nvk = __float_as_int(sm.red[1][1]);
   for (int j = 0; j < nk; ++j) {
-    const int cg = cache.k_slot_group[pg * d.SK + j];
     uint8_t* dst = cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes;
-    for (int i = tid; i < d.kslot_bytes; i += blockDim.x) dst[i] = sm.payload[cg][i];
+    cta_copy(dst, sm.payload[sm.keep_k[j]], d.kslot_bytes, d.kslot_bytes % 16 == 0 && al16(dst));
   }
   for (int j = 0; j < nvk; ++j) {
-    const int vb = cache.v_slot_block[pg * d.SV + j];
     uint8_t* dst = cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes;
-    for (int i = tid; i < d.vslot_bytes; i += blockDim.x) dst[i] = sm.payload[d.C + vb][i];
+    cta_copy(dst, sm.payload[d.C + sm.keep_v[j]], d.vslot_bytes, d.vslot_bytes % 16 == 0 && al16(dst));
   }
 }
 
