@@ -192,7 +192,8 @@ struct Dims {
   }
 };
 
-__host__ __device__ inline Dims make_dims(const carekv_config_t& c) {
+// every field except the three ratios G, C, NV
+__host__ __device__ inline Dims make_dims_shared(const carekv_config_t& c) {
   Dims d;
   d.L = c.num_layers;
   d.H = c.num_kv_heads;
@@ -201,11 +202,8 @@ __host__ __device__ inline Dims make_dims(const carekv_config_t& c) {
   d.bits = c.base_bits;
   d.R = row_bytes(c.head_dim, c.base_bits);
   d.gsize = c.group_size;
-  d.G = c.head_dim / c.group_size;
   d.kcg = c.k_channel_group;
-  d.C = c.head_dim / c.k_channel_group;
   d.vtb = c.v_token_block;
-  d.NV = kPage / c.v_token_block;
   d.SK = c.k_slots_per_page;
   d.SV = c.v_slots_per_page;
   d.kslot_bytes = kPage * c.k_channel_group / 2;
@@ -213,6 +211,24 @@ __host__ __device__ inline Dims make_dims(const carekv_config_t& c) {
   d.sketch = c.sketch_dim;
   d.scale_mode = c.scale_mode;
   d.scale_elem = c.scale_mode == CAREKV_SCALE_INT8 ? 1 : (c.scale_mode == CAREKV_SCALE_F32 ? 4 : 2);
+  return d;
+}
+__host__ __device__ inline Dims make_dims(const carekv_config_t& c) {
+  Dims d = make_dims_shared(c);
+  d.G = c.head_dim / c.group_size;
+  d.C = c.head_dim / c.k_channel_group;
+  d.NV = kPage / c.v_token_block;
+  return d;
+}
+
+// make_dims with shifts for the ratios of power-of-two sizes (head_dim,
+// group size, K channel group, V token block: checked at cache init).
+__device__ inline Dims make_dims_p2(const carekv_config_t& c) {
+  Dims d = make_dims_shared(c);
+  const int lgD = __ffs(c.head_dim) - 1;
+  d.G = 1 << (lgD - (__ffs(c.group_size) - 1));
+  d.C = 1 << (lgD - (__ffs(c.k_channel_group) - 1));
+  d.NV = kPage >> (__ffs(c.v_token_block) - 1);
   return d;
 }
 

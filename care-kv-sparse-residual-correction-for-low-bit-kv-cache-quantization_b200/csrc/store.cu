@@ -60,7 +60,7 @@ __global__ void __launch_bounds__(256) page_store_kernel(
     const void* __restrict__ Vin, int T, int seq_begin, carekv_store_params_t prm,
     const float* __restrict__ sketch_proj) {
   __shared__ StoreSmem sm;
-  const Dims d = make_dims(cfg);
+  const Dims d = make_dims_p2(cfg);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int h = blockIdx.y;
   const int s = blockIdx.z;
@@ -89,7 +89,7 @@ __global__ void __launch_bounds__(256) page_store_kernel(
     if (al16(Kin) && al16(Vin) && (D * esz) % 16 == 0 && blockDim.x == kStoreThreads) {
       // 16-byte chunks of both pages (at most 4 per thread for D <= 128),
       // every load issued before the first conversion
-      const int per = 16 / esz, nchunk = kPage * D / per, lgN = __ffs(nchunk) - 1;
+      const int lgP = esz == 4 ? 2 : 3, per = 1 << lgP, nchunk = (kPage * D) >> lgP, lgN = __ffs(nchunk) - 1;
       uint4 ld[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(256) page_store_kernel(
             const int c = lane + 32 * k;
             const float scale = group_scale(m[k], qmax, dt);
             sm.code[kind][r][c] = quant_code(xv[k], scale, qmax, dt);
-            if (c % gs == 0) sm.sc[kind][r][c / gs] = scale;
+            if ((c & (gs - 1)) == 0) sm.sc[kind][r][c >> lgGs] = scale;
           }
         }
       }
