@@ -293,6 +293,42 @@ def run_gpu(args, rank, world):
     return res
 
 
+def run_prefill_store(batch):
+    """Side measurement (not the bench line): the prefill page store of
+    `batch` sequences x the workload's context x kv heads (bf16 inputs,
+    the bench's cache configuration), two layers, the second timed with
+    CUDA events on the current stream."""
+    import torch
+    import importlib
+    for k, v in PAPER_BEST_ENV.items():
+        os.environ[k] = v
+    pkg = importlib.import_module(PKG)
+    dev = torch.device("cuda", 0)
+    w = WORKLOAD
+    H, D, N = w["kv_heads"], w["head_dim"], w["context"]
+    cfg = pkg.CacheConfig(num_layers=2, num_heads=w["heads"], num_kv_heads=H, head_dim=D, page_size=16,
+                          max_pages=N // 16 + 8, base_bits=w["bits"], group_size=w["group_size"],
+                          scale_quant="int8", packed_base=True, store_budget_mode="absolute",
+                          store_abs_k=w["store_k"], store_abs_v=w["store_v"], read_budget_mode="ratio",
+                          read_budget_ratio=w["read_ratio"], route_policy="joint")
+    cache = pkg.CAREKVCache(cfg, dev, batch=batch)
+    eng = pkg.DecodeEngine(cache)
+    g = torch.Generator(device=dev).manual_seed(0)
+    K = torch.randn(batch, H, N, D, device=dev, generator=g).to(torch.bfloat16)
+    V = torch.randn(batch, H, N, D, device=dev, generator=g).to(torch.bfloat16)
+    eng.prefill_store(0, K, V)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    eng.prefill_store(1, K, V)
+    e1.record()
+    torch.cuda.synchronize()
+    cache.check_errors()
+    ms = e0.elapsed_time(e1)
+    print(json.dumps(dict(measure="prefill page store (one layer)", batch=batch, tokens=N, kv_heads=H, head_dim=D,
+                          ms=ms, pages=batch * H * (N // 16), input_bytes=2 * K.numel() * K.element_size())))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -302,7 +338,12 @@ def main():
     ap.add_argument("--layers", type=int, default=WORKLOAD["layers"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--prefill-store", type=int, default=0, metavar="B",
+                    help="side measurement: time the prefill page store of B sequences and exit")
     args = ap.parse_args()
+    if args.prefill_store > 0:
+        run_prefill_store(args.prefill_store)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     w = WORKLOAD
