@@ -382,76 +382,76 @@ __global__ void __launch_bounds__(256) page_store_kernel(
   __syncthreads();
 
   // ── selection (residual_store.py:370-423) and slot tables ──
-  if (tid == 0) {
-    int order[8], n_k = 0, n_v = 0, korder[8], vorder[8];
+  // Warp 0, lane x = candidate x (K channel groups, then V token blocks).
+  // The reference sorts each kind stably by descending error (positive
+  // errors only), merges the two lists stably (K first on equal errors),
+  // keeps the first joint_budget (or k_budget / v_budget), caps them at the
+  // slot capacity and stores the kept ones in ascending group order with
+  // their sorted rank as slot id.  Here every lane computes its own rank
+  // and merged position by counting, so no thread sorts.
+  if (warp == 0) {
+    const int ncand = d.C + d.NV;
     const bool pos = prm.sensitivity > 0.f && !prm.store_nothing;
-    // stable descending by error, positive errors only
-    for (int i = 0; i < d.C; ++i)
-      if (pos && sm.err[i] > 0.f) korder[n_k++] = i;
-    for (int i = 0; i < d.NV; ++i)
-      if (pos && sm.err[d.C + i] > 0.f) vorder[n_v++] = d.C + i;
-    for (int a = 1; a < n_k; ++a)
-      for (int q = a; q > 0 && sm.err[korder[q]] > sm.err[korder[q - 1]]; --q) {
-        int t = korder[q]; korder[q] = korder[q - 1]; korder[q - 1] = t;
+    const bool isk = lane < d.C, isv = lane >= d.C && lane < ncand;
+    const float e = (isk || isv) ? sm.err[lane] : 0.f;
+    const bool elig = (isk || isv) && pos && e > 0.f;
+    int rank = 0, other = 0;   // rank in its kind; merged-order predecessors of the other kind
+    for (int o = 0; o < ncand; ++o) {
+      const float eo = sm.err[o];
+      if (!(pos && eo > 0.f)) continue;
+      if ((o < d.C) == isk) {
+        if (eo > e || (eo == e && o < lane)) ++rank;
+      } else {
+        if (isk ? eo > e : eo >= e) ++other;   // a V entry precedes a K entry only with a larger error
       }
-    for (int a = 1; a < n_v; ++a)
-      for (int q = a; q > 0 && sm.err[vorder[q]] > sm.err[vorder[q - 1]]; --q) {
-        int t = vorder[q]; vorder[q] = vorder[q - 1]; vorder[q - 1] = t;
-      }
-    int keep_k = 0, keep_v = 0;
+    }
+    const unsigned bk = __ballot_sync(0xffffffffu, elig && isk), bv = __ballot_sync(0xffffffffu, elig && isv);
+    const int n_k = __popc(bk), n_v = __popc(bv);
+    int keep_k, keep_v;
     if (prm.joint_budget > 0) {
-      // merge K then V stably by error, take joint_budget (residual_store.py:416-418)
-      int ik = 0, iv = 0, n = 0;
-      while (n < prm.joint_budget && (ik < n_k || iv < n_v)) {
-        if (iv >= n_v || (ik < n_k && !(sm.err[vorder[iv]] > sm.err[korder[ik]]))) { ++ik; ++keep_k; }
-        else { ++iv; ++keep_v; }
-        ++n;
-      }
+      const bool in = elig && rank + other < prm.joint_budget;
+      keep_k = __popc(__ballot_sync(0xffffffffu, in && isk));
+      keep_v = __popc(__ballot_sync(0xffffffffu, in && isv));
     } else {
       keep_k = min(n_k, prm.k_budget);
       keep_v = min(n_v, prm.v_budget);
     }
     keep_k = min(keep_k, d.SK);
     keep_v = min(keep_v, d.SV);
-    // kept candidates in ascending group order, with their score rank
-    int kr[8], nk = 0;
-    for (int i = 0; i < keep_k; ++i) order[i] = korder[i];
-    for (int cg = 0; cg < d.C; ++cg)
-      for (int i = 0; i < keep_k; ++i)
-        if (order[i] == cg) kr[nk++] = cg | (i << 8);
-    for (int j = 0; j < d.SK; ++j) {
-      const int64_t e = pg * d.SK + j;
-      if (j < nk) {
-        cache.k_slot_group[e] = static_cast<int8_t>(kr[j] & 0xFF);
-        cache.k_slot_scale[e] = f32_to_f16_bits(sm.s4[kr[j] & 0xFF]);
-        cache.k_slot_id[e] = kr[j] >> 8;  // local rank; the scan adds the arena base
-      } else {
-        cache.k_slot_group[e] = -1;
-        cache.k_slot_id[e] = -1;
-      }
+    const bool kept_k = elig && isk && rank < keep_k, kept_v = elig && isv && rank < keep_v;
+    const unsigned mk = __ballot_sync(0xffffffffu, kept_k), mv = __ballot_sync(0xffffffffu, kept_v);
+    const unsigned lt = (1u << lane) - 1u;
+    const int nk = __popc(mk), nvk = __popc(mv);
+    if (kept_k) {
+      const int j = __popc(mk & lt);
+      const int64_t sidx = pg * d.SK + j;
+      cache.k_slot_group[sidx] = static_cast<int8_t>(lane);
+      cache.k_slot_scale[sidx] = f32_to_f16_bits(sm.s4[lane]);
+      cache.k_slot_id[sidx] = rank;  // local rank; the scan adds the arena base
+      sm.keep_k[j] = lane;
     }
-    int vr[8], nvk = 0;
-    for (int i = 0; i < keep_v; ++i) order[i] = vorder[i];
-    for (int vb = 0; vb < d.NV; ++vb)
-      for (int i = 0; i < keep_v; ++i)
-        if (order[i] == d.C + vb) vr[nvk++] = vb | (i << 8);
-    for (int j = 0; j < d.SV; ++j) {
-      const int64_t e = pg * d.SV + j;
-      if (j < nvk) {
-        cache.v_slot_block[e] = static_cast<int8_t>(vr[j] & 0xFF);
-        cache.v_slot_scale[e] = f32_to_f16_bits(sm.s4[d.C + (vr[j] & 0xFF)]);
-        cache.v_slot_id[e] = vr[j] >> 8;
-      } else {
-        cache.v_slot_block[e] = -1;
-        cache.v_slot_id[e] = -1;
-      }
+    if (kept_v) {
+      const int j = __popc(mv & lt);
+      const int64_t sidx = pg * d.SV + j;
+      cache.v_slot_block[sidx] = static_cast<int8_t>(lane - d.C);
+      cache.v_slot_scale[sidx] = f32_to_f16_bits(sm.s4[lane]);
+      cache.v_slot_id[sidx] = rank;
+      sm.keep_v[j] = lane - d.C;
     }
-    for (int cg = 0; cg < d.C; ++cg) cache.k_err[pg * d.C + cg] = f32_to_f16_bits(sm.err[cg]);
-    for (int vb = 0; vb < d.NV; ++vb) cache.v_err[pg * d.NV + vb] = f32_to_f16_bits(sm.err[d.C + vb]);
-    sm.red[1][0] = __int_as_float(nk);
-    sm.red[1][1] = __int_as_float(nvk);
-    for (int j = 0; j < nk; ++j) sm.keep_k[j] = kr[j] & 0xFF;
-    for (int j = 0; j < nvk; ++j) sm.keep_v[j] = vr[j] & 0xFF;
+    if (lane >= nk && lane < d.SK) {
+      cache.k_slot_group[pg * d.SK + lane] = -1;
+      cache.k_slot_id[pg * d.SK + lane] = -1;
+    }
+    if (lane >= nvk && lane < d.SV) {
+      cache.v_slot_block[pg * d.SV + lane] = -1;
+      cache.v_slot_id[pg * d.SV + lane] = -1;
+    }
+    if (isk) cache.k_err[pg * d.C + lane] = f32_to_f16_bits(e);
+    if (isv) cache.v_err[pg * d.NV + lane - d.C] = f32_to_f16_bits(e);
+    if (lane == 0) {
+      sm.red[1][0] = __int_as_float(nk);
+      sm.red[1][1] = __int_as_float(nvk);
+    }
   }
   __syncthreads();
   // payload copies of the kept slots
