@@ -51,7 +51,8 @@ class Cache(ctypes.Structure):
 
 class StoreParams(ctypes.Structure):
     _fields_ = [("k_budget", i32), ("v_budget", i32), ("joint_budget", i32), ("store_nothing", i32),
-                ("sink_tokens", i32), ("token_start", i32), ("sensitivity", f32), ("input_dtype", i32)]
+                ("sink_tokens", i32), ("token_start", i32), ("sensitivity", f32), ("input_dtype", i32),
+                ("decode_page_master", i32)]
 
 
 class RouteParams(ctypes.Structure):

@@ -262,6 +262,10 @@ def resolve_store_params(cfg: CacheConfig, layer_id: int, input_dtype: int,
     p.token_start = token_start
     p.sensitivity = float(cfg.layer_sensitivity[layer_id])
     p.input_dtype = input_dtype
+    # CAREKV_DECODE_PAGE_MASTER=1: a page opened during decode takes its int8
+    # master from its first row instead of keeping the reference's 0
+    # (cache.py:689-695, whose appended rows then read back as zero)
+    p.decode_page_master = 1 if os.environ.get("CAREKV_DECODE_PAGE_MASTER", "0").lower() in {"1", "true", "yes"} else 0
     return p
 
 

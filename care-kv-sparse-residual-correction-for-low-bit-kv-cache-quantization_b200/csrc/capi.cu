@@ -199,6 +199,7 @@ int carekv_unpack_4bit(const uint8_t* packed, const uint16_t* scale_f16, float* 
 static int validate_store_params(const carekv_config_t* cfg, const carekv_store_params_t* p) {
   if (p == nullptr) return CAREKV_ERR_INVALID_ARG;
   CHECK(validate_dtype(p->input_dtype));
+  if (p->decode_page_master != 0 && p->decode_page_master != 1) return CAREKV_ERR_INVALID_ARG;
   const int C = cfg->head_dim / cfg->k_channel_group, NV = kPage / cfg->v_token_block;
   if (p->k_budget < 0 || p->v_budget < 0) return CAREKV_ERR_INVALID_ARG;
   if (p->joint_budget > 0) {

@@ -671,7 +671,16 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
     void* dst = kind == 0 ? cache.k_scale : cache.v_scale;
     const int64_t idx = (pg * kPage + off) * d.G + g;
     if (d.scale_mode == CAREKV_SCALE_INT8) {
-      const float m = f16_bits_to_f32(static_cast<uint16_t>(kind == 0 ? masters : masters >> 16));
+      uint16_t mb = static_cast<uint16_t>(kind == 0 ? masters : masters >> 16);
+      if (prm.decode_page_master && off == 0 && mb == 0) {
+        // a page opened by decode: its first row sets the master the way
+        // write_base does for a prefill page (max scale, clamped, / 127)
+        float mx = 0.f;
+        for (int gg = 0; gg < d.G; ++gg) mx = fmaxf(mx, fabsf(scs[kind][gg]));
+        mb = f32_to_f16_bits(__fdiv_rn(fmaxf(mx, clamp_lo(dt)), 127.0f));
+        if (g == 0) (kind == 0 ? cache.k_master : cache.v_master)[pg] = mb;
+      }
+      const float m = f16_bits_to_f32(mb);
       const float mc = fmaxf(m, 1e-8f);  // master.clamp(min=1e-8) in fp32
       const int8_t c8 = int8_scale_code(scs[kind][g], mc);
       reinterpret_cast<int8_t*>(dst)[idx] = c8;

@@ -116,6 +116,11 @@ typedef struct carekv_store_params {
     int32_t token_start;      /* absolute position of the first prefill row   */
     float   sensitivity;      /* layer sensitivity                            */
     int32_t input_dtype;      /* CAREKV_F32 / F16 / BF16 of the K and V rows   */
+    int32_t decode_page_master; /* int8 scales: 0 = a page opened by decode keeps
+                                 * master 0, so its rows read back as 0 (the
+                                 * reference, cache.py:689-695); 1 = its first
+                                 * appended row sets the master (max scale / 127,
+                                 * as write_base does, cache.py:592-606)        */
 } carekv_store_params_t;
 
 /* Per-call routing / correction policy (attention.py:576-957,
