@@ -162,3 +162,19 @@ def test_unbuilt_router_ablations_fail_loudly(knob, value):
             pkg.resolve_route_params(cfg, 0)
     with env(**{knob: None}):
         pkg.resolve_route_params(cfg, 0)      # default: accepted
+
+
+def test_decode_page_master_flag_resolution():
+    """CAREKV_DECODE_PAGE_MASTER reaches carekv_store_params_t (default 0 =
+    the reference's master-0 decode pages, cache.py:689-695)."""
+    pkg = load_pkg()
+    cfg = pkg.CacheConfig(num_layers=1, num_heads=4, num_kv_heads=2, head_dim=64, max_pages=4)
+    with env(CAREKV_DECODE_PAGE_MASTER=None):
+        assert pkg.resolve_store_params(cfg, 0, 0).decode_page_master == 0
+    with env(CAREKV_DECODE_PAGE_MASTER="1"):
+        assert pkg.resolve_store_params(cfg, 0, 0).decode_page_master == 1
+    fields = [f for f, _ in pkg._lib.StoreParams._fields_]
+    hdr = open(os.path.join(ROOT, "include", "carekv_b200.h")).read()
+    body = hdr[hdr.index("typedef struct carekv_store_params"):hdr.index("} carekv_store_params_t;")]
+    assert re.findall(r"int32_t\s+(\w+);|float\s+(\w+);", body) and \
+        [a or b for a, b in re.findall(r"int32_t\s+(\w+);|float\s+(\w+);", body)] == fields
