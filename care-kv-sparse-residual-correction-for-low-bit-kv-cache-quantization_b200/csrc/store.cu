@@ -563,8 +563,9 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
                                                     const void* __restrict__ kin,
                                                     const void* __restrict__ vin, int seq_begin,
                                                     carekv_store_params_t prm) {
-  const Dims d = make_dims(cfg);
+  const Dims d = make_dims_p2(cfg);
   const int lane = threadIdx.x;
+  const int lgGs = __ffs(d.gsize) - 1, lgG = __ffs(d.G) - 1;   // powers of two (cache init)
   const int h = blockIdx.x, s = blockIdx.y, b = seq_begin + s;
   const int dt = prm.input_dtype;
   const int D = d.D;
@@ -582,9 +583,18 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
   }
   uint32_t masters = 0;   // lane 0: fp16 K | V master of the target page, read early
   if (lane == 0) {
-    int np = cache.num_pages[lhp];
+    const int np = cache.num_pages[lhp];
     int p = np - 1;
-    if (p < 0 || cache.valid[lhp * d.P + p] >= kPage) {
+    // the last page's fill and masters in one round trip
+    int last_valid = kPage;
+    if (p >= 0) {
+      const int64_t pl = lhp * d.P + p;
+      last_valid = cache.valid[pl];
+      if (cfg.scale_mode == CAREKV_SCALE_INT8)
+        masters = cache.k_master[pl] | (static_cast<uint32_t>(cache.v_master[pl]) << 16);
+    }
+    if (last_valid >= kPage) {
+      masters = 0;
       p = np;
       if (p >= d.P) {
         atomicOr(cache.error_flag, kErrPageOverflow);
@@ -603,9 +613,7 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
       }
     }
     sh_p = p;
-    sh_off = p >= 0 ? cache.valid[lhp * d.P + p] : 0;
-    if (p >= 0 && cfg.scale_mode == CAREKV_SCALE_INT8)
-      masters = cache.k_master[lhp * d.P + p] | (static_cast<uint32_t>(cache.v_master[lhp * d.P + p]) << 16);
+    sh_off = p == np - 1 ? last_valid : 0;   // a page opened here starts empty
   }
   __syncwarp();
   const int p = sh_p;
@@ -621,7 +629,7 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
     for (int t = 0; t < 4; ++t) {
       const int c = lane + 32 * t;
       if (c < D) {
-        const int g = c / d.gsize;
+        const int g = c >> lgGs;
 #pragma unroll
         for (int gg = 0; gg < 4; ++gg) {
           if (gg == g) {
@@ -639,7 +647,7 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
         mx[1][gg] = fmaxf(mx[1][gg], __shfl_xor_sync(0xffffffffu, mx[1][gg], o));
       }
     if (lane < 2 * d.G) {
-      const int kind = lane / d.G, g = lane % d.G;
+      const int kind = lane >> lgG, g = lane & (d.G - 1);
       float m = mx[0][0];
 #pragma unroll
       for (int kk = 0; kk < 2; ++kk)
@@ -653,7 +661,7 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
     for (int t = 0; t < 4; ++t) {
       const int c = lane + 32 * t;
       if (c < D) {
-        const int g = c / d.gsize;
+        const int g = c >> lgGs;
         cs[0][c] = quant_code(xs[0][c], scs[0][g], qmax, dt);
         cs[1][c] = quant_code(xs[1][c], scs[1][g], qmax, dt);
       }
@@ -662,12 +670,12 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
   masters = __shfl_sync(0xffffffffu, masters, 0);
   __syncwarp();
   for (int j = lane; j < 2 * d.R; j += 32) {
-    const int kind = j / d.R, jj = j % d.R;
+    const int kind = j >= d.R ? 1 : 0, jj = j - kind * d.R;   // j < 2R
     (kind == 0 ? cache.k_codes : cache.v_codes)[(pg * kPage + off) * d.R + jj] = pack_byte(cs[kind], jj, d.bits);
   }
   __shared__ float rs[2][4];
   if (lane < 2 * d.G) {
-    const int kind = lane / d.G, g = lane % d.G;
+    const int kind = lane >> lgG, g = lane & (d.G - 1);
     void* dst = kind == 0 ? cache.k_scale : cache.v_scale;
     const int64_t idx = (pg * kPage + off) * d.G + g;
     if (d.scale_mode == CAREKV_SCALE_INT8) {
@@ -693,7 +701,7 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
   __syncwarp();
   float vn = 0.f;
   for (int c = lane; c < D; c += 32) {
-    const float vr = f16r(__fmul_rn(static_cast<float>(cs[1][c]), rs[1][c / d.gsize]));
+    const float vr = f16r(__fmul_rn(static_cast<float>(cs[1][c]), rs[1][c >> lgGs]));
     vn = fmaf(vr, vr, vn);
   }
   vn = warp_sum(vn);
