@@ -375,10 +375,13 @@ def gen_layer(out):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("CAREKV_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("CAREKV_REFERENCE"),
+                    help="root of the reference project checkout (or set CAREKV_REFERENCE)")
     ap.add_argument("--out", default=HERE)
     ap.add_argument("--only", default="", help="comma list of quant,store,correction,layer,kivi")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give --reference (or CAREKV_REFERENCE): the reference checkout the fixtures come from")
     import_reference(a.reference)
     import torch
     torch.set_num_threads(min(8, os.cpu_count() or 1))
