@@ -15,9 +15,10 @@ correction.  The dense projections / MLP are model work outside the path.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 
-N>1 runs one process per GPU (torchrun); each rank owns its own batch of
-32 sequences (weak scaling, no collective on the data path); the timing is
-the max over ranks.
+N>1 runs one process per GPU (torchrun).  By default the global batch of
+32 sequences is split over the ranks (strong scaling: rank r decodes
+sequences [r*32/N, (r+1)*32/N)); --scaling weak gives every rank its own 32.
+No collective is on the data path; the timing is the max over ranks.
 """
 
 import argparse
@@ -47,21 +48,28 @@ PAPER_BEST_ENV = dict(CAREKV_K_CORRECTION_MODE="exact", CAREKV_KSCORE_LIVE="1", 
                       CAREKV_PREFILL_RESIDUAL_KIND="both", CAREKV_STORE_POLICY="residual_kind_aware")
 
 
-def algorithmic_bytes_per_kvh(N, D=128, bits=3, G=4, sk=1, sv=1, page=16, vtb=4, qn=1, sel_v=1, act=2):
-    """Bytes the decode-attention op must move per (sequence, layer, kv head):
-    packed K+V codes, int8 scales, fp16 masters + valid counts, every stored
-    K slot (payload + fp16 scale + group id), the V slots' fp16 error norms and
-    block ids, the query in and the output out, and the V payloads read for
-    the selected slots."""
+def algorithmic_bytes_per_kvh(N, D=128, bits=3, G=4, sk=1, sv=1, page=16, vtb=4, qn=1, act=2):
+    """Bytes the decode-attention op must move per (sequence, layer, kv head)
+    before the routed reads: packed K+V codes, int8 scales, fp16 masters,
+    valid counts and V norms per page, every stored K slot (payload + fp16
+    scale + group id), the V slots' block ids and the page's fp16 V block
+    errors, the query in and the output out."""
     pages = math.ceil(N / page)
     codes = N * 2 * D * bits // 8
     scales = N * 2 * G
     page_meta = pages * (2 * 2 + 4 + 4)           # masters, valid, v_norm2
     k_slots = pages * sk * (page * 32 // 2 + 2 + 1)
-    v_meta = pages * sv * (2 + 1) + pages * (page // vtb) * 2 * 0
+    v_meta = pages * sv * 1 + pages * (page // vtb) * 2
     qo = 2 * qn * D * act
-    v_sel = qn * sel_v * (vtb * D // 2 + 2)
-    return codes + scales + page_meta + k_slots + v_meta + qo + v_sel
+    return codes + scales + page_meta + k_slots + v_meta + qo
+
+
+def selected_bytes(reads_k, reads_v, D=128, bits=3, G=4, page=16, vtb=4):
+    """Bytes the correction reads for the selected slots: a selected K slot's
+    page contributes its packed V rows and V scale codes (the exact
+    renormalisation re-weights the page's base V rows), a selected V slot
+    its 4-bit payload and fp16 scale."""
+    return reads_k * (page * D * bits // 8 + page * G) + reads_v * (vtb * D // 2 + 2)
 
 
 def sample_clocks(path):
@@ -100,15 +108,35 @@ def parse_clocks(path, gpu_index):
 PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "decode_attention_llama2_mha_b32_ctx4096.md")
 
 
+def build_id():
+    """Hash of the CUDA sources and the C header: names the build a profile
+    was captured on."""
+    import glob
+    import hashlib
+    h = hashlib.sha256()
+    files = sorted(glob.glob(os.path.join(ROOT, PKG, "csrc", "*")) + glob.glob(os.path.join(ROOT, "include", "*.h")))
+    for f in files:
+        if f.endswith((".cu", ".cuh", ".h")):
+            h.update(os.path.basename(f).encode())
+            with open(f, "rb") as fh:
+                h.update(fh.read())
+    return h.hexdigest()[:12]
+
+
 def profiled_traffic():
-    """DRAM bytes (read + write) of one decode-attention call, from the ncu
-    summary committed under profiles/ (None when it is absent)."""
+    """DRAM bytes (read + write) of one decode-attention call from the ncu
+    summary under profiles/, only when that capture was taken on this build
+    (its `build:` line equals build_id()); else None."""
     try:
+        vals = {}
         with open(PROFILE_SUMMARY) as f:
             for line in f:
-                if line.startswith("traffic_bytes_per_launch:"):
-                    return int(line.split(":", 1)[1])
-    except OSError:
+                for key in ("traffic_bytes_per_launch:", "build:"):
+                    if line.startswith(key):
+                        vals[key] = line.split(":", 1)[1].strip()
+        if vals.get("build:") == build_id() and "traffic_bytes_per_launch:" in vals:
+            return int(vals["traffic_bytes_per_launch:"])
+    except (OSError, ValueError):
         pass
     return None
 
@@ -179,8 +207,21 @@ def max_over_ranks(values, world, device=None):
 
 def aggregate_tok_s(world, batch_per_rank, steps, ms_max):
     """Whole-job tokens/s: every rank decodes `batch_per_rank` sequences per
-    step (weak scaling), timed as the slowest rank."""
+    step, timed as the slowest rank."""
     return world * batch_per_rank * steps / (ms_max / 1e3)
+
+
+def rank_batch(global_batch, world, rank, scaling):
+    """Sequences of rank `rank`: strong scaling splits the global batch into
+    contiguous shares (rank r owns sequences [r*B/N, (r+1)*B/N)); weak scaling
+    gives every rank the whole batch size.  Returns (first global sequence,
+    count)."""
+    if scaling == "weak":
+        return rank * global_batch, global_batch
+    if global_batch % world:
+        raise ValueError(f"global batch {global_batch} does not split over {world} ranks")
+    n = global_batch // world
+    return rank * n, n
 
 
 def run_gpu(args, rank, world):
@@ -193,7 +234,8 @@ def run_gpu(args, rank, world):
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
     w = WORKLOAD
-    L, H, D, B, N = args.layers, w["kv_heads"], w["head_dim"], w["batch"], w["context"]
+    seq0, B = rank_batch(w["batch"], world, rank, args.scaling)
+    L, H, D, N = args.layers, w["kv_heads"], w["head_dim"], w["context"]
     total_steps = args.warmup + args.steps + args.e2e_steps + 2
     max_pages = (N + total_steps + 15) // 16 + 8
     cfg = pkg.CacheConfig(num_layers=L, num_heads=w["heads"], num_kv_heads=H, head_dim=D, page_size=16,
@@ -203,7 +245,7 @@ def run_gpu(args, rank, world):
                           read_budget_ratio=w["read_ratio"], route_policy="joint")
     cache = pkg.CAREKVCache(cfg, dev, batch=B)
     eng = pkg.DecodeEngine(cache)
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    g = torch.Generator(device=dev).manual_seed(1234 + seq0)
     for l in range(L):   # prefill the context (not timed)
         K = torch.randn(B, H, N, D, device=dev, generator=g)
         K[..., :4] *= 20
@@ -253,6 +295,8 @@ def run_gpu(args, rank, world):
     lib = pkg._lib.lib()
     import ctypes
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+    rc = cache.view("read_counter")
+    rc.zero_()
     for l in range(L):
         a, b_ = ev[l]
         a.record(stream)
@@ -263,6 +307,7 @@ def run_gpu(args, rank, world):
         b_.record(stream)
     torch.cuda.synchronize()
     att_ms = [a.elapsed_time(b_) for a, b_ in ev]
+    reads_k, reads_v = (int(x) for x in rc.sum(dim=(0, 1)).tolist())   # slots read by the L timed calls
 
     # e2e through the public API: per step, pinned host inputs -> device,
     # step, output -> pinned host; DecodeStepGraph(host_io=...) keeps the
@@ -285,7 +330,8 @@ def run_gpu(args, rank, world):
     e2e_ms = f0.elapsed_time(f1)
 
     ms, e2e_ms, att_mean = max_over_ranks([ms, e2e_ms, statistics.mean(att_ms)], world, dev)
-    res = dict(ms=ms, e2e_ms=e2e_ms, att_ms=att_mean, launches=launches, ctx_end=ctx_end,
+    res = dict(ms=ms, e2e_ms=e2e_ms, att_ms=att_mean, launches=launches, ctx_end=ctx_end, batch=B,
+               reads_k=reads_k / L, reads_v=reads_v / L,
                clocks=parse_clocks(clk_path, dev.index) if rank == 0 else None,
                out_finite=bool(torch.isfinite(out.float()).all().item()),
                h2d=int(hq.numel() * 2 + hk.numel() * 2 + hv.numel() * 2), d2h=int(ho.numel() * 2))
@@ -338,6 +384,8 @@ def main():
     ap.add_argument("--layers", type=int, default=WORKLOAD["layers"])
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="strong: the global batch of 32 is split over the ranks; weak: 32 per rank")
     ap.add_argument("--prefill-store", type=int, default=0, metavar="B",
                     help="side measurement: time the prefill page store of B sequences and exit")
     args = ap.parse_args()
@@ -362,7 +410,7 @@ def main():
         r["value"] = val
         line = dict(impl="reference", metric=METRIC, value=val, unit=UNIT, n_gpus=args.gpus, steps=args.steps,
                     warmup=args.warmup, ms_per_step=1e3 * w["batch"] / val, higher_is_better=True,
-                    scaling="weak", vs_baseline=None, dtype="bf16", data="synthetic",
+                    scaling=args.scaling, vs_baseline=None, dtype="bf16", data="synthetic",
                     config=dict(workload=w["name"], global_batch=w["batch"], seq_len=w["context"],
                                 layers=w["layers"], parallelism="cpu"),
                     cpu_baseline=r, e2e=dict(value=val, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
@@ -386,27 +434,31 @@ def main():
         dist.destroy_process_group()
     if rank != 0:
         return
-    B, L = w["batch"], args.layers
+    B, L = res["batch"], args.layers
     tok_s = aggregate_tok_s(world, B, args.steps, res["ms"])
     e2e_tok_s = aggregate_tok_s(world, B, args.e2e_steps, res["e2e_ms"])
     peak, peak_kind = measured_peak_gbs()
     N_mid = res["ctx_end"]
-    bytes_call = B * w["kv_heads"] * algorithmic_bytes_per_kvh(N_mid, D=w["head_dim"], bits=w["bits"],
-                                                               G=w["head_dim"] // w["group_size"])
+    G = w["head_dim"] // w["group_size"]
+    bytes_call = (B * w["kv_heads"] * algorithmic_bytes_per_kvh(N_mid, D=w["head_dim"], bits=w["bits"], G=G)
+                  + selected_bytes(res["reads_k"], res["reads_v"], D=w["head_dim"], bits=w["bits"], G=G))
     achieved = bytes_call / (res["att_ms"] / 1e3) / 1e9
     line = dict(
         metric=METRIC, value=tok_s, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
-        ms_per_step=res["ms"] / args.steps, higher_is_better=True, scaling="weak", vs_baseline=None,
+        ms_per_step=res["ms"] / args.steps, higher_is_better=True, scaling=args.scaling, vs_baseline=None,
         dtype="bf16", data="synthetic (seeded K/V/Q; random-init stands in for Llama-2-7B)",
-        config=dict(workload=w["name"], global_batch=B * world, seq_len=w["context"], layers=L,
+        config=dict(workload=w["name"], global_batch=B * world, batch_per_gpu=B, seq_len=w["context"], layers=L,
                     heads=w["heads"], kv_heads=w["kv_heads"], head_dim=w["head_dim"], base_bits=w["bits"],
                     group_size=w["group_size"], store_slots="1K+1V per page", read_ratio=w["read_ratio"],
-                    correction="combined_kvscore+joint+normalize+exact", parallelism=f"dp{world} (batch-sharded)",
+                    correction="combined_kvscore+joint+normalize+exact",
+                    parallelism=f"dp{world} (batch-sharded, {args.scaling} scaling)",
                     l2="inputs larger than L2 (each layer call reads ~0.5 GB of KV; 32 layers ~16 GB)", cuda_graph=True),
         roofline=dict(bound="hbm", achieved=achieved, peak=peak, unit="GB/s", frac=achieved / peak,
-                      traffic=profiled_traffic(), traffic_source="ncu dram__bytes_read+write, " +
-                      os.path.relpath(PROFILE_SUMMARY, ROOT), kernel="carekv_decode_attention (split-K pass + route)",
-                      bytes_per_launch=bytes_call, launch_ms=res["att_ms"], peak_source=peak_kind),
+                      traffic=profiled_traffic(), traffic_source="ncu dram__bytes_read+write of build " +
+                      build_id() + " (null: no capture of this build), " + os.path.relpath(PROFILE_SUMMARY, ROOT),
+                      kernel="carekv_decode_attention (split-K pass + route)",
+                      bytes_per_launch=bytes_call, launch_ms=res["att_ms"], peak_source=peak_kind,
+                      selected_per_call=dict(k_slots=res["reads_k"], v_slots=res["reads_v"])),
         e2e=dict(value=e2e_tok_s, unit=UNIT, h2d_bytes_per_step=res["h2d"], d2h_bytes_per_step=res["d2h"]),
         gpu_launches=res["launches"],
         clocks=res["clocks"],

@@ -92,7 +92,7 @@ SIGNATURES = [
     ("carekv_decode_attention_noalloc", i32, [ctypes.POINTER(Config), ctypes.POINTER(Cache), i32, vp, vp, i32, i32,
                                               i32, i32, ctypes.POINTER(RouteParams), vp, vp]),
 ]
-NOALLOC_MAX_BYTES = 32 << 20
+NOALLOC_MAX_BYTES = 64 << 20
 
 _lib = None
 _load_error = None

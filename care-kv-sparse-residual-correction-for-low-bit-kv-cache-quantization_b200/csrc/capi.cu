@@ -258,16 +258,8 @@ int carekv_decode_attention(const carekv_config_t* cfg, const carekv_cache_t* ca
   if (max_pages_used < 0 || max_pages_used > cfg->max_pages) return CAREKV_ERR_INVALID_ARG;
   if (params->kind < CAREKV_KIND_BOTH || params->kind > CAREKV_KIND_NONE) return CAREKV_ERR_INVALID_ARG;
   if (params->kind != CAREKV_KIND_NONE) {
-    if (params->budget_mode == 0) {
-      if (params->read_k < 0 || params->read_v < 0 || params->read_k + params->read_v > kMaxSelHost)
-        return CAREKV_ERR_UNSUPPORTED;
-    } else {
-      const double nk = static_cast<double>(max_pages_used) * cfg->k_slots_per_page;
-      const double nv = static_cast<double>(max_pages_used) * cfg->v_slots_per_page;
-      const int bk = params->ratio_k > 0 ? std::max(1, static_cast<int>(nk * params->ratio_k)) : 0;
-      const int bv = params->ratio_v > 0 ? std::max(1, static_cast<int>(nv * params->ratio_v)) : 0;
-      if (bk + bv > kMaxSelHost) return CAREKV_ERR_UNSUPPORTED;
-    }
+    // any budget is served (selections beyond 32 entries apply in rounds)
+    if (params->budget_mode == 0 && (params->read_k < 0 || params->read_v < 0)) return CAREKV_ERR_INVALID_ARG;
     if (!params->kscore_live && (!cache->k_sketch || cfg->sketch_dim <= 0 || !sketch_proj))
       return CAREKV_ERR_INVALID_ARG;
   }
@@ -306,16 +298,8 @@ int carekv_prefill_correction(const carekv_config_t* cfg, const carekv_cache_t* 
       (!logits || !row_max || !cache->k_sketch || cfg->sketch_dim <= 0 || !sketch_proj))
     return CAREKV_ERR_INVALID_ARG;
   if (params->kind != CAREKV_KIND_NONE) {
-    if (params->budget_mode == 0) {
-      if (params->read_k < 0 || params->read_v < 0 || params->read_k + params->read_v > kMaxSelHost)
-        return CAREKV_ERR_UNSUPPORTED;
-    } else {
-      const double nk = static_cast<double>(max_pages_used) * cfg->k_slots_per_page;
-      const double nv = static_cast<double>(max_pages_used) * cfg->v_slots_per_page;
-      const int bk = params->ratio_k > 0 ? std::max(1, static_cast<int>(nk * params->ratio_k)) : 0;
-      const int bv = params->ratio_v > 0 ? std::max(1, static_cast<int>(nv * params->ratio_v)) : 0;
-      if (bk + bv > kMaxSelHost) return CAREKV_ERR_UNSUPPORTED;
-    }
+    // any budget is served (selections beyond 32 entries apply in rounds)
+    if (params->budget_mode == 0 && (params->read_k < 0 || params->read_v < 0)) return CAREKV_ERR_INVALID_ARG;
   }
   if (n_pos == 0) return CAREKV_OK;
   return prefill_correction(*cfg, *cache, layer, seq, n_pos, max_pages_used, q, logits, row_max, attn, attn_sum,

@@ -21,7 +21,6 @@
 #include "ptx.cuh"
 #include <algorithm>
 #include <cstdlib>
-#include <mutex>
 
 namespace carekv {
 
@@ -129,7 +128,6 @@ __global__ void __launch_bounds__(128) decode_partial_kernel(DecodeArgs a) {
   }
 }
 
-constexpr int kMaxSel = 32;  // selected slots per query (host-validated)
 
 // ─────────────────────────── host launch ───────────────────────────
 struct SplitPlan {
@@ -161,6 +159,11 @@ inline SplitPlan split_plan(int n_bh, int p_used, int slots) {
 }
 
 static inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
+// Entries per query of the selection readback: the count, then room for
+// every slot of the grid (a selection has no other upper bound).
+static inline int64_t sel_stride(const carekv_config_t& c, int p_used) {
+  return 1 + static_cast<int64_t>(p_used) * (c.k_slots_per_page + c.v_slots_per_page);
+}
 
 // Split-K pass chosen for a layout.  NARROW: INT3 or INT4 / int8 scales with at most
 // 4 query heads per kv head (decode_narrow.cu, 4 CTAs per SM, also computes
@@ -200,7 +203,7 @@ inline WsLayout ws_layout(const carekv_config_t& c, int seq_count, int p_used) {
   const SplitPlan sp = split_plan(chunk_size(seq_count) * c.num_kv_heads, p_used, pass_slots(pass));
   WsLayout w;
   int64_t o = 0;
-  w.sel = o;    o = align256(o + n_bh * qn * (kMaxSel + 1) * 4);
+  w.sel = o;    o = align256(o + n_bh * qn * sel_stride(c, p_used) * 4);
   w.scores = o; o = align256(o + n_bh * qn * static_cast<int64_t>(p_used) * (c.k_slots_per_page + c.v_slots_per_page) * 4);
   w.S = o;      o = align256(o + n_bh * qn * static_cast<int64_t>(p_used) * kPage * 4);
   w.pm = o;     o = align256(o + n_bh * sp.n_splits * qn * 4);
@@ -258,15 +261,34 @@ static cudaError_t launch_qn(DecodeArgs& a, cudaStream_t st, int n_bh) {
 // and the selection readback do not depend on the chunking.
 // Fork and join go through events, which stream capture records as graph
 // edges.  CAREKV_ATTEND_CHUNKS (1, 2 or 4; default 2) sets the count.
+// The helper streams and events belong to the calling host thread (one set
+// per device and thread), so concurrent calls from several threads, or a
+// capture on one thread while another thread runs uncaptured calls, never
+// share an event or a stream.
 namespace {
 constexpr int kMaxDev = 64, kMaxChunks = 4;
 struct ChunkStreams {
-  bool ready = false;
+  bool ready = false, failed = false;
   cudaStream_t st[kMaxChunks - 1] = {};
   cudaEvent_t fork = nullptr, join[kMaxChunks - 1] = {};
+  // release whatever exists (a partial set after a failed creation, or the
+  // whole set when the thread exits; errors after runtime teardown are moot)
+  void release() {
+    for (int i = 0; i < kMaxChunks - 1; ++i) {
+      if (st[i]) (void)cudaStreamDestroy(st[i]);
+      if (join[i]) (void)cudaEventDestroy(join[i]);
+      st[i] = nullptr;
+      join[i] = nullptr;
+    }
+    if (fork) (void)cudaEventDestroy(fork);
+    fork = nullptr;
+    ready = false;
+  }
+  ~ChunkStreams() {
+    if (ready) release();
+  }
 };
-ChunkStreams g_chunk[kMaxDev];
-std::mutex g_chunk_mu;
+thread_local ChunkStreams t_chunk[kMaxDev];
 
 int attend_chunks() {
   static const int n = [] {
@@ -277,26 +299,33 @@ int attend_chunks() {
   return n;
 }
 
-// Streams and events of the current device, created on first use outside
-// stream capture; null while they do not exist (the caller then runs
-// unchunked).
+// This thread's streams and events of the current device, created on first
+// use outside stream capture; null while they do not exist (the caller then
+// runs unchunked).  A creation that fails part-way releases what it made and
+// leaves this thread on the device unchunked from then on.
 ChunkStreams* chunk_streams(cudaStream_t caller) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
-  std::lock_guard<std::mutex> lock(g_chunk_mu);
-  ChunkStreams& cs = g_chunk[dev];
+  ChunkStreams& cs = t_chunk[dev];
   if (cs.ready) return &cs;
+  if (cs.failed) return nullptr;
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(caller, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) return nullptr;
   int least = 0, greatest = 0;
-  if (cudaDeviceGetStreamPriorityRange(&least, &greatest) != cudaSuccess) return nullptr;
-  for (int i = 0; i < kMaxChunks - 1; ++i) {
+  bool ok = cudaDeviceGetStreamPriorityRange(&least, &greatest) == cudaSuccess;
+  for (int i = 0; ok && i < kMaxChunks - 1; ++i) {
     // chunk 0 gets the greatest priority, later chunks step down towards the caller's
     const int prio = std::min(least, greatest + i);
-    if (cudaStreamCreateWithPriority(&cs.st[i], cudaStreamNonBlocking, prio) != cudaSuccess) return nullptr;
-    if (cudaEventCreateWithFlags(&cs.join[i], cudaEventDisableTiming) != cudaSuccess) return nullptr;
+    ok = cudaStreamCreateWithPriority(&cs.st[i], cudaStreamNonBlocking, prio) == cudaSuccess &&
+         cudaEventCreateWithFlags(&cs.join[i], cudaEventDisableTiming) == cudaSuccess;
   }
-  if (cudaEventCreateWithFlags(&cs.fork, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+  ok = ok && cudaEventCreateWithFlags(&cs.fork, cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) {
+    cs.release();
+    cs.failed = true;
+    (void)cudaGetLastError();   // the failure is handled here, not by the next launch check
+    return nullptr;
+  }
   cs.ready = true;
   return &cs;
 }
@@ -336,6 +365,7 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
   const WsLayout wl = ws_layout(cfg, seq_count, p_used);
   char* w = static_cast<char*>(ws);
   a.sel_out = reinterpret_cast<int*>(w + wl.sel);
+  a.sel_stride = static_cast<int>(sel_stride(cfg, p_used));
   a.scores = reinterpret_cast<float*>(w + wl.scores);
   a.S = reinterpret_cast<float*>(w + wl.S);
   a.pm = reinterpret_cast<float*>(w + wl.pm);
@@ -386,7 +416,7 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
     ac.seq_begin = seq_begin + s0;
     ac.q = static_cast<const char*>(q) + bh0 * qn * D * es;
     ac.out = static_cast<char*>(out) + bh0 * qn * D * es;
-    ac.sel_out = a.sel_out + bh0 * qn * (kMaxSel + 1);
+    ac.sel_out = a.sel_out + bh0 * qn * a.sel_stride;
     ac.scores = a.scores + bh0 * qn * NGs;
     ac.S = a.S + bh0 * qn * p_used * kPage;
     ac.pm = a.pm + bh0 * a.n_splits * qn;
@@ -446,6 +476,7 @@ int prefill_correction(const carekv_config_t& cfg, const carekv_cache_t& cache, 
   const WsLayout wl = ws_layout(cfg, n_pos, p_used);
   char* w = static_cast<char*>(ws);
   a.sel_out = reinterpret_cast<int*>(w + wl.sel);
+  a.sel_stride = static_cast<int>(sel_stride(cfg, p_used));
   a.scores = reinterpret_cast<float*>(w + wl.scores);
   a.S = const_cast<float*>(logits);
   a.pm = const_cast<float*>(row_max);

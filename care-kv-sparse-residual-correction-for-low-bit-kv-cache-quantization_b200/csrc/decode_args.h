@@ -23,7 +23,8 @@ struct DecodeArgs {
   float* pl;
   float* po;        // [bh][n_splits][qn][D]
   float* scores;    // [bh][qn][p_used*(SK+SV)]
-  int* sel_out;     // [bh][qn][1 + kMaxSel]: count, then selected grid indices
+  int* sel_out;     // [bh][qn][sel_stride]: count, then the selected grid indices
+  int sel_stride;   // 1 + p_used * (SK + SV): room for every slot of the grid
   float* kw;        // [bh][qn][p_used*SK][16]: q . R_K per stored K slot and token, written by
                     // the narrow split-K pass when live K scoring runs there; null otherwise
   int s_perm;       // 1: S and kw hold a page's 16 tokens in tok_pos() order

@@ -34,5 +34,4 @@ int prefill_correction(const carekv_config_t& cfg, const carekv_cache_t& cache, 
                        const float* A_sum, const float* O, const float* O_exact, const float* v_rows,
                        const float* v_pnorm, void* out, int dtype, const carekv_route_params_t& rp,
                        const float* sketch_proj, void* ws, size_t ws_bytes, cudaStream_t st);
-constexpr int kMaxSelHost = 32;
 }  // namespace carekv

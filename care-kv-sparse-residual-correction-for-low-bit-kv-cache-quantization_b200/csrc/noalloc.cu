@@ -34,7 +34,7 @@
 namespace carekv {
 namespace {
 
-constexpr size_t kMaxBytes = CAREKV_NOALLOC_MAX_BYTES;  // 32 MiB per device
+constexpr size_t kMaxBytes = CAREKV_NOALLOC_MAX_BYTES;  // 64 MiB per device
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kMaxBytes];
 

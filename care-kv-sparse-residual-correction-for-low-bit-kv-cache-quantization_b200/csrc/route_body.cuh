@@ -29,7 +29,7 @@
 
 namespace carekv {
 
-constexpr int kRSel = 32;     // selected slots per query (host-validated)
+constexpr int kRSel = 32;     // selected items per apply round (a selection may hold more)
 constexpr int kRStg = 12 * 1024;   // apply staging bytes per CTA
 constexpr float kREps = 1e-6f;
 constexpr float kRL2e = 1.4426950408889634f;
@@ -142,9 +142,11 @@ struct RouteSmem {
   float M[QN], invL[QN], L[QN], mlb[QN];   // mlb = M log2(e) + log2(L)
   float red[NW][QN], red2[NW][QN];
   float nk[QN], nv[QN];
-  int sel[QN][kRSel];
-  float selv[QN][kRSel];
-  int nsel[QN];
+  int sel[QN][kRSel];            // the first kRSel selected entries, or the current apply round
+  int nsel[QN];                  // selected entries per query (any count up to the grid size)
+  int hist[256];                 // radix-select histogram (selections above kRSel)
+  int rsel[4];                   // radix select: digit, remaining count; scan totals
+  int scan[NW];
   // per-warp top-32 lists of the selection; the prefilter uses the first NW
   // entries for thresholds and entries 32..95 for candidates
   float gv[NW * 32 > 96 ? NW * 32 : 96];
@@ -258,7 +260,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   __syncthreads();
 
   auto write_base = [&]() {
-    if (tid < QN) a.sel_out[(static_cast<int64_t>(bh) * QN + tid) * (kRSel + 1)] = 0;
+    if (tid < QN) a.sel_out[(static_cast<int64_t>(bh) * QN + tid) * a.sel_stride] = 0;
     for (int idx = tid; idx < QN * D; idx += NT) {
       const int i = idx / D, c = idx % D;
       store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + c, sm.O[i][c], a.dt);
@@ -667,25 +669,146 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   // running list); warp 0 merges the warps' lists the same way.  Excluded
   // entries hold a negative score and sort last.
   // Publish the first n of a sorted list (one element per lane) into sel[i].
+  int* const gsel_base = a.sel_out + static_cast<int64_t>(bh) * QN * a.sel_stride;
   auto publish = [&](int i, float mv, int mi, int k) {
     const int base = sm.nsel[i];
-    const int room = kRSel - base;
     int n = __popc(__ballot_sync(0xffffffffu, mv >= 0.f));
     n = min(n, k);
-    if (n > room) {
-      if (lane == 0) atomicOr(a.cache.error_flag, 8);
-      n = room;
-    }
     if (lane < n) {
-      sm.sel[i][base + lane] = mi;
-      sm.selv[i][base + lane] = mv;
+      gsel_base[i * a.sel_stride + 1 + base + lane] = mi;
+      if (base + lane < kRSel) sm.sel[i][base + lane] = mi;
     }
     if (__any_sync(0xffffffffu, lane < n && mi < KG) && lane == 0) sm.any_k = 1;
     __syncwarp();
     if (lane == 0) sm.nsel[i] = base + n;
   };
+  // exclusive prefix sum of v over the CTA's threads (thread order); every
+  // thread calls it
+  auto block_scan = [&](int v, int& total) -> int {
+    int x = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) sm.scan[warp] = x;
+    __syncthreads();
+    int before = 0;
+    total = 0;
+    for (int w = 0; w < NW; ++w) {
+      const int t = sm.scan[w];
+      if (w < warp) before += t;
+      total += t;
+    }
+    __syncthreads();
+    return before + x - v;
+  };
+  // Top-k (k > kRSel) of sc[i][lo:hi) by (score desc, index asc), appended
+  // to the selection in index order.  Radix select on the candidates'
+  // score bits (non-negative fp32 scores order like their bit patterns),
+  // four 8-bit digits from the top, finds the k-th score T; every entry
+  // above T is taken and, of the entries equal to T, the lowest indices
+  // (a block-wide stable compaction in index order).
+  auto pick_large = [&](int i, int lo, int hi, int k) {
+    const float* row = sc + i * NG;
+    auto key_of = [&](int e, bool& cand) -> uint32_t {
+      const float x = row[e];
+      cand = x >= 0.f;   // NaN and excluded entries (negative) are not candidates
+      return __float_as_uint(__fadd_rn(x, 0.0f));
+    };
+    int ncand = 0;
+    for (int e = lo + tid; e < hi; e += NT) {
+      bool c;
+      (void)key_of(e, c);
+      ncand += c;
+    }
+    int tot = 0;
+    (void)block_scan(ncand, tot);
+    const int need = min(k, tot);
+    if (need <= 0) return;
+    uint32_t prefix = 0, pmask = 0;
+    int remaining = need;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int x = tid; x < 256; x += NT) sm.hist[x] = 0;
+      __syncthreads();
+      for (int e = lo + tid; e < hi; e += NT) {
+        bool c;
+        const uint32_t u = key_of(e, c);
+        if (c && (u & pmask) == prefix) atomicAdd(&sm.hist[(u >> shift) & 255], 1);
+      }
+      __syncthreads();
+      if (warp == 0) {
+        // lane l holds digits 255-8l .. 248-8l (descending); suffix counts
+        int cnt[8], own = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { cnt[j] = sm.hist[255 - 8 * lane - j]; own += cnt[j]; }
+        int incl = own;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        const int above = incl - own;   // entries in digits above this lane's range
+        // the lane whose range holds the remaining-th largest entry
+        const bool mine = above < remaining && remaining <= incl;
+        if (mine) {
+          int acc = above;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            if (acc + cnt[j] >= remaining) {
+              sm.rsel[0] = 255 - 8 * lane - j;
+              sm.rsel[1] = remaining - acc;
+              break;
+            }
+            acc += cnt[j];
+          }
+        }
+      }
+      __syncthreads();
+      prefix |= static_cast<uint32_t>(sm.rsel[0]) << shift;
+      pmask |= 255u << shift;
+      remaining = sm.rsel[1];
+      __syncthreads();
+    }
+    // prefix = T (exact score bits); remaining = entries equal to T to take
+    const int len = hi - lo, chunk = (len + NT - 1) / NT;
+    const int c0 = lo + min(len, tid * chunk), c1 = lo + min(len, (tid + 1) * chunk);
+    int gt = 0, eq = 0;
+    for (int e = c0; e < c1; ++e) {
+      bool c;
+      const uint32_t u = key_of(e, c);
+      if (c) { gt += u > prefix; eq += u == prefix; }
+    }
+    int t2 = 0;
+    const int eq_before = block_scan(eq, t2);
+    const int take = max(0, min(eq, remaining - eq_before));
+    const int off = block_scan(gt + take, t2);
+    const int base = sm.nsel[i];
+    int* g = gsel_base + i * a.sel_stride + 1 + base + off;
+    int w = 0, te = 0;
+    bool anyk = false;
+    for (int e = c0; e < c1; ++e) {
+      bool c;
+      const uint32_t u = key_of(e, c);
+      const bool tk = c && (u > prefix || (u == prefix && te++ < take));
+      if (tk) {
+        g[w] = e;
+        if (base + off + w < kRSel) sm.sel[i][base + off + w] = e;
+        ++w;
+        anyk |= e < KG;
+      }
+    }
+    if (anyk) sm.any_k = 1;
+    __syncthreads();
+    if (tid == 0) sm.nsel[i] = base + t2;
+    __syncthreads();
+  };
   auto pick = [&](int i, int lo, int hi, int k) {
     if (k <= 0 || hi <= lo) return;
+    if (k > kRSel) {
+      pick_large(i, lo, hi, k);
+      return;
+    }
     const float* row = sc + i * NG;
     // ── prefilter: tau = min over warps of each warp's r-th best lane
     // maximum, r = ceil(k / NW); the r best lanes of every warp hold
@@ -773,11 +896,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       if (score_v) pick(i, KG, NG, bv);
     }
   }
-  if (tid < QN) {
-    int* so = a.sel_out + (static_cast<int64_t>(bh) * QN + tid) * (kRSel + 1);
-    so[0] = sm.nsel[tid];
-    for (int k = 0; k < sm.nsel[tid]; ++k) so[1 + k] = sm.sel[tid][k];
-  }
+  if (tid < QN) gsel_base[tid * a.sel_stride] = sm.nsel[tid];
   if (scores_in_smem) {
     float* g = a.scores + static_cast<int64_t>(bh) * QN * NG;
     for (int e = tid; e < QN * NG; e += NT) g[e] = sc[e];
@@ -814,110 +933,35 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   int n_batches = 0;    // batches staged so far (mbarrier phase)
   bool stg_failed = false;
   for (int i = 0; i < QN; ++i) {
-    // selected K pages (the first selection of a page leads it) and V slots,
-    // with the per-item scalars (one round trip)
-    if (warp == 0) {
-      const int nsel = sm.nsel[i];
-      const int e = lane < nsel ? sm.sel[i][lane] : -1;
-      const bool isk = e >= 0 && e < KG, isv = e >= KG;
-      const int p = isk ? e / d.SK : -1;
-      const int e_lo = isk ? p * d.SK : 0, e_hi = isk ? e_lo + d.SK : 0;   // the page's K entries
-      bool leader = isk;
-      int msk = 0;
-      for (int k = 0; k < nsel; ++k) {
-        const int ek = sm.sel[i][k];
-        if (ek >= e_lo && ek < e_hi) {
-          if (k < lane) leader = false;
-          msk |= 1 << (ek - e_lo);
+    const int n_all = sm.nsel[i];
+    // more than kRSel selected entries: the apply runs in rounds over the
+    // list in the workspace (index order), each round's items in the tables
+    const bool multi = n_all > kRSel;
+    const int* gl = gsel_base + i * a.sel_stride + 1;
+    // end of the round starting at r0: at most kRSel entries, never splitting
+    // the K entries of one page (adjacent in an index-ordered list)
+    auto round_end = [&](int r0) -> int {
+      int r1 = min(n_all, r0 + kRSel);
+      if (multi && r1 < n_all) {
+        const int en = gl[r1];
+        if (en < KG) {
+          while (r1 > r0 + 1) {
+            const int ep = gl[r1 - 1];
+            if (ep < KG && ep / d.SK == en / d.SK) --r1;
+            else break;
+          }
         }
       }
-      const unsigned lt = (1u << lane) - 1u;
-      const unsigned bl = __ballot_sync(0xffffffffu, leader);
-      const unsigned bv = __ballot_sync(0xffffffffu, isv);
-      const unsigned bk = __ballot_sync(0xffffffffu, isk);
-      const int nkp_w = __popc(bl);
-      if (leader) {
-        const int u = __popc(bl & lt);
-        const int64_t pg = lhp * d.P + p;
-        sm.kp_page[u] = p;
-        sm.kp_mask[u] = msk;
-        sm.kp_nv[u] = a.cache.valid[pg];
-        sm.kp_vm[u] = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
-      }
-      if (isv) {
-        const int v = __popc(bv & lt), ev = e - KG;
-        const int pv = ev / d.SV, j = ev % d.SV;
-        const int64_t pg = lhp * d.P + pv;
-        sm.vsel[v] = ev;
-        const int vb = a.cache.v_slot_block[pg * d.SV + j];
-        const int t0 = vb * d.vtb;
-        sm.vs_t0[v] = t0;
-        sm.vs_t1[v] = min(t0 + d.vtb, a.cache.valid[pg]);
-        sm.vs_rs[v] = f16_bits_to_f32(a.cache.v_slot_scale[pg * d.SV + j]);
-      }
-      if (lane == 0) {
-        sm.nkp = nkp_w;
-        sm.nvs = __popc(bv);
-        reads_k += __popc(bk);
-        reads_v += __popc(bv);
-      }
-    }
-    __syncthreads();
-    const int nkp = sm.nkp, nvs = sm.nvs, nit = nkp + nvs;
-    // batch plan: item -> staging offset, batch boundaries
-    if (tid == 0) {
-      int off = 0, nb = 0;
-      sm.bnd[0] = 0;
-      for (int it = 0; it < nit; ++it) {
-        const int sz = it < nkp ? k_item_b : v_item_b;
-        if (off + sz > kRStg) {
-          sm.bnd[++nb] = it;
-          off = 0;
-        }
-        sm.ioff[it] = off;
-        off += sz;
-      }
-      sm.bnd[++nb] = nit;
-      sm.nb = nb;
-    }
-    __syncthreads();
-    const int nb = sm.nb;
-    // bulk copies of batch `bt` by the lanes of warp 0 (item per lane)
-    auto stage_batch = [&](int bt) {
-      if (!bulk || warp != 0) return;
-      const int lo = sm.bnd[bt], hi = sm.bnd[bt + 1];
-      uint32_t bytes = 0;
-      for (int it = lo; it < hi; ++it) bytes += it < nkp ? k_item_b : v_item_b;
-      if (lane == 0) mbar_expect_tx(&sm.stg_bar, bytes);
-      __syncwarp();
-      for (int it = lo + lane; it < hi; it += 32) {
-        uint8_t* dst = sm.stg + sm.ioff[it];
-        fence_proxy_async();
-        if (it < nkp) {
-          const int p = sm.kp_page[it];
-          const int64_t pg = lhp * d.P + p;
-          bulk_g2s(dst, a.cache.v_codes + pg * k_codes_b, k_codes_b, &sm.stg_bar);
-          bulk_g2s(dst + k_codes_b, reinterpret_cast<const uint8_t*>(a.cache.v_scale) + pg * k_sc_b, k_sc_b, &sm.stg_bar);
-          bulk_g2s(dst + k_codes_b + k_sc_b, Wb + i * sst + p * kPage, kPage * 4, &sm.stg_bar);
-        } else {
-          const int ev = sm.vsel[it - nkp];
-          const int pv = ev / d.SV, j = ev % d.SV;
-          const int64_t pg = lhp * d.P + pv;
-          bulk_g2s(dst, a.cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes, d.vslot_bytes, &sm.stg_bar);
-          bulk_g2s(dst + d.vslot_bytes, Wb + i * sst + pv * kPage, kPage * 4, &sm.stg_bar);
-        }
-      }
+      return r1;
     };
-    stage_batch(0);
-    // wK per (selected K page, token): q . R_K summed over the page's selected groups
-    for (int x = tid; x < nkp * kPage; x += NT) {
-      const int u = x / kPage, t = x % kPage;
-      const int64_t pg = lhp * d.P + sm.kp_page[u];
+    // wK of token t of page p: q . R_K summed over the selected slots in mask
+    auto wk_of = [&](int p, int mask, int t) -> float {
+      const int64_t pg = lhp * d.P + p;
       float acc = 0.f;
       for (int j = 0; j < d.SK; ++j) {
-        if (!((sm.kp_mask[u] >> j) & 1)) continue;
+        if (!((mask >> j) & 1)) continue;
         if (a.kw != nullptr) {
-          acc += a.kw[((static_cast<int64_t>(bh) * QN + i) * KG + sm.kp_page[u] * d.SK + j) * kPage + tok_pos(t, a.s_perm)];
+          acc += a.kw[((static_cast<int64_t>(bh) * QN + i) * KG + p * d.SK + j) * kPage + tok_pos(t, a.s_perm)];
           continue;
         }
         const int grp = a.cache.k_slot_group[pg * d.SK + j];
@@ -933,28 +977,165 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         }
         acc += dot;
       }
-      sm.ds[u][t] = acc;
-    }
-    __syncthreads();
-    if (exact && warp == 0) {
-      float mx = -INFINITY;
-      int covered = 0;
-      for (int u = 0; u < nkp; ++u) {
-        const int nv = sm.kp_nv[u];
-        covered += nv;
-        if (lane < nv) mx = fmaxf(mx, __fdiv_rn(sm.ds[u][lane], a.sqrt_d));
+      return acc;
+    };
+    // selected K slots of page p anywhere in the list (warp-wide; multi-round
+    // lists, where a V slot's page may lead a K item of another round)
+    auto sel_kmask = [&](int p) -> int {
+      int m = 0;
+      for (int x = lane; x < n_all; x += 32) {
+        const int e = gl[x];
+        if (e < KG && e / d.SK == p) m |= 1 << (e - p * d.SK);
       }
-      mx = warp_max(mx);
-      if (lane == 0) sm.mshift = (nkp == 0) ? 0.f : (covered >= ntot ? mx : fmaxf(mx, 0.f));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m |= __shfl_xor_sync(0xffffffffu, m, o);
+      return m;
+    };
+    // tables of the round [r0, r1): selected K pages (the first selection of
+    // a page leads it) and V slots with the per-item scalars (one round
+    // trip), then wK per (selected K page, token)
+    auto load_round = [&](int r0, int r1, bool count_reads) {
+      if (warp == 0) {
+        const int nsel = r1 - r0;
+        if (multi) {
+          if (lane < nsel) sm.sel[i][lane] = gl[r0 + lane];
+          __syncwarp();
+        }
+        const int e = lane < nsel ? sm.sel[i][lane] : -1;
+        const bool isk = e >= 0 && e < KG, isv = e >= KG;
+        const int p = isk ? e / d.SK : -1;
+        const int e_lo = isk ? p * d.SK : 0, e_hi = isk ? e_lo + d.SK : 0;   // the page's K entries
+        bool leader = isk;
+        int msk = 0;
+        for (int k = 0; k < nsel; ++k) {
+          const int ek = sm.sel[i][k];
+          if (ek >= e_lo && ek < e_hi) {
+            if (k < lane) leader = false;
+            msk |= 1 << (ek - e_lo);
+          }
+        }
+        const unsigned lt = (1u << lane) - 1u;
+        const unsigned bl = __ballot_sync(0xffffffffu, leader);
+        const unsigned bv = __ballot_sync(0xffffffffu, isv);
+        const unsigned bk = __ballot_sync(0xffffffffu, isk);
+        const int nkp_w = __popc(bl);
+        if (leader) {
+          const int u = __popc(bl & lt);
+          const int64_t pg = lhp * d.P + p;
+          sm.kp_page[u] = p;
+          sm.kp_mask[u] = msk;
+          sm.kp_nv[u] = a.cache.valid[pg];
+          sm.kp_vm[u] = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
+        }
+        if (isv) {
+          const int v = __popc(bv & lt), ev = e - KG;
+          const int pv = ev / d.SV, j = ev % d.SV;
+          const int64_t pg = lhp * d.P + pv;
+          sm.vsel[v] = ev;
+          const int vb = a.cache.v_slot_block[pg * d.SV + j];
+          const int t0 = vb * d.vtb;
+          sm.vs_t0[v] = t0;
+          sm.vs_t1[v] = min(t0 + d.vtb, a.cache.valid[pg]);
+          sm.vs_rs[v] = f16_bits_to_f32(a.cache.v_slot_scale[pg * d.SV + j]);
+        }
+        if (lane == 0) {
+          sm.nkp = nkp_w;
+          sm.nvs = __popc(bv);
+          if (count_reads) {
+            reads_k += __popc(bk);
+            reads_v += __popc(bv);
+          }
+        }
+      }
+      __syncthreads();
+      __syncthreads();
+      for (int x = tid; x < sm.nkp * kPage; x += NT) {
+        const int u = x / kPage, t = x % kPage;
+        sm.ds[u][t] = wk_of(sm.kp_page[u], sm.kp_mask[u], t);
+      }
+      __syncthreads();
+    };
+    // exact form: shift by the largest ds over the valid tokens of every
+    // selected K page (all rounds)
+    float mshift = 0.f;
+    if (exact) {
+      float mx = -INFINITY;
+      int covered = 0, nkp_all = 0;
+      for (int q0 = 0; q0 < n_all;) {
+        const int q1 = round_end(q0);
+        load_round(q0, q1, !multi);
+        if (warp == 0) {
+          for (int u = 0; u < sm.nkp; ++u) {
+            const int nv = sm.kp_nv[u];
+            covered += nv;
+            if (lane < nv) mx = fmaxf(mx, __fdiv_rn(sm.ds[u][lane], a.sqrt_d));
+          }
+        }
+        nkp_all += sm.nkp;
+        q0 = q1;
+        __syncthreads();
+      }
+      if (warp == 0) {
+        mx = warp_max(mx);
+        if (lane == 0) sm.mshift = (nkp_all == 0) ? 0.f : (covered >= ntot ? mx : fmaxf(mx, 0.f));
+      }
+      __syncthreads();
+      mshift = sm.mshift;
     }
-    __syncthreads();
-    const float mshift = exact ? sm.mshift : 0.f;
     const float cbase = exact ? expf(-mshift) : 1.f;
-    // numerator sum_S cf * V_hat + sum_V cf * R_V and z = sum over K tokens of cf:
-    // exact  dO = (cbase O + num) / (cbase + z) - O,   linear  dO = num - z O
     float num[4] = {0.f, 0.f, 0.f, 0.f};   // channel lane + 32 jj (per-channel decode)
     float acc8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // channels 8 wl + j (word decode)
     float zp = 0.f;
+    for (int r0 = 0; r0 < n_all;) {
+      const int r1 = round_end(r0);
+      if (r0 > 0) __syncthreads();   // every warp is done with the previous round's tables
+      if (multi || !exact) load_round(r0, r1, true);   // a single round is loaded by the exact pass
+      const int nkp = sm.nkp, nvs = sm.nvs, nit = nkp + nvs;
+      // batch plan: item -> staging offset, batch boundaries
+      if (tid == 0) {
+        int off = 0, nb = 0;
+        sm.bnd[0] = 0;
+        for (int it = 0; it < nit; ++it) {
+          const int sz = it < nkp ? k_item_b : v_item_b;
+          if (off + sz > kRStg) {
+            sm.bnd[++nb] = it;
+            off = 0;
+          }
+          sm.ioff[it] = off;
+          off += sz;
+        }
+        sm.bnd[++nb] = nit;
+        sm.nb = nb;
+      }
+      __syncthreads();
+      const int nb = sm.nb;
+      // bulk copies of batch `bt` by the lanes of warp 0 (item per lane)
+      auto stage_batch = [&](int bt) {
+        if (!bulk || warp != 0) return;
+        const int lo = sm.bnd[bt], hi = sm.bnd[bt + 1];
+        uint32_t bytes = 0;
+        for (int it = lo; it < hi; ++it) bytes += it < nkp ? k_item_b : v_item_b;
+        if (lane == 0) mbar_expect_tx(&sm.stg_bar, bytes);
+        __syncwarp();
+        for (int it = lo + lane; it < hi; it += 32) {
+          uint8_t* dst = sm.stg + sm.ioff[it];
+          fence_proxy_async();
+          if (it < nkp) {
+            const int p = sm.kp_page[it];
+            const int64_t pg = lhp * d.P + p;
+            bulk_g2s(dst, a.cache.v_codes + pg * k_codes_b, k_codes_b, &sm.stg_bar);
+            bulk_g2s(dst + k_codes_b, reinterpret_cast<const uint8_t*>(a.cache.v_scale) + pg * k_sc_b, k_sc_b, &sm.stg_bar);
+            bulk_g2s(dst + k_codes_b + k_sc_b, Wb + i * sst + p * kPage, kPage * 4, &sm.stg_bar);
+          } else {
+            const int ev = sm.vsel[it - nkp];
+            const int pv = ev / d.SV, j = ev % d.SV;
+            const int64_t pg = lhp * d.P + pv;
+            bulk_g2s(dst, a.cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes, d.vslot_bytes, &sm.stg_bar);
+            bulk_g2s(dst + d.vslot_bytes, Wb + i * sst + pv * kPage, kPage * 4, &sm.stg_bar);
+          }
+        }
+      };
+      stage_batch(0);
     for (int bt = 0; bt < nb; ++bt) {
       if (bt > 0) {
         __syncthreads();   // every warp is done with the previous batch
@@ -1044,6 +1225,8 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           const float rs = sm.vs_rs[v];
           int u = -1;
           for (int x = 0; x < nkp; ++x) if (sm.kp_page[x] == p) u = x;
+          // the page's selected K slots led by an item of another round
+          const int omask = (exact && multi && u < 0) ? sel_kmask(p) : 0;
           if (lane < d.vtb) {
             const int t = t0 + lane;
             float cf = 0.f;
@@ -1051,7 +1234,8 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
               const float A = attw(srow[tok_pos(t, a.s_perm)], i);
               float w = 1.f;
               if (exact) {
-                const float dsv = u >= 0 ? __fdiv_rn(sm.ds[u][t], a.sqrt_d) : 0.f;
+                const float dsv = u >= 0 ? __fdiv_rn(sm.ds[u][t], a.sqrt_d)
+                                         : (omask ? __fdiv_rn(wk_of(p, omask, t), a.sqrt_d) : 0.f);
                 w = dsv <= 80.f ? cbase * expf(dsv) : expf(dsv - mshift);
               }
               cf = A * w;
@@ -1065,6 +1249,9 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         }
         __syncwarp();
       }
+    }
+      if (stg_failed) break;
+      r0 = r1;
     }
     if (stg_failed) {
       // the staging copies did not land in time: flag it, let the copies in

@@ -214,7 +214,9 @@ class DecodeEngine:
         self.cache.lengths[b][layer] += 1
 
     # ── parity readback (tests) ───────────────────────────────────────
-    MAX_SEL = 32
+    def _sel_stride(self, pages: int) -> int:
+        cfg = self.cache.ccfg
+        return 1 + pages * (cfg.k_slots_per_page + cfg.v_slots_per_page)
 
     def last_selection(self, layer: int, seq_begin: int, seq_count: int, pages: int, cache_seq: Optional[int] = None):
         """Selected slots of the last attend(): {(seq, kv_head, query): [(kind, page, group), ...]}.
@@ -228,7 +230,8 @@ class DecodeEngine:
         cfg = self.cache.ccfg
         qn = cfg.num_heads // cfg.num_kv_heads
         n_bh = seq_count * cfg.num_kv_heads
-        sel = self._ws[: n_bh * qn * (self.MAX_SEL + 1) * 4].view(torch.int32).view(n_bh, qn, self.MAX_SEL + 1)
+        stride = self._sel_stride(pages)
+        sel = self._ws[: n_bh * qn * stride * 4].view(torch.int32).view(n_bh, qn, stride)
         sel = sel.cpu()
         SK, SV = cfg.k_slots_per_page, cfg.v_slots_per_page
         KG = pages * SK
@@ -256,7 +259,7 @@ class DecodeEngine:
         cfg = self.cache.ccfg
         qn = cfg.num_heads // cfg.num_kv_heads
         n_bh = seq_count * cfg.num_kv_heads
-        off = (n_bh * qn * (self.MAX_SEL + 1) * 4 + 255) // 256 * 256   # regions are 256-byte aligned
+        off = (n_bh * qn * self._sel_stride(pages) * 4 + 255) // 256 * 256   # regions are 256-byte aligned
         ng = pages * (cfg.k_slots_per_page + cfg.v_slots_per_page)
         return self._ws[off: off + n_bh * qn * ng * 4].view(torch.float32).view(n_bh, qn, ng).clone()
 

@@ -120,7 +120,11 @@ typedef struct carekv_store_params {
                                  * master 0, so its rows read back as 0 (the
                                  * reference, cache.py:689-695); 1 = its first
                                  * appended row sets the master (max scale / 127,
-                                 * as write_base does, cache.py:592-606)        */
+                                 * as write_base does, cache.py:592-606); later
+                                 * rows keep it, so a later group scale above
+                                 * 127 x master saturates at int8 code 127 and
+                                 * that row reads back clipped (write_base takes
+                                 * the largest scale of the whole page)         */
 } carekv_store_params_t;
 
 /* Per-call routing / correction policy (attention.py:576-957,
@@ -223,8 +227,8 @@ int carekv_decode_workspace_bytes(const carekv_config_t *cfg, int32_t seq_count,
  * pages plus the routed residual correction.  q, out: [seq_count][num_heads][D]
  * in `dtype`.  The workspace must hold carekv_decode_workspace_bytes.
  * sketch_proj ([k_channel_group][sketch_dim] fp32) is read only by the
- * sketch proxy score (params->kscore_live == 0).  At most 32 slots may be
- * selected per query (absolute budgets, or the worst case of ratio budgets).
+ * sketch proxy score (params->kscore_live == 0).  Any read budget is served:
+ * selections of more than 32 slots per query are applied in rounds.
  * Replaces CAREKVMultiHeadAttention.forward (attention.py:1042-1077) with
  * vectorized_joint_correction applied to each kv head's query group. */
 int carekv_decode_attention(const carekv_config_t *cfg, const carekv_cache_t *cache, int32_t layer,
@@ -238,7 +242,12 @@ int carekv_decode_attention(const carekv_config_t *cfg, const carekv_cache_t *ca
  * batch runs in CAREKV_ATTEND_CHUNKS (environment, 1 / 2 / 4, default 2)
  * chunks on prioritised streams forked from the caller's stream and joined
  * back into it (events, so stream capture records them), routing of one
- * chunk overlapping the split-K pass of the next. */
+ * chunk overlapping the split-K pass of the next.  The helper streams and
+ * events belong to the calling host thread (one set per thread and device,
+ * created by its first call outside stream capture; a thread whose first
+ * call is captured runs that call unchunked), so several host threads may
+ * call concurrently on one device, and one thread may capture while others
+ * run uncaptured calls. */
 int carekv_decode_attention_launches(const carekv_config_t *cfg, int32_t seq_count, int32_t *launches);
 
 /* Decode attention for callers that cannot allocate device memory.
@@ -260,8 +269,19 @@ int carekv_decode_attention_launches(const carekv_config_t *cfg, int32_t seq_cou
  * CAREKV_ERR_WORKSPACE without running anything.  All calls share the one
  * array: no part of it needs clearing between calls, but calls that may
  * overlap on the GPU race on it, so the caller must serialise them.  The call
- * allocates nothing. */
-#define CAREKV_NOALLOC_MAX_BYTES ((size_t)32 << 20)
+ * allocates nothing.
+ *
+ * Which shapes fit: with S sequences, H kv heads, QN query heads per kv head,
+ * P = max_pages_used and SK / SV slots per page, the scratch is about
+ *   S*H*QN*P*(8*(SK+SV) + 64 + 64*SK) bytes
+ * (selection readback and scores, logits, q . R_K of the stored K slots)
+ * plus the split-K partials, S*H*splits*QN*(head_dim+2)*4 bytes.  Examples:
+ * 32 sequences x 32 kv heads x 4096-token context (P = 264, SK = SV = 1,
+ * QN = 1, Llama-2-7B shape) need 37.6 MiB and fit; 16 sequences x 8 kv
+ * heads x 4 query heads x 32768 tokens (P = 2056, Mistral-7B shape) need
+ * 147 MiB and are rejected, while one kv head of that batch (a shard of
+ * one kv head per GPU) needs 19.1 MiB and fits. */
+#define CAREKV_NOALLOC_MAX_BYTES ((size_t)64 << 20)
 int carekv_decode_attention_noalloc(const carekv_config_t *cfg, const carekv_cache_t *cache,
                                     int32_t layer, const void *q, void *out, int32_t dtype,
                                     int32_t seq_begin, int32_t seq_count, int32_t max_pages_used,

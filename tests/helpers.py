@@ -192,3 +192,20 @@ def selection_margin(info, q, qn_total=None):
     if k <= 0 or k >= s.size:
         return math.inf
     return float(s[k - 1] - s[k]) / max(abs(float(s[k - 1])), 1e-30)
+
+
+def classify_selection(got, want, info, q, tie_margin=1e-5):
+    """Compare one query's selected (kind, page, group) set with the oracle's.
+
+    Returns "equal" for identical sets, "tie" when they differ only where
+    the normalised scores at the cut are within tie_margin (a tie within
+    fp32 accumulation order), "saturated" when they differ on a query whose
+    attention is saturated in fp32 (saturated_attention), and "mismatch"
+    otherwise."""
+    if sorted(got) == sorted(want):
+        return "equal"
+    if selection_margin(info, q) < tie_margin:
+        return "tie"
+    if saturated_attention(info, q):
+        return "saturated"
+    return "mismatch"

@@ -33,8 +33,9 @@ def _decode_page(pkg, flag):
         g = torch.Generator(device=dev).manual_seed(3)
         eng.prefill_store(0, torch.randn(1, H, 16, D, device=dev, generator=g),
                           torch.randn(1, H, 16, D, device=dev, generator=g))   # one full page
-        rows = [(torch.randn(1, H, D, device=dev, generator=g), torch.randn(1, H, D, device=dev, generator=g))
-                for _ in range(3)]
+        # row 1 is smaller than row 0, row 2 an outlier 8x larger
+        rows = [(torch.randn(1, H, D, device=dev, generator=g) * f, torch.randn(1, H, D, device=dev, generator=g) * f)
+                for f in (1.0, 0.5, 8.0)]
         for k, v in rows:                        # the first append opens page 1
             eng.append(0, k, v)
         out = eng.attend(0, torch.randn(1, H, D, device=dev, generator=g))
@@ -49,19 +50,31 @@ def _decode_page(pkg, flag):
             vh = Vc.float() * Vs.float().repeat_interleave(D // G, dim=1)
             k_in = torch.stack([r[0][0, h] for r in rows]).float()
             v_in = torch.stack([r[1][0, h] for r in rows]).float()
-            res.append((kh, vh, k_in, v_in))
+            km = cache.view("k_master")[0, 0, h, 1].float().item()
+            vm = cache.view("v_master")[0, 0, h, 1].float().item()
+            res.append((kh, vh, k_in, v_in, km, vm))
         return res
 
 
 def test_decode_opened_page_reads_zero_by_default(pkg):
-    for kh, vh, _, _ in _decode_page(pkg, "0"):
+    for kh, vh, *_ in _decode_page(pkg, "0"):
         assert torch.count_nonzero(kh) == 0 and torch.count_nonzero(vh) == 0
 
 
 def test_decode_page_master_flag(pkg):
-    for kh, vh, k_in, v_in in _decode_page(pkg, "1"):
-        for got, want in ((kh, k_in), (vh, v_in)):
+    for kh, vh, k_in, v_in, km, vm in _decode_page(pkg, "1"):
+        for got, want, m in ((kh, k_in, km), (vh, v_in, vm)):
+            assert m > 0
             assert torch.count_nonzero(got, dim=1).min() > 0
-            # the first row's own master: INT3 group quantization error only
-            rel = (got[0] - want[0]).norm() / want[0].norm()
-            assert rel < 0.4, rel
+            # rows 0 and 1 fit the master set by row 0: INT3 group
+            # quantization error only
+            for r in (0, 1):
+                rel = (got[r] - want[r]).norm() / want[r].norm()
+                assert rel < 0.4, (r, rel)
+            # row 2's group scales exceed 127 x master: its int8 scale codes
+            # saturate at 127, so it reads back clipped to 3 x 127 x master
+            lim = 3 * 127 * m * (1 + 2e-3)
+            assert got[2].abs().max().item() <= lim
+            assert want[2].abs().max().item() > lim
+            rel2 = (got[2] - want[2]).norm() / want[2].norm()
+            assert rel2 > 0.4, rel2

@@ -54,3 +54,20 @@ def test_single_rank_passthrough():
     import bench
     assert bench.max_over_ranks([1.0, 2.0], 1) == [1.0, 2.0]
     assert bench.aggregate_tok_s(1, 32, 20, 100.0) == pytest.approx(6400.0)
+
+
+def test_rank_batch_partition():
+    """Strong scaling: the global batch splits into contiguous, disjoint
+    shares that cover it; weak scaling gives every rank a full batch."""
+    import bench
+    for world in (1, 2, 4, 8):
+        owned = []
+        for r in range(world):
+            s0, n = bench.rank_batch(32, world, r, "strong")
+            assert n == 32 // world
+            owned += list(range(s0, s0 + n))
+        assert owned == list(range(32))
+        assert bench.aggregate_tok_s(world, 32 // world, 10, 100.0) == pytest.approx(3200.0)
+    assert bench.rank_batch(32, 4, 2, "weak") == (64, 32)
+    with pytest.raises(ValueError):
+        bench.rank_batch(32, 3, 0, "strong")
