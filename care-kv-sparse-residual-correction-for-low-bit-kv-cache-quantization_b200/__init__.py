@@ -5,7 +5,7 @@ HF-patch surface on the decode path, backed by hand-written sm_100a CUDA
 kernels in lib/libcarekv_b200.so (C ABI: include/carekv_b200.h).
 """
 
-from . import _lib
+from . import _lib, partition
 from .config import (CacheConfig, apply_carekv_env_overrides, layer_budget_multiplier,
                      resolve_route_params, resolve_store_params, k_correction_mode)
 from .cache import CAREKVCache, PageMeta

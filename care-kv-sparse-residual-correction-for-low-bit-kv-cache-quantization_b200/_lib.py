@@ -62,6 +62,10 @@ class RouteParams(ctypes.Structure):
                 ("lambda_k", f32), ("lambda_v", f32)]
 
 
+class Shard(ctypes.Structure):
+    _fields_ = [("kvh_begin", i32), ("kvh_total", i32)]
+
+
 # (name, restype, argtypes) of every exported symbol declared in the header
 SIGNATURES = [
     ("carekv_abi_version", i32, []),
@@ -91,6 +95,13 @@ SIGNATURES = [
                                         ctypes.c_size_t, vp]),
     ("carekv_decode_attention_noalloc", i32, [ctypes.POINTER(Config), ctypes.POINTER(Cache), i32, vp, vp, i32, i32,
                                               i32, i32, ctypes.POINTER(RouteParams), vp, vp]),
+    ("carekv_prefill_store_shard", i32, [ctypes.POINTER(Config), ctypes.POINTER(Cache), i32, vp, vp, i32, i32, i32,
+                                         ctypes.POINTER(StoreParams), vp, ctypes.POINTER(Shard), vp]),
+    ("carekv_append_shard", i32, [ctypes.POINTER(Config), ctypes.POINTER(Cache), i32, vp, vp, i32, i32,
+                                  ctypes.POINTER(StoreParams), vp, i32, ctypes.POINTER(Shard), vp]),
+    ("carekv_decode_attention_shard", i32, [ctypes.POINTER(Config), ctypes.POINTER(Cache), i32, vp, vp, i32, i32,
+                                            i32, i32, ctypes.POINTER(RouteParams), vp, vp, ctypes.c_size_t,
+                                            ctypes.POINTER(Shard), vp]),
 ]
 NOALLOC_MAX_BYTES = 64 << 20
 

@@ -62,6 +62,17 @@ int validate_dtype(int32_t dt) {
 
 int cuda_status(cudaError_t e) { return e == cudaSuccess ? CAREKV_OK : CAREKV_ERR_CUDA; }
 
+// A kv-head shard: the arena's kv heads are [kvh_begin, kvh_begin + H) of a
+// model with kvh_total kv heads.
+int validate_shard(const carekv_config_t* c, const carekv_shard_t* sh) {
+  if (sh == nullptr || sh->kvh_begin < 0 || sh->kvh_total < c->num_kv_heads ||
+      sh->kvh_begin + c->num_kv_heads > sh->kvh_total)
+    return CAREKV_ERR_INVALID_ARG;
+  return CAREKV_OK;
+}
+
+int64_t act_bytes(int32_t dt) { return dt == CAREKV_F32 ? 4 : 2; }
+
 #define CHECK(x)                      \
   do {                                \
     const int _s = (x);               \
@@ -215,27 +226,53 @@ int carekv_prefill_store(const carekv_config_t* cfg, const carekv_cache_t* cache
                          const void* V, int32_t T, int32_t seq_begin, int32_t seq_count,
                          const carekv_store_params_t* params, const float* sketch_proj, void* stream) {
   CHECK(validate_config(cfg));
+  const carekv_shard_t whole = {0, cfg->num_kv_heads};
+  return carekv_prefill_store_shard(cfg, cache, layer, K, V, T, seq_begin, seq_count, params, sketch_proj, &whole,
+                                    stream);
+}
+
+int carekv_prefill_store_shard(const carekv_config_t* cfg, const carekv_cache_t* cache, int32_t layer,
+                               const void* K, const void* V, int32_t T, int32_t seq_begin, int32_t seq_count,
+                               const carekv_store_params_t* params, const float* sketch_proj,
+                               const carekv_shard_t* shard, void* stream) {
+  CHECK(validate_config(cfg));
+  CHECK(validate_shard(cfg, shard));
   CHECK(validate_cache(cfg, cache));
   CHECK(validate_range(cache, layer, seq_begin, seq_count, cfg));
   CHECK(validate_store_params(cfg, params));
   if (T < 0 || (T > 0 && (!K || !V))) return CAREKV_ERR_INVALID_ARG;
   if ((T + kPage - 1) / kPage > cfg->max_pages) return CAREKV_ERR_CACHE_FULL;
   if (cfg->sketch_dim > 0 && cache->k_sketch && !sketch_proj) return CAREKV_ERR_INVALID_ARG;
-  return cuda_status(launch_prefill_store(*cfg, *cache, layer, K, V, T, seq_begin, seq_count, *params, sketch_proj,
-                                          as_stream(stream)));
+  const int64_t off = static_cast<int64_t>(shard->kvh_begin) * T * cfg->head_dim * act_bytes(params->input_dtype);
+  return cuda_status(launch_prefill_store(*cfg, *cache, layer, static_cast<const char*>(K) + off,
+                                          static_cast<const char*>(V) + off, T, seq_begin, seq_count, *params,
+                                          sketch_proj, shard->kvh_total, as_stream(stream)));
 }
 
 int carekv_append(const carekv_config_t* cfg, const carekv_cache_t* cache, int32_t layer, const void* k,
                   const void* v, int32_t seq_begin, int32_t seq_count, const carekv_store_params_t* params,
                   const float* sketch_proj, int32_t may_fill_page, void* stream) {
   CHECK(validate_config(cfg));
+  const carekv_shard_t whole = {0, cfg->num_kv_heads};
+  return carekv_append_shard(cfg, cache, layer, k, v, seq_begin, seq_count, params, sketch_proj, may_fill_page,
+                             &whole, stream);
+}
+
+int carekv_append_shard(const carekv_config_t* cfg, const carekv_cache_t* cache, int32_t layer, const void* k,
+                        const void* v, int32_t seq_begin, int32_t seq_count, const carekv_store_params_t* params,
+                        const float* sketch_proj, int32_t may_fill_page, const carekv_shard_t* shard,
+                        void* stream) {
+  CHECK(validate_config(cfg));
+  CHECK(validate_shard(cfg, shard));
   CHECK(validate_cache(cfg, cache));
   CHECK(validate_range(cache, layer, seq_begin, seq_count, cfg));
   CHECK(validate_store_params(cfg, params));
   if (seq_count > 0 && (!k || !v)) return CAREKV_ERR_INVALID_ARG;
   if (cfg->sketch_dim > 0 && cache->k_sketch && !sketch_proj) return CAREKV_ERR_INVALID_ARG;
-  return cuda_status(launch_append(*cfg, *cache, layer, k, v, seq_begin, seq_count, *params, sketch_proj,
-                                   may_fill_page != 0, as_stream(stream)));
+  const int64_t off = static_cast<int64_t>(shard->kvh_begin) * cfg->head_dim * act_bytes(params->input_dtype);
+  return cuda_status(launch_append(*cfg, *cache, layer, static_cast<const char*>(k) + off,
+                                   static_cast<const char*>(v) + off, seq_begin, seq_count, *params, sketch_proj,
+                                   may_fill_page != 0, shard->kvh_total, as_stream(stream)));
 }
 
 int carekv_decode_workspace_bytes(const carekv_config_t* cfg, int32_t seq_count, int32_t max_pages_used,
@@ -251,6 +288,18 @@ int carekv_decode_attention(const carekv_config_t* cfg, const carekv_cache_t* ca
                             const carekv_route_params_t* params, const float* sketch_proj, void* workspace,
                             size_t workspace_bytes_, void* stream) {
   CHECK(validate_config(cfg));
+  const carekv_shard_t whole = {0, cfg->num_kv_heads};
+  return carekv_decode_attention_shard(cfg, cache, layer, q, out, dtype, seq_begin, seq_count, max_pages_used,
+                                       params, sketch_proj, workspace, workspace_bytes_, &whole, stream);
+}
+
+int carekv_decode_attention_shard(const carekv_config_t* cfg, const carekv_cache_t* cache, int32_t layer,
+                                  const void* q, void* out, int32_t dtype, int32_t seq_begin, int32_t seq_count,
+                                  int32_t max_pages_used, const carekv_route_params_t* params,
+                                  const float* sketch_proj, void* workspace, size_t workspace_bytes_,
+                                  const carekv_shard_t* shard, void* stream) {
+  CHECK(validate_config(cfg));
+  CHECK(validate_shard(cfg, shard));
   CHECK(validate_cache(cfg, cache));
   CHECK(validate_range(cache, layer, seq_begin, seq_count, cfg));
   CHECK(validate_dtype(dtype));
@@ -266,8 +315,11 @@ int carekv_decode_attention(const carekv_config_t* cfg, const carekv_cache_t* ca
   if (seq_count == 0 || max_pages_used == 0) {
     if (seq_count == 0) return CAREKV_OK;
   }
-  return decode_attention(*cfg, *cache, layer, q, out, dtype, seq_begin, seq_count, std::max(1, max_pages_used),
-                          *params, workspace, workspace_bytes_, sketch_proj, as_stream(stream));
+  const int qn = cfg->num_heads / cfg->num_kv_heads;
+  const int64_t off = static_cast<int64_t>(shard->kvh_begin) * qn * cfg->head_dim * act_bytes(dtype);
+  return decode_attention(*cfg, *cache, layer, static_cast<const char*>(q) + off, static_cast<char*>(out) + off, dtype,
+                          seq_begin, seq_count, std::max(1, max_pages_used), *params, workspace, workspace_bytes_,
+                          sketch_proj, shard->kvh_total * qn, as_stream(stream));
 }
 
 int carekv_prefill_workspace_bytes(const carekv_config_t* cfg, int32_t n_pos, int32_t max_pages_used,

@@ -35,7 +35,7 @@ __global__ void __launch_bounds__(128) decode_partial_kernel(DecodeArgs a) {
   const int64_t lhp = d.lhp(b, a.layer, h);
   const int np = min(a.cache.num_pages[lhp], a.p_used);
   const int p0 = split * a.pps, p1 = min(np, p0 + a.pps);
-  const int Hq = d.H * QN;
+  const int Hq = a.act_heads;   // query heads per activation row
 
   float q[QN][DPL];
 #pragma unroll
@@ -134,20 +134,27 @@ struct SplitPlan {
   int pps, n_splits;
 };
 
-// Pages per split so the CTA count fills whole waves of the split-K pass
-// (`slots` resident CTAs over the 148 SMs) while every CTA keeps at least 64
-// pages (16 per warp, enough to fill the staging pipeline); fewer splits win
-// ties.
+// Pages per split.  A CTA costs its pages plus a fixed overhead (query
+// operands, pipeline fill, partial merge; about kCtaOverheadPages pages of
+// streaming, fitted to measured call times), and the pass takes as many
+// waves as its CTAs fill `slots` resident CTAs over the 148 SMs:
+//   cost(ns) = waves(ns) * (pages per CTA + kCtaOverheadPages),
+// minimised over ns with at least 64 pages per CTA (16 per warp, enough to
+// fill the staging pipeline); fewer splits win ties.  A large batch (1024
+// (sequence, kv head) pairs of 264 pages) then runs one split, a small one
+// (128 pairs) four.
+constexpr int kCtaOverheadPages = 32;
 inline SplitPlan split_plan(int n_bh, int p_used, int slots) {
   int best_ns = 1;
-  double best = -1.0;
+  long long best = -1;
   for (int ns = 1; ns <= 32; ++ns) {
-    if (ns > 1 && (p_used + ns - 1) / ns < 64) break;
+    const int pps = (p_used + ns - 1) / ns;
+    if (ns > 1 && pps < 64) break;
     const long long total = static_cast<long long>(n_bh) * ns;
     const long long waves = (total + slots - 1) / slots;
-    const double eff = static_cast<double>(total) / static_cast<double>(waves * slots);
-    if (eff > best + 0.01) {
-      best = eff;
+    const long long cost = waves * (pps + kCtaOverheadPages);
+    if (best < 0 || cost < best) {
+      best = cost;
       best_ns = ns;
     }
   }
@@ -250,17 +257,19 @@ static cudaError_t launch_qn(DecodeArgs& a, cudaStream_t st, int n_bh) {
   return launch_route<QN>(a, st, n_bh);
 }
 
-// Batch chunking of decode attention.  The split-K pass is issue-bound and
-// the router latency-bound, so the batch is cut into `chunks` ranges of
-// sequences that run on separate streams: chunk c (c < chunks - 1) on an
-// internal stream of higher priority than chunk c + 1, the last chunk on
-// the caller's stream.  Routing a chunk then overlaps the split-K pass of the
-// later chunks, whose CTAs fill the SMs the router leaves idle.  Every chunk
+// Batch chunking of decode attention (optional; one chunk by default).  The
+// batch may be cut into `chunks` ranges of sequences that run on separate
+// streams: chunk c (c < chunks - 1) on an internal stream of higher priority
+// than chunk c + 1, the last chunk on the caller's stream, so routing a
+// chunk overlaps the split-K pass of the later chunks.  With the split-K
+// pass at its current rate one chunk is faster at the benchmark shape (227
+// vs 235 us per call at 32 sequences x 32 kv heads x 4096 tokens): the
+// chunks' narrower grids cost more than the overlap gains.  Every chunk
 // uses the split plan of one chunk and its slice of the one workspace layout
 // (all regions are indexed by (sequence, kv head)), so the workspace size
 // and the selection readback do not depend on the chunking.
 // Fork and join go through events, which stream capture records as graph
-// edges.  CAREKV_ATTEND_CHUNKS (1, 2 or 4; default 2) sets the count.
+// edges.  CAREKV_ATTEND_CHUNKS (1, 2 or 4; default 1) sets the count.
 // The helper streams and events belong to the calling host thread (one set
 // per device and thread), so concurrent calls from several threads, or a
 // capture on one thread while another thread runs uncaptured calls, never
@@ -293,8 +302,8 @@ thread_local ChunkStreams t_chunk[kMaxDev];
 int attend_chunks() {
   static const int n = [] {
     const char* e = std::getenv("CAREKV_ATTEND_CHUNKS");
-    const int v = e ? std::atoi(e) : 2;
-    return v == 1 || v == 2 || v == 4 ? v : 2;
+    const int v = e ? std::atoi(e) : 1;
+    return v == 1 || v == 2 || v == 4 ? v : 1;
   }();
   return n;
 }
@@ -342,7 +351,7 @@ int decode_attention_chunks(int seq_count) {
 int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* q,
                      void* out, int dtype, int seq_begin, int seq_count, int p_used,
                      const carekv_route_params_t& rp, void* ws, size_t ws_bytes, const float* sketch_proj,
-                     cudaStream_t st) {
+                     int act_heads, cudaStream_t st) {
   if (ws_bytes < workspace_bytes(cfg, seq_count, p_used)) return CAREKV_ERR_WORKSPACE;
   DecodeArgs a;
   a.cfg = cfg;
@@ -353,6 +362,7 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
   a.dt = dtype;
   a.seq_begin = seq_begin;
   a.qn = cfg.num_heads / cfg.num_kv_heads;
+  a.act_heads = act_heads;
   const int H = cfg.num_kv_heads;
   const SplitPlan sp = split_plan(chunk_size(seq_count) * H, p_used, pass_slots(choose_pass(cfg)));
   a.pps = sp.pps;
@@ -414,8 +424,8 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
     const int64_t bh0 = static_cast<int64_t>(s0) * H;
     DecodeArgs ac = a;
     ac.seq_begin = seq_begin + s0;
-    ac.q = static_cast<const char*>(q) + bh0 * qn * D * es;
-    ac.out = static_cast<char*>(out) + bh0 * qn * D * es;
+    ac.q = static_cast<const char*>(q) + static_cast<int64_t>(s0) * act_heads * D * es;
+    ac.out = static_cast<char*>(out) + static_cast<int64_t>(s0) * act_heads * D * es;
     ac.sel_out = a.sel_out + bh0 * qn * a.sel_stride;
     ac.scores = a.scores + bh0 * qn * NGs;
     ac.S = a.S + bh0 * qn * p_used * kPage;
@@ -468,6 +478,7 @@ int prefill_correction(const carekv_config_t& cfg, const carekv_cache_t& cache, 
   a.dt = dtype;
   a.seq_begin = 0;
   a.qn = cfg.num_heads / cfg.num_kv_heads;
+  a.act_heads = cfg.num_heads;
   a.pps = p_used;
   a.n_splits = 0;
   a.p_used = p_used;

@@ -13,6 +13,7 @@ struct DecodeArgs {
   int dt;
   int seq_begin;
   int qn;           // query heads per kv head
+  int act_heads;    // query heads per row of q / out (the model's, for a kv-head shard)
   int pps;          // pages per split
   int n_splits;
   int p_used;       // workspace page stride

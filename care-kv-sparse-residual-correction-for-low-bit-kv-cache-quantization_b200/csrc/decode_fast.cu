@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) decode_partial_int3(DecodeArgs
   const int pb = pa + qv + (warp < rv ? 1 : 0);
   const int G = d.G;                 // scale bytes per row
   const int gsz = d.gsize;
-  const int Hq = d.H * QN;
+  const int Hq = a.act_heads;   // query heads per activation row
 
   uint8_t* wsm = smem + warp * (kNS * SL::bytes);
   uint64_t* bar = bars[warp];

@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   const int qv = n_cta / kWarps, rv = n_cta % kWarps;
   const int pa = ca + warp * qv + min(warp, rv);
   const int pb = pa + qv + (warp < rv ? 1 : 0);
-  const int Hq = d.H * QN;
+  const int Hq = a.act_heads;   // query heads per activation row
   const int G = GC > 0 ? GC : d.G, SK = SKC > 0 ? SKC : d.SK;
   const bool kslot = a.kw != nullptr;
   const Geo g = geo(D, G, SK, kslot, BITS);

@@ -13,18 +13,21 @@ cudaError_t launch_unpack(const uint8_t* packed, int8_t* codes, int64_t rows, in
 cudaError_t launch_pack4(const float* x, uint8_t* packed, uint16_t* sc, int64_t n, int numel, cudaStream_t st);
 cudaError_t launch_unpack4(const uint8_t* packed, const uint16_t* sc, float* out, int64_t n, int numel,
                            cudaStream_t st);
+// in_H: kv heads per activation row of K / V (the model's, for a kv-head
+// shard; the pointers then start at the shard's first head)
 cudaError_t launch_prefill_store(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* K,
                                  const void* V, int T, int seq_begin, int seq_count,
-                                 const carekv_store_params_t& prm, const float* sketch_proj, cudaStream_t st);
+                                 const carekv_store_params_t& prm, const float* sketch_proj, int in_H,
+                                 cudaStream_t st);
 cudaError_t launch_append(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* k,
                           const void* v, int seq_begin, int seq_count, const carekv_store_params_t& prm,
-                          const float* sketch_proj, int may_fill, cudaStream_t st);
+                          const float* sketch_proj, int may_fill, int in_H, cudaStream_t st);
 cudaError_t launch_kivi_k(const void* x, void* out, int64_t n, int T, int D, int bits, int dt, cudaStream_t st);
 cudaError_t launch_kivi_v(const void* x, void* out, int64_t rows, int D, int bits, int dt, cudaStream_t st);
 int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* q,
                      void* out, int dtype, int seq_begin, int seq_count, int p_used,
                      const carekv_route_params_t& rp, void* ws, size_t ws_bytes, const float* sketch_proj,
-                     cudaStream_t st);
+                     int act_heads, cudaStream_t st);
 size_t workspace_bytes(const carekv_config_t& c, int seq_count, int p_used);
 void prepare_decode_streams();
 int decode_attention_chunks(int seq_count);   // batch chunks one decode attention call runs   // creates the chunk streams of the current device (not under capture)

@@ -49,6 +49,10 @@ __device__ __forceinline__ void bulk_g2s_pol(void* dst, const void* src, uint32_
 __device__ __forceinline__ void st_f2_pol(float* p, float x, float y, uint64_t pol) {
   asm volatile("st.global.L2::cache_hint.v2.f32 [%0], {%1, %2}, %3;" ::"l"(p), "f"(x), "f"(y), "l"(pol) : "memory");
 }
+// One arrival (release, CTA scope) on an mbarrier.
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -59,7 +63,9 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: false after ~2^31 cycles (about a second) without completion.
+// The clock is read only when the first test fails.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
     if (clock64() - t0 > (1ll << 31)) return false;

@@ -189,7 +189,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   const int s = bh / d.H, h = bh % d.H;
   const int b = PF && a.seq_fixed >= 0 ? a.seq_fixed : a.seq_begin + s;
   const int D = d.D;
-  const int Hq = d.H * QN;
+  const int Hq = a.act_heads;   // query heads per activation row
   const int64_t lhp = d.lhp(b, a.layer, h);
   const int np = min(a.cache.num_pages[lhp], a.p_used);
   const carekv_route_params_t& rp = a.rp;

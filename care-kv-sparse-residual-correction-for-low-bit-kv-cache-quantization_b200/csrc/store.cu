@@ -57,7 +57,7 @@ __device__ __forceinline__ bool al16(const void* p) { return (reinterpret_cast<u
 template <int MODE>
 __global__ void __launch_bounds__(256) page_store_kernel(
     carekv_config_t cfg, carekv_cache_t cache, int layer, const void* __restrict__ Kin,
-    const void* __restrict__ Vin, int T, int seq_begin, carekv_store_params_t prm,
+    const void* __restrict__ Vin, int T, int seq_begin, carekv_store_params_t prm, int in_H,
     const float* __restrict__ sketch_proj) {
   __shared__ StoreSmem sm;
   const Dims d = make_dims_p2(cfg);
@@ -84,7 +84,7 @@ __global__ void __launch_bounds__(256) page_store_kernel(
       return;
     }
     // stage rows; padded rows are zero (layer.py:262-271)
-    const int64_t base = ((static_cast<int64_t>(s) * d.H + h) * T + t0) * D;
+    const int64_t base = ((static_cast<int64_t>(s) * in_H + h) * T + t0) * D;
     const int esz = dt == CAREKV_F32 ? 4 : 2;
     if (al16(Kin) && al16(Vin) && (D * esz) % 16 == 0 && blockDim.x == kStoreThreads) {
       // 16-byte chunks of both pages (at most 4 per thread for D <= 128),
@@ -562,7 +562,7 @@ __global__ void __launch_bounds__(1024) slot_id_scan_kernel(carekv_config_t cfg,
 __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_cache_t cache, int layer,
                                                     const void* __restrict__ kin,
                                                     const void* __restrict__ vin, int seq_begin,
-                                                    carekv_store_params_t prm) {
+                                                    carekv_store_params_t prm, int in_H) {
   const Dims d = make_dims_p2(cfg);
   const int lane = threadIdx.x;
   const int lgGs = __ffs(d.gsize) - 1, lgG = __ffs(d.G) - 1;   // powers of two (cache init)
@@ -576,7 +576,7 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
   __shared__ int sh_p, sh_off;
 
   // the new rows first: their loads do not depend on the page state
-  const int64_t src = (static_cast<int64_t>(s) * d.H + h) * D;
+  const int64_t src = (static_cast<int64_t>(s) * in_H + h) * D;
   for (int c = lane; c < D; c += 32) {
     xs[0][c] = load_act(kin, src + c, dt);
     xs[1][c] = load_act(vin, src + c, dt);
@@ -717,11 +717,12 @@ namespace carekv {
 
 cudaError_t launch_prefill_store(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* K,
                                  const void* V, int T, int seq_begin, int seq_count,
-                                 const carekv_store_params_t& prm, const float* sketch_proj, cudaStream_t st) {
+                                 const carekv_store_params_t& prm, const float* sketch_proj, int in_H,
+                                 cudaStream_t st) {
   const int n_new = (T + kPage - 1) / kPage;
   if (n_new == 0 || seq_count == 0) return cudaSuccess;
   dim3 grid(n_new, cfg.num_kv_heads, seq_count);
-  page_store_kernel<0><<<grid, 256, 0, st>>>(cfg, cache, layer, K, V, T, seq_begin, prm, sketch_proj);
+  page_store_kernel<0><<<grid, 256, 0, st>>>(cfg, cache, layer, K, V, T, seq_begin, prm, in_H, sketch_proj);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   slot_id_scan_kernel<0><<<seq_count, 1024, 0, st>>>(cfg, cache, layer, seq_begin, n_new);
@@ -730,14 +731,15 @@ cudaError_t launch_prefill_store(const carekv_config_t& cfg, const carekv_cache_
 
 cudaError_t launch_append(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* k,
                           const void* v, int seq_begin, int seq_count, const carekv_store_params_t& prm,
-                          const float* sketch_proj, int may_fill, cudaStream_t st) {
+                          const float* sketch_proj, int may_fill, int in_H, cudaStream_t st) {
   if (seq_count == 0) return cudaSuccess;
   dim3 g(cfg.num_kv_heads, seq_count);
-  append_kernel<<<g, 32, 0, st>>>(cfg, cache, layer, k, v, seq_begin, prm);
+  append_kernel<<<g, 32, 0, st>>>(cfg, cache, layer, k, v, seq_begin, prm, in_H);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || !may_fill) return e;
   dim3 g2(1, cfg.num_kv_heads, seq_count);
-  page_store_kernel<1><<<g2, 256, 0, st>>>(cfg, cache, layer, nullptr, nullptr, 0, seq_begin, prm, sketch_proj);
+  page_store_kernel<1><<<g2, 256, 0, st>>>(cfg, cache, layer, nullptr, nullptr, 0, seq_begin, prm, cfg.num_kv_heads,
+                                            sketch_proj);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   slot_id_scan_kernel<1><<<seq_count, 1024, 0, st>>>(cfg, cache, layer, seq_begin, 1);

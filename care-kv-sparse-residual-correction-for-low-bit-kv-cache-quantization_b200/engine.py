@@ -11,7 +11,7 @@ whether a page can complete, so no call reads device memory back.
 from __future__ import annotations
 
 import ctypes
-from typing import Optional, Sequence
+from typing import Optional, Sequence, Tuple
 
 import torch
 
@@ -23,11 +23,26 @@ _DT = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF
 
 
 class DecodeEngine:
-    def __init__(self, cache: CAREKVCache):
+    """shard = (kvh_begin, kvh_total): the cache holds kv heads [kvh_begin,
+    kvh_begin + cfg.num_kv_heads) of a model with kvh_total kv heads, and the
+    engine takes the model's full activation rows (k / v [n, kvh_total, D],
+    q / out [n, kvh_total * QN, D]), touching only its own heads (the C
+    ABI's _shard entry points).  None: the cache holds every kv head."""
+
+    def __init__(self, cache: CAREKVCache, shard: Optional[Tuple[int, int]] = None):
         self.cache = cache
         self.cfg = cache.cfg
         self._ws = None
         self._ws_bytes = 0
+        H = self.cfg.num_kv_heads
+        if shard is None:
+            shard = (0, H)
+        b0, tot = int(shard[0]), int(shard[1])
+        if b0 < 0 or b0 + H > tot:
+            raise ValueError(f"shard {shard}: kv heads [{b0}, {b0 + H}) do not fit {tot}")
+        self.shard = _lib.Shard(b0, tot)
+        self.kvh_total = tot
+        self.qn = self.cfg.num_heads // H
 
     # ── helpers ───────────────────────────────────────────────────────
     def _stream(self) -> int:
@@ -69,8 +84,8 @@ class DecodeEngine:
         """Write T rows per (sequence, kv head): K, V [seq_count, Hkv, T, D]."""
         cfg = self.cfg
         n, H, T, D = K.shape
-        K = self._check_tensor(K, (n, cfg.num_kv_heads, T, cfg.head_dim), "prefill K")
-        V = self._check_tensor(V, (n, cfg.num_kv_heads, T, cfg.head_dim), "prefill V")
+        K = self._check_tensor(K, (n, self.kvh_total, T, cfg.head_dim), "prefill K")
+        V = self._check_tensor(V, (n, self.kvh_total, T, cfg.head_dim), "prefill V")
         if K.dtype != V.dtype:
             raise ValueError("K and V must share a dtype")
         n_new = (T + cfg.page_size - 1) // cfg.page_size
@@ -78,9 +93,10 @@ class DecodeEngine:
             if self._pages(b, layer) + n_new > cfg.max_pages:
                 raise _lib.CacheFullError(_lib.ERR_CACHE_FULL, "prefill_store")
         sp = resolve_store_params(cfg, layer, _DT[K.dtype], token_start, sink_tokens)
-        _lib.check(_lib.lib().carekv_prefill_store(ctypes.byref(self.cache.ccfg), ctypes.byref(self.cache.c), layer,
-                                                   K.data_ptr(), V.data_ptr(), T, seq_begin, n, ctypes.byref(sp),
-                                                   self._sketch_ptr(), self._stream()), "carekv_prefill_store")
+        _lib.check(_lib.lib().carekv_prefill_store_shard(
+            ctypes.byref(self.cache.ccfg), ctypes.byref(self.cache.c), layer, K.data_ptr(), V.data_ptr(), T,
+            seq_begin, n, ctypes.byref(sp), self._sketch_ptr(), ctypes.byref(self.shard), self._stream()),
+            "carekv_prefill_store")
         if T > 0:
             last = T % cfg.page_size or cfg.page_size
             for b in range(seq_begin, seq_begin + n):
@@ -92,8 +108,8 @@ class DecodeEngine:
         """Append one token per sequence: k, v [seq_count, Hkv, D]."""
         cfg = self.cfg
         n = k.shape[0]
-        k = self._check_tensor(k, (n, cfg.num_kv_heads, cfg.head_dim), "append k")
-        v = self._check_tensor(v, (n, cfg.num_kv_heads, cfg.head_dim), "append v")
+        k = self._check_tensor(k, (n, self.kvh_total, cfg.head_dim), "append k")
+        v = self._check_tensor(v, (n, self.kvh_total, cfg.head_dim), "append v")
         T = cfg.page_size
         may_fill = 0
         for b in range(seq_begin, seq_begin + n):
@@ -105,9 +121,10 @@ class DecodeEngine:
             if last + 1 == T:
                 may_fill = 1       # this append completes a page: run the page store
         sp = resolve_store_params(cfg, layer, _DT[k.dtype])
-        _lib.check(_lib.lib().carekv_append(ctypes.byref(self.cache.ccfg), ctypes.byref(self.cache.c), layer,
-                                            k.data_ptr(), v.data_ptr(), seq_begin, n, ctypes.byref(sp),
-                                            self._sketch_ptr(), may_fill, self._stream()), "carekv_append")
+        _lib.check(_lib.lib().carekv_append_shard(ctypes.byref(self.cache.ccfg), ctypes.byref(self.cache.c), layer,
+                                                  k.data_ptr(), v.data_ptr(), seq_begin, n, ctypes.byref(sp),
+                                                  self._sketch_ptr(), may_fill, ctypes.byref(self.shard),
+                                                  self._stream()), "carekv_append")
         for b in range(seq_begin, seq_begin + n):
             self._advance(b, layer)
 
@@ -117,9 +134,9 @@ class DecodeEngine:
         """Decode attention for [seq_count, Hq, D] queries against the cache."""
         cfg = self.cfg
         n = q.shape[0]
-        q = self._check_tensor(q, (n, cfg.num_heads, cfg.head_dim), "decode q")
+        q = self._check_tensor(q, (n, self.kvh_total * self.qn, cfg.head_dim), "decode q")
         if out is None:
-            out = torch.empty_like(q)
+            out = torch.empty_like(q) if self.kvh_total == cfg.num_kv_heads else torch.zeros_like(q)
         if pages is None:
             pages = max(1, max((self._pages(b, layer) for b in range(seq_begin, seq_begin + n)), default=1))
         rp = resolve_route_params(cfg, layer, kind=kind, score_normalize=score_normalize,
@@ -128,10 +145,10 @@ class DecodeEngine:
             rp.kind = _lib.KIND_NONE
         nbytes = self.workspace_bytes(n, pages)
         ws = self.workspace(nbytes)
-        _lib.check(_lib.lib().carekv_decode_attention(
+        _lib.check(_lib.lib().carekv_decode_attention_shard(
             ctypes.byref(self.cache.ccfg), ctypes.byref(self.cache.c), layer, q.data_ptr(), out.data_ptr(),
             _DT[q.dtype], seq_begin, n, pages, ctypes.byref(rp), self._sketch_ptr(), ws.data_ptr(), ws.numel(),
-            self._stream()), "carekv_decode_attention")
+            ctypes.byref(self.shard), self._stream()), "carekv_decode_attention")
         return out
 
     def prefill_correct(self, layer: int, seq: int, q: torch.Tensor, attn: torch.Tensor, o_base: torch.Tensor,
@@ -268,6 +285,7 @@ class DecodeStepGraph:
     """One decode step over every layer, captured as CUDA graphs.
 
     Per layer the step appends the new K/V rows and runs decode attention
+    (on the engine's kv-head shard: q / k / v / out are the model's rows)
     (three kernel launches; five on steps where a page completes).  Kernels
     read page counts from device memory, so one graph replays for every
     step; a second graph adds the page-full store and is replayed on the
@@ -348,13 +366,15 @@ class DecodeStepGraph:
         for l in range(self.L):
             if io is not None:
                 stream.wait_event(ready[l])
-            _lib.check(lib.carekv_append(ctypes.byref(cache.ccfg), ctypes.byref(cache.c), l, self.k[l].data_ptr(),
-                                         self.v[l].data_ptr(), 0, self.B, ctypes.byref(self.store_params[l]),
-                                         self.sketch, fill, st), "carekv_append")
-            _lib.check(lib.carekv_decode_attention(
+            shard = ctypes.byref(self.engine.shard)
+            _lib.check(lib.carekv_append_shard(ctypes.byref(cache.ccfg), ctypes.byref(cache.c), l,
+                                               self.k[l].data_ptr(), self.v[l].data_ptr(), 0, self.B,
+                                               ctypes.byref(self.store_params[l]), self.sketch, fill, shard, st),
+                       "carekv_append")
+            _lib.check(lib.carekv_decode_attention_shard(
                 ctypes.byref(cache.ccfg), ctypes.byref(cache.c), l, self.q[l].data_ptr(), self.out[l].data_ptr(),
                 _DT[self.q.dtype], 0, self.B, self.max_pages, ctypes.byref(self.route_params[l]), self.sketch,
-                self.ws.data_ptr(), self.ws.numel(), st), "carekv_decode_attention")
+                self.ws.data_ptr(), self.ws.numel(), shard, st), "carekv_decode_attention")
             if io is not None:
                 done = torch.cuda.Event()
                 done.record(stream)

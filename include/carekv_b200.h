@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define CAREKV_ABI_VERSION 1
+#define CAREKV_ABI_VERSION 2
 
 /* status codes */
 #define CAREKV_OK                 0
@@ -218,6 +218,33 @@ int carekv_append(const carekv_config_t *cfg, const carekv_cache_t *cache, int32
                   const carekv_store_params_t *params, const float *sketch_proj,
                   int32_t may_fill_page, void *stream);
 
+/* ---- kv-head shards ------------------------------------------------------ */
+/* An arena may hold a contiguous range of a model's kv heads: kv heads
+ * [kvh_begin, kvh_begin + cfg->num_kv_heads) of a model with kvh_total kv
+ * heads (each with cfg->num_heads / cfg->num_kv_heads query heads), as when
+ * the kv heads of a layer are spread over GPUs (Mistral-7B: 8 kv heads, one
+ * per GPU).  The _shard forms below take the model's full activation rows
+ * -- K / V [seq_count][kvh_total][T][D], k / v [seq_count][kvh_total][D],
+ * q / out [seq_count][kvh_total * QN][D] -- and read or write only this
+ * shard's heads, so no caller-side gather or scatter is needed.  The plain
+ * entry points are the shard {0, cfg->num_kv_heads}.  The work of a
+ * (sequence, kv head) is independent of every other, so shards exchange
+ * nothing (the reference's per (layer, kv head) slot pools and budgets,
+ * attention.py:576). */
+typedef struct carekv_shard {
+    int32_t kvh_begin;   /* first model kv head held by the arena */
+    int32_t kvh_total;   /* kv heads of the model's activation rows */
+} carekv_shard_t;
+
+int carekv_prefill_store_shard(const carekv_config_t *cfg, const carekv_cache_t *cache, int32_t layer,
+                               const void *K, const void *V, int32_t T, int32_t seq_begin,
+                               int32_t seq_count, const carekv_store_params_t *params,
+                               const float *sketch_proj, const carekv_shard_t *shard, void *stream);
+int carekv_append_shard(const carekv_config_t *cfg, const carekv_cache_t *cache, int32_t layer,
+                        const void *k, const void *v, int32_t seq_begin, int32_t seq_count,
+                        const carekv_store_params_t *params, const float *sketch_proj,
+                        int32_t may_fill_page, const carekv_shard_t *shard, void *stream);
+
 /* Workspace bytes carekv_decode_attention needs for `seq_count` sequences
  * holding at most `max_pages_used` pages per (layer, kv head). */
 int carekv_decode_workspace_bytes(const carekv_config_t *cfg, int32_t seq_count,
@@ -237,12 +264,23 @@ int carekv_decode_attention(const carekv_config_t *cfg, const carekv_cache_t *ca
                             const carekv_route_params_t *params, const float *sketch_proj,
                             void *workspace, size_t workspace_bytes, void *stream);
 
+/* carekv_decode_attention on a kv-head shard (see carekv_shard_t): q / out
+ * are the model's rows [seq_count][shard->kvh_total * QN][D]; the workspace
+ * is sized for this arena's own kv heads. */
+int carekv_decode_attention_shard(const carekv_config_t *cfg, const carekv_cache_t *cache, int32_t layer,
+                                  const void *q, void *out, int32_t dtype, int32_t seq_begin,
+                                  int32_t seq_count, int32_t max_pages_used,
+                                  const carekv_route_params_t *params, const float *sketch_proj,
+                                  void *workspace, size_t workspace_bytes, const carekv_shard_t *shard,
+                                  void *stream);
+
 /* Kernel launches one carekv_decode_attention call over `seq_count`
  * sequences issues: a split-K pass and a route kernel per batch chunk.  The
- * batch runs in CAREKV_ATTEND_CHUNKS (environment, 1 / 2 / 4, default 2)
- * chunks on prioritised streams forked from the caller's stream and joined
- * back into it (events, so stream capture records them), routing of one
- * chunk overlapping the split-K pass of the next.  The helper streams and
+ * batch runs in CAREKV_ATTEND_CHUNKS (environment, 1 / 2 / 4, default 1)
+ * chunks; with more than one they run on prioritised streams forked from the
+ * caller's stream and joined back into it (events, so stream capture records
+ * them), routing of one chunk overlapping the split-K pass of the next.  The
+ * helper streams and
  * events belong to the calling host thread (one set per thread and device,
  * created by its first call outside stream capture; a thread whose first
  * call is captured runs that call unchunked), so several host threads may

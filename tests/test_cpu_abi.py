@@ -40,7 +40,7 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, n), f"{n} declared in include/carekv_b200.h but not exported"
     bound = {s[0] for s in pkg._lib.SIGNATURES}
     assert bound == set(names), "ctypes bindings and header disagree"
-    assert lib.carekv_abi_version() == 1
+    assert lib.carekv_abi_version() == 2
 
 
 def test_status_strings():

@@ -2,6 +2,9 @@
 against the eager DecodeEngine calls, and its host-I/O form (transfers in
 the graph, overlapping other layers) against the plain graph."""
 
+import ctypes
+import os
+
 import pytest
 import torch
 
@@ -61,7 +64,11 @@ def test_step_graph_matches_eager_and_host_io(pkg):
             fill = step.next_fill()
             fills += fill
             # append (+ page store and id scan on a filling step) and two launches per batch chunk
-            assert step.replay() == step.launches[fill] == L * ((3 if fill else 1) + 2 * 2)
+            n_att = ctypes.c_int32(0)
+            pkg._lib.check(pkg._lib.lib().carekv_decode_attention_launches(ctypes.byref(c_g.ccfg), B,
+                                                                           ctypes.byref(n_att)), "launches")
+            assert n_att.value == 2 * (int(os.environ.get("CAREKV_ATTEND_CHUNKS", "1")) if B > 1 else 1)
+            assert step.replay() == step.launches[fill] == L * ((3 if fill else 1) + n_att.value)
             for h_, d_ in zip(io[:3], (qs, ks, vs)):
                 h_.copy_(d_.cpu())
             step_io.replay()

@@ -71,3 +71,69 @@ def test_rank_batch_partition():
     assert bench.rank_batch(32, 4, 2, "weak") == (64, 32)
     with pytest.raises(ValueError):
         bench.rank_batch(32, 3, 0, "strong")
+
+
+def _partition_worker(rank, world, port, q):
+    """Each rank computes a stand-in output for the (sequence, kv head) pairs
+    it owns under both partitions; the ranks' parts are gathered and
+    reassembled into the model layout."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import importlib
+        P = importlib.import_module(
+            "care-kv-sparse-residual-correction-for-low-bit-kv-cache-quantization_b200").partition
+        B, H, QN, D = 6, 8, 4, 3
+        full = torch.arange(B * H * QN * D, dtype=torch.float32).view(B, H * QN, D)
+
+        def out_of(seq, qhead):          # what the owner of (seq, qhead // QN) computes
+            return full[seq, qhead]
+
+        # kv-head shards: the rank writes its query heads into model rows
+        kb, kn = P.kv_head_shard(H, world, rank)
+        mine = torch.zeros_like(full)
+        for s in range(B):
+            for qh in range(kb * QN, (kb + kn) * QN):
+                assert P.owner(s, qh // QN, B, H, world, "kv_head") == rank
+                mine[s, qh] = out_of(s, qh)
+        parts = [torch.empty_like(full) for _ in range(world)]
+        dist.all_gather(parts, mine)
+        got_kv = P.reassemble_kv_heads(parts, QN)
+        # batch shards: the rank computes every head of its sequences
+        sb, sn = P.batch_shard(B, world, rank)
+        rows = torch.stack([full[s] for s in range(sb, sb + sn)])
+        for s in range(sb, sb + sn):
+            assert P.owner(s, 0, B, H, world, "batch") == rank
+        sizes = [P.batch_shard(B, world, r)[1] for r in range(world)]
+        bparts = [torch.empty(n, H * QN, D) for n in sizes]
+        dist.all_gather(bparts, rows)
+        got_b = P.reassemble_batch(bparts)
+        q.put((rank, bool(torch.equal(got_kv, full)), bool(torch.equal(got_b, full))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.timeout(120)
+def test_two_gloo_ranks_partition_and_reassembly():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_partition_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted(q.get(timeout=100) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res == [(0, True, True), (1, True, True)]
+
+
+def test_contiguous_shares_cover_and_balance():
+    import importlib
+    P = importlib.import_module("care-kv-sparse-residual-correction-for-low-bit-kv-cache-quantization_b200").partition
+    for total in (1, 7, 8, 32):
+        for world in (1, 2, 3, 8):
+            shares = [P.contiguous_share(total, world, r) for r in range(world)]
+            items = [i for b, n in shares for i in range(b, b + n)]
+            assert items == list(range(total))
+            assert max(n for _, n in shares) - min(n for _, n in shares) <= 1
