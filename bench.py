@@ -375,6 +375,104 @@ def run_prefill_store(batch):
                           ms=ms, pages=batch * H * (N // 16), input_bytes=2 * K.numel() * K.element_size())))
 
 
+# ─────────────────────────── side measurements ───────────────────────────
+# Decode-attention calls at the shapes of the other BASELINE configurations,
+# one JSON line each (not the bench line): the GQA-8 wide pass (config 1's
+# head geometry at batch 32 and 4096 tokens), INT4 g64 MHA (config 5's
+# per-GPU shard under 8-way tensor parallelism: 5 of 40 heads, batch 64,
+# 8192 tokens) and the KIVI-style INT2 base (config 4's per-GPU shard under
+# 8-way kv-head sharding: 1 of 8 kv heads with its 4 query heads, batch 16,
+# 32768 tokens).  Two layers are stored; each call is one layer.
+SIDE = {
+    "gqa8_int3": dict(heads=32, kv_heads=4, head_dim=64, batch=32, context=4096, bits=3, group_size=32,
+                      base="uniform", workload="tinyllama-gqa8-int3-b32-ctx4096 (config 1 heads, scaled)"),
+    "int4_g64_mha": dict(heads=5, kv_heads=5, head_dim=128, batch=64, context=8192, bits=4, group_size=64,
+                         base="uniform", workload="llama2-13b-tp8-shard-int4g64-b64-ctx8192 (config 5 per GPU)"),
+    "kivi_int2_gqa4": dict(heads=4, kv_heads=1, head_dim=128, batch=16, context=32768, bits=2, group_size=128,
+                           base="kivi_style", workload="mistral-7b-kvshard-kivi-int2-b16-ctx32768 (config 4 per GPU)"),
+}
+
+
+def side_bytes_per_kvh(N, D, bits, G, qn, base, sk=1, sv=1, page=16, vtb=4, act=2):
+    """Algorithmic bytes of one decode-attention call per (sequence, kv head)
+    before the routed reads, as algorithmic_bytes_per_kvh, for the side
+    shapes: uniform bases with int8 scales and fp16 masters; the KIVI base
+    with fp32 per-token V scales, fp32 per-channel K scales and fp16 K rows
+    for tokens past the prefill (none here)."""
+    pages = math.ceil(N / page)
+    codes = N * 2 * D * bits // 8
+    if base == "uniform":
+        scales = N * 2 * G + pages * 4
+    else:
+        scales = N * 4 + D * 4 + 4
+    page_meta = pages * (4 + 4)
+    k_slots = pages * sk * (page * 32 // 2 + 2 + 1)
+    v_meta = pages * sv * 1 + pages * (page // vtb) * 2
+    return codes + scales + page_meta + k_slots + v_meta + 2 * qn * D * act
+
+
+def run_side(name, steps, warmup):
+    import torch
+    import importlib
+    for k, v in PAPER_BEST_ENV.items():
+        os.environ[k] = v
+    pkg = importlib.import_module(PKG)
+    dev = torch.device("cuda", 0)
+    sd = SIDE[name]
+    B, H, Hq, D, N = sd["batch"], sd["kv_heads"], sd["heads"], sd["head_dim"], sd["context"]
+    L = 2
+    kw = dict(num_layers=L, num_heads=Hq, num_kv_heads=H, head_dim=D, page_size=16, max_pages=N // 16 + 8,
+              base_bits=sd["bits"], group_size=sd["group_size"], scale_quant="int8", packed_base=True,
+              store_budget_mode="absolute", store_abs_k=1, store_abs_v=1, read_budget_mode="ratio",
+              read_budget_ratio=0.03, route_policy="joint")
+    if sd["base"] != "uniform":
+        kw.update(base_quantizer=sd["base"], scale_quant="none", kivi_window_pages=2)
+    cfg = pkg.CacheConfig(**kw)
+    cache = pkg.CAREKVCache(cfg, dev, batch=B)
+    eng = pkg.DecodeEngine(cache)
+    g = torch.Generator(device=dev).manual_seed(7)
+    for l in range(L):
+        for b0 in range(0, B, 8):
+            nb = min(8, B - b0)
+            K = torch.randn(nb, H, N, D, device=dev, generator=g)
+            K[..., :4] *= 20
+            eng.prefill_store(l, K.to(torch.bfloat16),
+                              torch.randn(nb, H, N, D, device=dev, generator=g).to(torch.bfloat16), seq_begin=b0)
+            del K
+    for l in range(L):
+        k = torch.randn(B, H, D, device=dev, generator=g).to(torch.bfloat16)
+        eng.append(l, k, torch.randn_like(k))
+    q = torch.randn(L, B, Hq, D, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty_like(q)
+    for i in range(warmup):
+        eng.attend(i % L, q[i % L], out=out[i % L])
+    torch.cuda.synchronize()
+    rc = cache.view("read_counter")
+    rc.zero_()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        ev[i][0].record()
+        eng.attend(i % L, q[i % L], out=out[i % L])
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    cache.check_errors()
+    ms = statistics.mean(a.elapsed_time(b) for a, b in ev)
+    reads_k, reads_v = (int(x) / steps for x in rc.sum(dim=(0, 1)).tolist())
+    Nt = N + 1
+    G = D // sd["group_size"]
+    bytes_call = (B * H * side_bytes_per_kvh(Nt, D, sd["bits"], G, Hq // H, sd["base"])
+                  + selected_bytes(reads_k, reads_v, D=D, bits=sd["bits"], G=G))
+    peak, peak_kind = measured_peak_gbs()
+    ach = bytes_call / (ms / 1e3) / 1e9
+    print(json.dumps(dict(measure="decode attention side line", name=name, workload=sd["workload"],
+                          batch=B, kv_heads=H, query_heads=Hq, head_dim=D, context=Nt, bits=sd["bits"],
+                          base=sd["base"], calls=steps, launch_ms=ms, tokens_per_s_per_layer=B / (ms / 1e3),
+                          selected_per_call=dict(k_slots=reads_k, v_slots=reads_v),
+                          roofline=dict(bound="hbm", achieved=ach, peak=peak, unit="GB/s", frac=ach / peak,
+                                        bytes_per_launch=bytes_call, peak_source=peak_kind),
+                          out_finite=bool(torch.isfinite(out.float()).all().item()))))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -388,7 +486,12 @@ def main():
                     help="strong: the global batch of 32 is split over the ranks; weak: 32 per rank")
     ap.add_argument("--prefill-store", type=int, default=0, metavar="B",
                     help="side measurement: time the prefill page store of B sequences and exit")
+    ap.add_argument("--side", choices=sorted(SIDE), default=None,
+                    help="side measurement: decode-attention calls at another configuration's shape")
     args = ap.parse_args()
+    if args.side:
+        run_side(args.side, args.steps, args.warmup)
+        return
     if args.prefill_store > 0:
         run_prefill_store(args.prefill_store)
         return

@@ -22,7 +22,8 @@ ERR_DEVICE_CHECK = 6
 F32, F16, BF16 = 0, 1, 2
 SCALE_INT8, SCALE_F16, SCALE_BF16, SCALE_F32 = 0, 1, 2, 3
 KIND_BOTH, KIND_K, KIND_V, KIND_NONE = 0, 1, 2, 3
-NUM_BUFFERS = 23
+NUM_BUFFERS = 26
+BASE_UNIFORM, BASE_KIVI = 0, 1
 
 i32 = ctypes.c_int32
 i64 = ctypes.c_int64
@@ -34,14 +35,14 @@ class Config(ctypes.Structure):
     _fields_ = [(n, i32) for n in (
         "num_layers", "num_heads", "num_kv_heads", "head_dim", "page_size", "max_pages",
         "base_bits", "group_size", "k_channel_group", "v_token_block", "sketch_dim",
-        "residual_bits", "scale_mode", "k_slots_per_page", "v_slots_per_page")]
+        "residual_bits", "scale_mode", "k_slots_per_page", "v_slots_per_page", "base_kind", "kivi_window_pages")]
 
 
 CACHE_PTR_FIELDS = (
     "k_codes", "v_codes", "k_scale", "v_scale", "k_master", "v_master", "valid", "num_pages",
     "v_norm2", "k_slot_group", "k_slot_data", "k_slot_scale", "k_slot_id", "v_slot_block",
     "v_slot_data", "v_slot_scale", "v_slot_id", "k_err", "v_err", "k_sketch", "slot_counter",
-    "read_counter", "error_flag")
+    "read_counter", "error_flag", "k_chan_scale", "k_window", "prefill_tokens")
 assert len(CACHE_PTR_FIELDS) == NUM_BUFFERS
 
 

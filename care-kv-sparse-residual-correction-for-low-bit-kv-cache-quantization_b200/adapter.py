@@ -7,8 +7,9 @@ what this library builds:
 
 * ``setup_model`` patches a model object (or loads a local checkpoint
   directory); this build has no model hub access.
-* Only the uniform base quantizer is built (``base_quantizer`` other than
-  ``uniform`` raises NotImplementedError).
+* The uniform and KIVI-style (``kivi_style`` / ``kvquant_style``) base
+  quantizers are built; the rotation and calibrated bases raise
+  NotImplementedError.
 """
 
 from __future__ import annotations
@@ -32,8 +33,8 @@ class CAREKVAdapter:
                  bits_k: int = -1, bits_v: int = -1, max_pages: int = 0, k_store_mode: str = "post_rope",
                  correction_impl: str = "cached", k_channel_group: int = 32, v_token_block: int = 4,
                  prefill_mode: str = "carekv_stored"):
-        if base_quantizer != "uniform":
-            raise NotImplementedError(f"base_quantizer={base_quantizer}: only the uniform base is built")
+        if base_quantizer not in ("uniform", "kivi_style", "kvquant_style"):
+            raise NotImplementedError(f"base_quantizer={base_quantizer}: the uniform and KIVI-style bases are built")
         if mode not in ("fixed", "adaptive"):
             raise ValueError(f"mode={mode}")
         self.mode = mode

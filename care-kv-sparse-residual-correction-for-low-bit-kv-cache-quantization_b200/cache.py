@@ -144,6 +144,9 @@ class CAREKVCache:
             "k_sketch": (torch.float16, (B, L, H, P, C, max(c.sketch_dim, 1))),
             "slot_counter": (torch.int32, (B, 2)), "read_counter": (torch.int64, (L, H, 2)),
             "error_flag": (torch.int32, (1,)),
+            "k_chan_scale": (torch.float32, (B, L, H, D)),
+            "k_window": (torch.float16, (B, L, H, max(c.kivi_window_pages, 1), T, D)),
+            "prefill_tokens": (torch.int32, (B, L, H)),
         }[name]
         return self._view(name, *spec)
 
@@ -218,6 +221,42 @@ class CAREKVCache:
             m = self.view(f"{which}_master")[seq, layer, h, p]
             return (s.float() * m.float()).to(torch.float16)
         return s.to(torch.float16)
+
+    def read_base_hat_concat(self, layer: int, kv_head: int, page_ids: Optional[List[int]] = None, seq: int = 0):
+        """KIVI base: the valid K_hat / V_hat rows of the pages in fp16, as the
+        reference's side buffer returns them (cache.py:845-865), rebuilt from
+        the packed codes, the per-channel K / per-token V scales and the fp16
+        window of decode-appended K rows.  Returns (K_hat, V_hat, valid_lens)."""
+        c = self.ccfg
+        if c.base_kind != _lib.BASE_KIVI:
+            raise AssertionError("read_base_hat_concat requires a KIVI-style base_quantizer")
+        from .quantizer import unpack_codes_2d
+        D, T = c.head_dim, c.page_size
+        if page_ids is None:
+            page_ids = self.all_page_ids(layer, kv_head, seq)
+        dt = getattr(self, "kivi_dtype", torch.float32)
+        pf = int(self.view("prefill_tokens")[seq, layer, kv_head].item())
+        cs = self.view("k_chan_scale")[seq, layer, kv_head]
+        kw = self.view("k_window")[seq, layer, kv_head]
+        Ks, Vs, lens = [], [], []
+        for p in page_ids:
+            n = int(self.view("valid")[seq, layer, kv_head, p].item())
+            lens.append(n)
+            if n == 0:
+                continue
+            kc = unpack_codes_2d(self.view("k_codes")[seq, layer, kv_head, p, :n].contiguous(), c.base_bits, D)
+            vc = unpack_codes_2d(self.view("v_codes")[seq, layer, kv_head, p, :n].contiguous(), c.base_bits, D)
+            vs = self.view("v_scale")[seq, layer, kv_head, p, :n]                       # [n, 1]
+            kh = (kc.float() * cs.unsqueeze(0)).to(dt).to(torch.float16)
+            npk = max(0, min(n, pf - p * T))
+            if npk < n:
+                kh[npk:] = kw[p - pf // T, npk:n]
+            Ks.append(kh)
+            Vs.append((vc.float() * vs).to(dt).to(torch.float16))
+        if not Ks:
+            z = torch.zeros(0, D, dtype=torch.float16, device=self.device)
+            return z, z, lens
+        return torch.cat(Ks), torch.cat(Vs), lens
 
     def read_counters(self):
         rc = self.view("read_counter")

@@ -132,6 +132,10 @@ class CacheConfig:
     # B200 build only: keep the fp16 K sketches (read only by the sketch
     # proxy score; the combined_kvscore path never reads them).
     store_sketch: bool = False
+    # B200 build only, KIVI-style base: pages of fp16 K rows per (sequence,
+    # layer, kv head) kept for decode-appended tokens (the reference keeps
+    # them in its fp16 side buffer, cache.py:487-499)
+    kivi_window_pages: int = 8
 
     def __post_init__(self):
         if self.layer_sensitivity is None:
@@ -192,10 +196,22 @@ class CacheConfig:
                 sv = max(sv, min(sp.v_budget, self.num_v_blocks))
         return sk, sv
 
+    @property
+    def is_kivi(self) -> bool:
+        """KIVI-style base (kivi_style; kvquant_style is its post-RoPE twin,
+        kivi_helpers.py:187-189)."""
+        return self.base_quantizer in ("kivi_style", "kvquant_style")
+
     def c_config(self) -> "_lib.Config":
-        if self.base_quantizer != "uniform":
+        if self.base_quantizer not in ("uniform", "kivi_style", "kvquant_style"):
             raise NotImplementedError(
-                f"base_quantizer={self.base_quantizer!r}: only the uniform per-group base is built")
+                f"base_quantizer={self.base_quantizer!r}: the uniform and KIVI-style bases are built")
+        if self.is_kivi:
+            for o in (self.k_bits_override, self.v_bits_override):
+                if o > 0 and o != self.base_bits:
+                    raise NotImplementedError("KIVI base: K and V bits must both equal base_bits")
+            if self.k_store_mode != "post_rope":
+                raise NotImplementedError("KIVI base: only the post-RoPE K store is built")
         if self.residual_bits != 4:
             raise NotImplementedError("residual_bits must be 4")
         sk, sv = self.slot_capacity()
@@ -207,14 +223,18 @@ class CacheConfig:
         c.page_size = self.page_size
         c.max_pages = self.padded_max_pages
         c.base_bits = self.base_bits
-        c.group_size = self.group_size
+        # KIVI: one V scale per token (group = head_dim), scales kept as fp32
+        # holding their activation-dtype values
+        c.group_size = self.head_dim if self.is_kivi else self.group_size
         c.k_channel_group = self.k_channel_group
         c.v_token_block = self.v_token_block
         c.sketch_dim = self.sketch_dim if self.store_sketch else 0
         c.residual_bits = self.residual_bits
-        c.scale_mode = self.scale_mode()
+        c.scale_mode = _lib.SCALE_F32 if self.is_kivi else self.scale_mode()
         c.k_slots_per_page = sk
         c.v_slots_per_page = sv
+        c.base_kind = _lib.BASE_KIVI if self.is_kivi else _lib.BASE_UNIFORM
+        c.kivi_window_pages = self.kivi_window_pages if self.is_kivi else 0
         return c
 
 

@@ -33,6 +33,14 @@ int validate_config(const carekv_config_t* c) {
   if (c->scale_mode < CAREKV_SCALE_INT8 || c->scale_mode > CAREKV_SCALE_F32) return CAREKV_ERR_INVALID_ARG;
   if (c->k_slots_per_page < 0 || c->k_slots_per_page > C) return CAREKV_ERR_INVALID_ARG;
   if (c->v_slots_per_page < 0 || c->v_slots_per_page > NV) return CAREKV_ERR_INVALID_ARG;
+  if (c->base_kind != CAREKV_BASE_UNIFORM && c->base_kind != CAREKV_BASE_KIVI) return CAREKV_ERR_INVALID_ARG;
+  if (c->base_kind == CAREKV_BASE_KIVI) {
+    // one V scale per token, scales kept as their activation-dtype values
+    if (c->group_size != c->head_dim || c->scale_mode != CAREKV_SCALE_F32) return CAREKV_ERR_INVALID_ARG;
+    if (c->kivi_window_pages < 0 || c->kivi_window_pages > c->max_pages) return CAREKV_ERR_INVALID_ARG;
+  } else if (c->kivi_window_pages != 0) {
+    return CAREKV_ERR_INVALID_ARG;
+  }
   return CAREKV_OK;
 }
 
@@ -45,6 +53,9 @@ int validate_cache(const carekv_config_t* c, const carekv_cache_t* k) {
   if (c->k_slots_per_page > 0 && (!k->k_slot_group || !k->k_slot_data || !k->k_slot_scale || !k->k_slot_id))
     return CAREKV_ERR_INVALID_ARG;
   if (c->v_slots_per_page > 0 && (!k->v_slot_block || !k->v_slot_data || !k->v_slot_scale || !k->v_slot_id))
+    return CAREKV_ERR_INVALID_ARG;
+  if (c->base_kind == CAREKV_BASE_KIVI && (!k->k_chan_scale || !k->prefill_tokens ||
+                                           (c->kivi_window_pages > 0 && !k->k_window)))
     return CAREKV_ERR_INVALID_ARG;
   return CAREKV_OK;
 }
@@ -128,6 +139,11 @@ int carekv_cache_layout(const carekv_config_t* cfg, int32_t batch, size_t sizes[
   sizes[i++] = static_cast<size_t>(batch) * 2 * 4;           // slot_counter
   sizes[i++] = static_cast<size_t>(d.L) * d.H * 2 * 8;       // read_counter
   sizes[i++] = 4;                                            // error_flag
+  const size_t lh = static_cast<size_t>(batch) * d.L * d.H;
+  const bool kivi = cfg->base_kind == CAREKV_BASE_KIVI;
+  sizes[i++] = kivi ? lh * d.D * 4 : 0;                                          // k_chan_scale
+  sizes[i++] = kivi ? lh * static_cast<size_t>(cfg->kivi_window_pages) * kPage * d.D * 2 : 0;  // k_window
+  sizes[i++] = kivi ? lh * 4 : 0;                                                // prefill_tokens
   return CAREKV_OK;
 }
 
@@ -141,11 +157,13 @@ int carekv_cache_init(const carekv_config_t* cfg, const carekv_cache_t* cache, v
       cache->v_master,     cache->valid,        cache->num_pages,    cache->v_norm2,     cache->k_slot_group,
       cache->k_slot_data,  cache->k_slot_scale, cache->k_slot_id,    cache->v_slot_block, cache->v_slot_data,
       cache->v_slot_scale, cache->v_slot_id,    cache->k_err,        cache->v_err,       cache->k_sketch,
-      cache->slot_counter, cache->read_counter, cache->error_flag};
+      cache->slot_counter, cache->read_counter, cache->error_flag, cache->k_chan_scale,
+      cache->k_window,     cache->prefill_tokens};
   // slot tables start empty (-1); everything else starts at zero
   const bool minus_one[CAREKV_NUM_BUFFERS] = {false, false, false, false, false, false, false, false,
                                               false, true,  false, false, true,  true,  false, false,
-                                              true,  false, false, false, false, false, false};
+                                              true,  false, false, false, false, false, false, false,
+                                              false, false};
   prepare_decode_streams();
   cudaStream_t st = as_stream(stream);
   for (int i = 0; i < CAREKV_NUM_BUFFERS; ++i) {

@@ -77,6 +77,27 @@ __device__ __forceinline__ int8_t quant_code(float x, float scale, int qmax, int
   t = fminf(fmaxf(t, static_cast<float>(-qmax - 1)), static_cast<float>(qmax));
   return static_cast<int8_t>(static_cast<int>(t));
 }
+// ───────────────────────── KIVI-style base (kivi_helpers.py:35-59) ─────────
+// scale = amax / qmax rounded to dt, then clamp(min=1e-8) in dt.  A scale of
+// 0 (an all-zero fp16 slice, where the clamp bound underflows to 0) makes the
+// reference's codes 0/0 = NaN and its x_hat NaN; it is kept as a NaN scale so
+// code * scale reads back NaN the same way.
+__device__ __forceinline__ float kivi_scale(float amax, int qmax, int dt) {
+  const float s = fmaxf(rnd(__fdiv_rn(amax, static_cast<float>(qmax)), dt), clamp_lo(dt));
+  return s == 0.f ? __int_as_float(0x7fc00000) : s;
+}
+// clamp(round(rnd(x / scale)), -qmax - 1, qmax) with the quotient rounded to
+// dt as torch divides in dt; a NaN quotient (zero scale) gives code 0.
+__device__ __forceinline__ int kivi_code_dt(float x, float scale, int qmax, int dt) {
+  float t = rintf(rnd(__fdiv_rn(x, scale), dt));
+  if (t != t) return 0;
+  return static_cast<int>(fminf(fmaxf(t, static_cast<float>(-qmax - 1)), static_cast<float>(qmax)));
+}
+// x_hat = code * scale in dt (NaN scale -> NaN)
+__device__ __forceinline__ float kivi_hat(int code, float scale, int dt) {
+  return rnd(__fmul_rn(static_cast<float>(code), scale), dt);
+}
+
 // dequantize: code * scale in fp32, rounded to the scale dtype.
 __device__ __forceinline__ float dequant(int code, float scale, int dt) {
   return rnd(__fmul_rn(static_cast<float>(code), scale), dt);
@@ -183,6 +204,8 @@ struct Dims {
   int L, H, P, D, R, G, C, NV, SK, SV, kslot_bytes, vslot_bytes, sketch;
   int bits, gsize, kcg, vtb, scale_mode;
   int scale_elem;  // bytes per stored base scale
+  int kivi;        // 1: KIVI base (per-channel K / per-token V scales, fp16 K window)
+  int W;           // KIVI: window pages of decode-appended fp16 K rows
 
   __host__ __device__ int64_t lhp(int b, int l, int h) const {
     return (static_cast<int64_t>(b) * L + l) * H + h;
@@ -211,6 +234,8 @@ __host__ __device__ inline Dims make_dims_shared(const carekv_config_t& c) {
   d.sketch = c.sketch_dim;
   d.scale_mode = c.scale_mode;
   d.scale_elem = c.scale_mode == CAREKV_SCALE_INT8 ? 1 : (c.scale_mode == CAREKV_SCALE_F32 ? 4 : 2);
+  d.kivi = c.base_kind == CAREKV_BASE_KIVI;
+  d.W = d.kivi ? c.kivi_window_pages : 0;
   return d;
 }
 __host__ __device__ inline Dims make_dims(const carekv_config_t& c) {

@@ -54,6 +54,15 @@ __global__ void __launch_bounds__(128) decode_partial_kernel(DecodeArgs a) {
   }
   float* Srow = a.S + static_cast<int64_t>(bh) * QN * a.p_used * kPage;
   const int64_t sstride = static_cast<int64_t>(a.p_used) * kPage;
+  // KIVI base: the prefill's per-channel K scales of this lane's channels,
+  // and where the fp16 window of decode-appended K rows starts
+  float kcs[DPL];
+  int pf = 0;
+  if (d.kivi) {
+#pragma unroll
+    for (int j = 0; j < DPL; ++j) kcs[j] = a.cache.k_chan_scale[lhp * D + lane + 32 * j];
+    pf = a.cache.prefill_tokens[lhp];
+  }
 
   for (int p = p0 + warp; p < p1; p += 4) {
     const int64_t pg = lhp * d.P + p;
@@ -68,14 +77,29 @@ __global__ void __launch_bounds__(128) decode_partial_kernel(DecodeArgs a) {
       const uint8_t* vr = a.cache.v_codes + (pg * kPage + t) * d.R;
       const int64_t srow = (pg * kPage + t) * d.G;
       float kh[DPL], vh[DPL];
+      if (d.kivi) {
+        // K_hat: packed prefill rows (per-channel scale) or the fp16 window
+        // row of a decode-appended token; V_hat: per-token scale.  Both as
+        // the reference's fp16 side buffer holds them (cache.py:800-821)
+        const bool packed_row = p * kPage + t < pf;
+        const uint16_t* wrow = packed_row ? nullptr : a.cache.k_window + ((lhp * d.W + (p - pf / kPage)) * kPage + t) * D;
+        const float vs = reinterpret_cast<const float*>(a.cache.v_scale)[srow];
 #pragma unroll
-      for (int j = 0; j < DPL; ++j) {
-        const int c = lane + 32 * j;
-        const int g = c / d.gsize;
-        const float sk = read_scale(a.cache.k_scale, srow + g, d.scale_mode, mk);
-        const float sv = read_scale(a.cache.v_scale, srow + g, d.scale_mode, mv);
-        kh[j] = f16r(__fmul_rn(static_cast<float>(unpack_code(kr, c, d.bits)), sk));
-        vh[j] = f16r(__fmul_rn(static_cast<float>(unpack_code(vr, c, d.bits)), sv));
+        for (int j = 0; j < DPL; ++j) {
+          const int c = lane + 32 * j;
+          kh[j] = packed_row ? f16r(kivi_hat(unpack_code(kr, c, d.bits), kcs[j], a.dt)) : f16_bits_to_f32(wrow[c]);
+          vh[j] = f16r(kivi_hat(unpack_code(vr, c, d.bits), vs, a.dt));
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < DPL; ++j) {
+          const int c = lane + 32 * j;
+          const int g = c / d.gsize;
+          const float sk = read_scale(a.cache.k_scale, srow + g, d.scale_mode, mk);
+          const float sv = read_scale(a.cache.v_scale, srow + g, d.scale_mode, mv);
+          kh[j] = f16r(__fmul_rn(static_cast<float>(unpack_code(kr, c, d.bits)), sk));
+          vh[j] = f16r(__fmul_rn(static_cast<float>(unpack_code(vr, c, d.bits)), sv));
+        }
       }
 #pragma unroll
       for (int i = 0; i < QN; ++i) {
@@ -179,7 +203,7 @@ static inline int64_t sel_stride(const carekv_config_t& c, int p_used) {
 enum class Pass { GENERIC, WIDE, NARROW };
 inline Pass choose_pass(const carekv_config_t& c) {
   const int D = c.head_dim;
-  const bool tiled = c.scale_mode == CAREKV_SCALE_INT8 && (D == 64 || D == 128) &&
+  const bool tiled = c.base_kind == CAREKV_BASE_UNIFORM && c.scale_mode == CAREKV_SCALE_INT8 && (D == 64 || D == 128) &&
                      c.group_size % (D / 4) == 0 && c.group_size % (D / 8) == 0 && c.page_size == kPage;
   const int qn = c.num_heads / c.num_kv_heads;
   if (tiled && qn <= 4 && (c.base_bits == 3 || c.base_bits == 4)) return Pass::NARROW;

@@ -32,6 +32,7 @@ namespace carekv {
 constexpr int kRSel = 32;     // selected items per apply round (a selection may hold more)
 constexpr int kRStg = 12 * 1024;   // apply staging bytes per CTA
 constexpr float kREps = 1e-6f;
+constexpr float kIllNorm = 0.01f;   // new-normaliser bound below which the direct exact form runs
 constexpr float kRL2e = 1.4426950408889634f;
 
 // 2^x with the SFU approximation (relative error ~2^-22; results below
@@ -161,6 +162,9 @@ struct RouteSmem {
   uint64_t stg_bar;
   float acc[NW][128];
   float z[NW];
+  float acc2[NW][128];   // attention-weighted V of the tokens outside the selected K pages
+  float z2[NW];          // and their attention mass (direct form of an ill-conditioned query)
+  int ill;
   union {
     __align__(16) uint32_t qfrag[4][2][32][4];  // A fragments of q_hi / q_lo per channel group and k-step (scoring)
     __align__(16) uint8_t stg[kRStg];           // staged items (apply)
@@ -169,6 +173,7 @@ struct RouteSmem {
   float coef[NW][kPage];
   int cnt_k, cnt_v, ntot, any_k, nkp, nvs;
   float mshift;
+  float zS;              // sum over the selected K pages' tokens of A (e^ds - 1)
 };
 
 // Route + correct one (sequence, kv head) `bh` with the NW warps of the
@@ -532,8 +537,11 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
               if (v_rows) {
                 vh = v_rows[((static_cast<int64_t>(h) * a.p_used + p) * kPage + t) * D + c];
               } else {
-                const float svv = read_scale(a.cache.v_scale, (pg * kPage + t) * d.G + c / d.gsize, d.scale_mode, mv);
-                vh = f16r(__fmul_rn(static_cast<float>(unpack_code(a.cache.v_codes + (pg * kPage + t) * d.R, c, d.bits)), svv));
+                const int64_t si = (pg * kPage + t) * d.G + c / d.gsize;
+                const float svv = d.kivi ? reinterpret_cast<const float*>(a.cache.v_scale)[si]
+                                         : read_scale(a.cache.v_scale, si, d.scale_mode, mv);
+                const int cv = unpack_code(a.cache.v_codes + (pg * kPage + t) * d.R, c, d.bits);
+                vh = d.kivi ? f16r(kivi_hat(cv, svv, a.dt)) : f16r(__fmul_rn(static_cast<float>(cv), svv));
               }
               const float df = vh - sm.O[i][c];
               acc = fmaf(df, df, acc);
@@ -1057,9 +1065,22 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
     };
     // exact form: shift by the largest ds over the valid tokens of every
     // selected K page (all rounds)
+    //
+    // The sparse form dO = (cbase O + sum_S cf V) / (cbase + sum_S cf) - O,
+    // cf = A cbase (e^ds - 1), takes the tokens outside S through O.  When S
+    // holds nearly all the attention and its ds are strongly negative, the
+    // new normaliser 1 + sum_S A (e^ds - 1) is tiny and the result rests on
+    // O minus the S tokens' share: a few ulps of O's fp32 rounding become
+    // errors of 1e-2.  Such a query (normaliser < kIllNorm) takes the direct
+    // form instead: the tokens outside S are summed explicitly (A V and A, a
+    // pass over their V rows) and S enters with A cbase e^ds, so every term
+    // is positive, as in the reference's a_new = A w / sum(A w)
+    // (attention.py:96-118).  Decode only (the prefill correction's base
+    // output comes from the caller).
     float mshift = 0.f;
+    bool ill = false;
     if (exact) {
-      float mx = -INFINITY;
+      float mx = -INFINITY, zs = 0.f;
       int covered = 0, nkp_all = 0;
       for (int q0 = 0; q0 < n_all;) {
         const int q1 = round_end(q0);
@@ -1068,7 +1089,11 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           for (int u = 0; u < sm.nkp; ++u) {
             const int nv = sm.kp_nv[u];
             covered += nv;
-            if (lane < nv) mx = fmaxf(mx, __fdiv_rn(sm.ds[u][lane], a.sqrt_d));
+            if (lane < nv) {
+              const float dsv = __fdiv_rn(sm.ds[u][lane], a.sqrt_d);
+              mx = fmaxf(mx, dsv);
+              if (!PF) zs += attw(Sb[i * sst + sm.kp_page[u] * kPage + tok_pos(lane, a.s_perm)], i) * expm1f(dsv);
+            }
           }
         }
         nkp_all += sm.nkp;
@@ -1077,10 +1102,15 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       }
       if (warp == 0) {
         mx = warp_max(mx);
-        if (lane == 0) sm.mshift = (nkp_all == 0) ? 0.f : (covered >= ntot ? mx : fmaxf(mx, 0.f));
+        zs = warp_sum(zs);
+        if (lane == 0) {
+          sm.mshift = (nkp_all == 0) ? 0.f : (covered >= ntot ? mx : fmaxf(mx, 0.f));
+          sm.ill = !PF && nkp_all > 0 && covered < ntot && 1.f + zs < kIllNorm;
+        }
       }
       __syncthreads();
       mshift = sm.mshift;
+      ill = sm.ill != 0;
     }
     const float cbase = exact ? expf(-mshift) : 1.f;
     float num[4] = {0.f, 0.f, 0.f, 0.f};   // channel lane + 32 jj (per-channel decode)
@@ -1165,14 +1195,19 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           }
           const float* srow = reinterpret_cast<const float*>(stg + k_codes_b + k_sc_b);
           for (int x = lane; x < (vrow ? 0 : kPage * G); x += 32)
-            sm.stage_sc[warp][x] = read_scale(stg + k_codes_b, x, d.scale_mode, sm.kp_vm[u]);
+            // KIVI scales are exact activation-dtype values (fp32 storage); the
+            // uniform base reads its scales back as fp16 (cache.py:713-718)
+            sm.stage_sc[warp][x] = d.kivi ? reinterpret_cast<const float*>(stg + k_codes_b)[x]
+                                          : read_scale(stg + k_codes_b, x, d.scale_mode, sm.kp_vm[u]);
           float cf = 0.f;
           if (lane < kPage && lane < nv) {
             const float A = attw(srow[tok_pos(lane, a.s_perm)], i);
             const float wk = sm.ds[u][lane];
             if (exact) {
               const float dsv = __fdiv_rn(wk, a.sqrt_d);
-              cf = A * (dsv <= 80.f ? cbase * expm1f(dsv) : expf(dsv - mshift) - cbase);
+              // direct form (ill): the S token's own new weight A e^(ds - m)
+              cf = ill ? A * (dsv <= 80.f ? cbase * expf(dsv) : expf(dsv - mshift))
+                       : A * (dsv <= 80.f ? cbase * expm1f(dsv) : expf(dsv - mshift) - cbase);
             } else {
               cf = A * wk * rp.k_corr_scale;
             }
@@ -1201,8 +1236,10 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
               for (int jj = 0; jj < 4; ++jj) {
                 const int ch = lane + 32 * jj;
                 if (ch < D) {
-                  const float vh = f16r(__fmul_rn(static_cast<float>(unpack_code(stg + t * R, ch, d.bits)),
-                                                  sm.stage_sc[warp][t * G + ch / d.gsize]));
+                  const int cv = unpack_code(stg + t * R, ch, d.bits);
+                  const float sc = sm.stage_sc[warp][t * G + ch / d.gsize];
+                  // KIVI: V_hat rounded in the activation dtype, then fp16
+                  const float vh = d.kivi ? f16r(kivi_hat(cv, sc, a.dt)) : f16r(__fmul_rn(static_cast<float>(cv), sc));
                   num[jj] = fmaf(c, vh, num[jj]);
                 }
               }
@@ -1264,6 +1301,50 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       write_base();
       return;
     }
+    if (ill) {
+      // direct form: A V and A of every valid token outside the selected K
+      // pages (a page bitmap in the staging area, free after the rounds)
+      uint32_t* kbits = reinterpret_cast<uint32_t*>(sm.stg);
+      const int nwords = (a.p_used + 31) >> 5;
+      __syncthreads();
+      for (int x = tid; x < nwords; x += NT) kbits[x] = 0u;
+      __syncthreads();
+      for (int x = tid; x < n_all; x += NT) {
+        const int e = multi ? gl[x] : sm.sel[i][x];
+        if (e < KG) atomicOr(&kbits[(e / d.SK) >> 5], 1u << ((e / d.SK) & 31));
+      }
+      __syncthreads();
+      float o2[4] = {0.f, 0.f, 0.f, 0.f}, z2 = 0.f;
+      for (int p = warp; p < np; p += NW) {
+        if ((kbits[p >> 5] >> (p & 31)) & 1u) continue;
+        const int64_t pg = lhp * d.P + p;
+        const int nv = a.cache.valid[pg];
+        const float vm = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
+        for (int t = 0; t < nv; ++t) {
+          const float A = attw(Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)], i);
+          z2 += A;
+          const uint8_t* vr = a.cache.v_codes + (pg * kPage + t) * R;
+          const int64_t srow = (pg * kPage + t) * G;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            const int c = lane + 32 * jj;
+            if (c < D) {
+              const int cv = unpack_code(vr, c, d.bits);
+              const float vh = d.kivi ? f16r(kivi_hat(cv, reinterpret_cast<const float*>(a.cache.v_scale)[srow], a.dt))
+                                      : f16r(__fmul_rn(static_cast<float>(cv),
+                                                       read_scale(a.cache.v_scale, srow + c / d.gsize, d.scale_mode, vm)));
+              o2[jj] = fmaf(A, vh, o2[jj]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int c = lane + 32 * jj;
+        if (c < D) sm.acc2[warp][c] = o2[jj];
+      }
+      if (lane == 0) sm.z2[warp] = z2;
+    }
     // fold the word layout's row groups onto lanes 0 .. WPR-1
     for (int o = WPR; o < 32; o <<= 1)
 #pragma unroll
@@ -1288,7 +1369,15 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       const int64_t row = static_cast<int64_t>(bh) * QN + i;
       const float oe = o_exact ? o_exact[row * D + tid] : ob;
       const float as = (po_direct && a.pl) ? a.pl[row] : 1.f;
-      const float delta = exact ? (__fdiv_rn(fmaf(cbase, oe, n), fmaf(cbase, as, z)) - ob) : (n - z * ob);
+      float delta;
+      if (ill) {
+        // direct form: (cbase sum_notS A V + sum_S A cbase e^ds V) / (cbase sum_notS A + sum_S A cbase e^ds)
+        float on = 0.f, zn = 0.f;
+        for (int w = 0; w < NW; ++w) { on += sm.acc2[w][tid]; zn += sm.z2[w]; }
+        delta = __fdiv_rn(fmaf(cbase, on, n), fmaf(cbase, zn, z)) - ob;
+      } else {
+        delta = exact ? (__fdiv_rn(fmaf(cbase, oe, n), fmaf(cbase, as, z)) - ob) : (n - z * ob);
+      }
       store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + tid, ob + delta, a.dt);
     }
     __syncthreads();

@@ -140,9 +140,18 @@ __global__ void __launch_bounds__(256) page_store_kernel(
     const int64_t pg = lhp * d.P + p;
     if (cache.valid[pg] != kPage) return;  // only the page this step filled
     nv = kPage;
+    if (d.kivi) {
+      // KIVI: the reference re-stores a page filled by decode with K_orig :=
+      // K_hat and V_orig := V_hat from its fp16 side buffer (layer.py:1089-1101):
+      // every residual is exactly 0
+      for (int i = tid; i < kPage * D; i += blockDim.x) {
+        sm.x[0][i >> lgD][i & (D - 1)] = 0.f;
+        sm.x[1][i >> lgD][i & (D - 1)] = 0.f;
+      }
+    }
     const float mk = cfg.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(cache.k_master[pg]) : 0.f;
     const float mv = cfg.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(cache.v_master[pg]) : 0.f;
-    for (int i = tid; i < kPage * D; i += blockDim.x) {
+    for (int i = tid; i < (d.kivi ? 0 : kPage * D); i += blockDim.x) {
       const int r = i >> lgD, c = i & (D - 1);
       const int64_t srow = (pg * kPage + r) * d.G + (c >> lgGs);
       const float sk = read_scale(cache.k_scale, srow, d.scale_mode, mk);
@@ -166,7 +175,27 @@ __global__ void __launch_bounds__(256) page_store_kernel(
   if (MODE == 0) {
     // ── per-group quantization (quantizer.py:31-64) ──
     const int gs = d.gsize;
-    if ((D == 64 || D == 128) && (gs == 16 || gs == 32 || gs == 64 || gs == 128) && D % gs == 0) {
+    if (d.kivi) {
+      // KIVI (kivi_helpers.py:35-59): K codes with the per-channel scale of
+      // the whole prefill (k_chan_scale), V codes with a per-token scale; the
+      // padded rows of a last page are zero with zero scales (the reference
+      // pads K_hat / V_hat with zeros after quantizing, layer.py:279-292)
+      const float* cs = cache.k_chan_scale + lhp * D;
+      for (int r = warp; r < kPage; r += blockDim.x / 32) {
+        float m = 0.f;
+        for (int c = lane; c < D; c += 32) m = fmaxf(m, fabsf(sm.x[1][r][c]));
+        m = warp_max(m);
+        const float vs = r < nv ? kivi_scale(m, qmax, dt) : 0.f;
+        for (int c = lane; c < D; c += 32) {
+          sm.code[1][r][c] = r < nv ? static_cast<int8_t>(kivi_code_dt(sm.x[1][r][c], vs, qmax, dt)) : 0;
+          sm.code[0][r][c] = r < nv ? static_cast<int8_t>(kivi_code_dt(sm.x[0][r][c], cs[c], qmax, dt)) : 0;
+        }
+        if (lane == 0) {
+          sm.sc[1][r][0] = vs;
+          sm.sc[0][r][0] = 0.f;   // K scales are per channel (k_chan_scale)
+        }
+      }
+    } else if ((D == 64 || D == 128) && (gs == 16 || gs == 32 || gs == 64 || gs == 128) && D % gs == 0) {
       // warp per (kind, row), lane on channels lane + 32k: the group maximum
       // is a segmented (gs = 16) or whole-warp max combined over the
       // group's columns; max is order-free, so the scale is the reference's
@@ -286,14 +315,17 @@ __global__ void __launch_bounds__(256) page_store_kernel(
     __syncthreads();
     // ── residual in place (residual_store.py:271-285) + V_hat norm ──
     float vn = 0.f;
+    const float* kcs = d.kivi ? cache.k_chan_scale + lhp * D : nullptr;
     for (int i = tid; i < kPage * D; i += blockDim.x) {
       const int r = i >> lgD, c = i & (D - 1), g = c >> lgGs;
       if (r < nv) {
-        const float kh = dequant(sm.code[0][r][c], sm.sc[0][r][g], dt);
+        const float kh = dequant(sm.code[0][r][c], d.kivi ? kcs[c] : sm.sc[0][r][g], dt);
         const float vh = dequant(sm.code[1][r][c], sm.sc[1][r][g], dt);
         sm.x[0][r][c] = rnd(__fsub_rn(sm.x[0][r][c], kh), dt);
         sm.x[1][r][c] = rnd(__fsub_rn(sm.x[1][r][c], vh), dt);
-        const float vr = f16r(__fmul_rn(static_cast<float>(sm.code[1][r][c]), sm.rscale[1][r][g]));
+        // the V rows as stored: fp16 of V_hat (the KIVI side buffer holds
+        // fp16(V_hat)), or code * the scale as read back
+        const float vr = d.kivi ? f16r(vh) : f16r(__fmul_rn(static_cast<float>(sm.code[1][r][c]), sm.rscale[1][r][g]));
         vn = fmaf(vr, vr, vn);
       } else {
         sm.x[0][r][c] = 0.f;
@@ -557,6 +589,44 @@ __global__ void __launch_bounds__(1024) slot_id_scan_kernel(carekv_config_t cfg,
   }
 }
 
+// KIVI per-channel K scales of a prefill (quant_dequant_kivi_k over the
+// whole prefill, kivi_helpers.py:35-47): first the channel maxima of |K|
+// over T, in chunks of rows, folded with an integer max (the bit patterns of
+// non-negative floats order like their values) into k_chan_scale, which
+// cache init zeroed; then the maxima become scales in place.
+constexpr int kKiviRows = 256;   // rows per CTA of the channel maximum
+__global__ void __launch_bounds__(128) kivi_chan_amax_kernel(carekv_config_t cfg, carekv_cache_t cache, int layer,
+                                                             const void* __restrict__ Kin, int T, int seq_begin,
+                                                             int in_H, int dt) {
+  const Dims d = make_dims(cfg);
+  const int h = blockIdx.y, s = blockIdx.z, b = seq_begin + s;
+  const int t0 = blockIdx.x * kKiviRows, t1 = min(T, t0 + kKiviRows);
+  const int64_t lhp = d.lhp(b, layer, h);
+  const int64_t base = (static_cast<int64_t>(s) * in_H + h) * T * d.D;
+  for (int c = threadIdx.x; c < d.D; c += blockDim.x) {
+    float m = 0.f;
+#pragma unroll 8
+    for (int t = t0; t < t1; ++t) m = fmaxf(m, fabsf(load_act(Kin, base + static_cast<int64_t>(t) * d.D + c, dt)));
+    atomicMax(reinterpret_cast<unsigned int*>(cache.k_chan_scale + lhp * d.D + c), __float_as_uint(m));
+  }
+}
+__global__ void __launch_bounds__(128) kivi_chan_scale_kernel(carekv_config_t cfg, carekv_cache_t cache, int layer,
+                                                              int T, int seq_begin, int dt) {
+  const Dims d = make_dims(cfg);
+  const int h = blockIdx.x, s = blockIdx.y, b = seq_begin + s;
+  const int64_t lhp = d.lhp(b, layer, h);
+  const int qmax = (1 << (d.bits - 1)) - 1;
+  for (int c = threadIdx.x; c < d.D; c += blockDim.x) {
+    float* sc = cache.k_chan_scale + lhp * d.D + c;
+    *sc = kivi_scale(*sc, qmax, dt);
+  }
+  if (threadIdx.x == 0) {
+    // the KIVI scales belong to one prefill per (sequence, layer)
+    if (cache.num_pages[lhp] != 0 || cache.prefill_tokens[lhp] != 0) atomicOr(cache.error_flag, kErrBadState);
+    cache.prefill_tokens[lhp] = T;
+  }
+}
+
 // Decode append of one row per (sequence, kv head) (layer.py:1028-1085,
 // cache.py:656-701).  One warp per (sequence, kv head).
 __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_cache_t cache, int layer,
@@ -621,6 +691,45 @@ __global__ void __launch_bounds__(32) append_kernel(carekv_config_t cfg, carekv_
   const int off = sh_off;
   const int64_t pg = lhp * d.P + p;
   const int qmax = (1 << (d.bits - 1)) - 1;
+  if (d.kivi) {
+    // KIVI decode append (layer.py:1037-1085): the K row quantized per
+    // channel over its single token (scale |k| / qmax per channel), kept as
+    // fp16 in the window; the V row quantized per token into the packed page
+    const int pf = cache.prefill_tokens[lhp];
+    const int wp = p - pf / kPage;   // window page of this page
+    if (wp < 0 || wp >= d.W) {
+      if (lane == 0) atomicOr(cache.error_flag, kErrPageOverflow);
+      return;
+    }
+    uint16_t* krow = cache.k_window + ((lhp * d.W + wp) * kPage + off) * D;
+    float mv = 0.f;
+    for (int c = lane; c < D; c += 32) {
+      const float x = xs[0][c];
+      const float ks = kivi_scale(fabsf(x), qmax, dt);
+      krow[c] = f32_to_f16_bits(kivi_hat(kivi_code_dt(x, ks, qmax, dt), ks, dt));
+      mv = fmaxf(mv, fabsf(xs[1][c]));
+    }
+    mv = warp_max(mv);
+    const float vs = kivi_scale(mv, qmax, dt);
+    for (int c = lane; c < D; c += 32) cs[1][c] = static_cast<int8_t>(kivi_code_dt(xs[1][c], vs, qmax, dt));
+    __syncwarp();
+    for (int j = lane; j < d.R; j += 32) cache.v_codes[(pg * kPage + off) * d.R + j] = pack_byte(cs[1], j, d.bits);
+    if (lane == 0) {
+      reinterpret_cast<float*>(cache.v_scale)[pg * kPage + off] = vs;
+      reinterpret_cast<float*>(cache.k_scale)[pg * kPage + off] = 0.f;
+    }
+    float vn = 0.f;
+    for (int c = lane; c < D; c += 32) {
+      const float vr = f16r(kivi_hat(cs[1][c], vs, dt));
+      vn = fmaf(vr, vr, vn);
+    }
+    vn = warp_sum(vn);
+    if (lane == 0) {
+      cache.v_norm2[pg] += vn;
+      cache.valid[pg] = off + 1;
+    }
+    return;
+  }
   // per-group max |x| of both rows: every lane folds its channels c = lane +
   // 32 t into the (kind, group) maxima, then one butterfly per maximum
   {
@@ -721,6 +830,14 @@ cudaError_t launch_prefill_store(const carekv_config_t& cfg, const carekv_cache_
                                  cudaStream_t st) {
   const int n_new = (T + kPage - 1) / kPage;
   if (n_new == 0 || seq_count == 0) return cudaSuccess;
+  if (cfg.base_kind == CAREKV_BASE_KIVI) {
+    dim3 ga((T + kKiviRows - 1) / kKiviRows, cfg.num_kv_heads, seq_count);
+    kivi_chan_amax_kernel<<<ga, 128, 0, st>>>(cfg, cache, layer, K, T, seq_begin, in_H, prm.input_dtype);
+    dim3 gs(cfg.num_kv_heads, seq_count);
+    kivi_chan_scale_kernel<<<gs, 128, 0, st>>>(cfg, cache, layer, T, seq_begin, prm.input_dtype);
+    cudaError_t e0 = cudaGetLastError();
+    if (e0 != cudaSuccess) return e0;
+  }
   dim3 grid(n_new, cfg.num_kv_heads, seq_count);
   page_store_kernel<0><<<grid, 256, 0, st>>>(cfg, cache, layer, K, V, T, seq_begin, prm, in_H, sketch_proj);
   cudaError_t e = cudaGetLastError();

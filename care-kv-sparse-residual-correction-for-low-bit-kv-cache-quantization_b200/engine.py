@@ -92,6 +92,11 @@ class DecodeEngine:
         for b in range(seq_begin, seq_begin + n):
             if self._pages(b, layer) + n_new > cfg.max_pages:
                 raise _lib.CacheFullError(_lib.ERR_CACHE_FULL, "prefill_store")
+            if cfg.is_kivi and self._pages(b, layer) > 0:
+                # the per-channel K scales span one prefill (kivi_helpers.py:35-47)
+                raise NotImplementedError("KIVI base: one prefill per sequence and layer, before any append")
+        if cfg.is_kivi:
+            self.cache.kivi_dtype = K.dtype
         sp = resolve_store_params(cfg, layer, _DT[K.dtype], token_start, sink_tokens)
         _lib.check(_lib.lib().carekv_prefill_store_shard(
             ctypes.byref(self.cache.ccfg), ctypes.byref(self.cache.c), layer, K.data_ptr(), V.data_ptr(), T,
@@ -102,6 +107,8 @@ class DecodeEngine:
             for b in range(seq_begin, seq_begin + n):
                 self._state()[(b, layer)] = (self._pages(b, layer) + n_new, last)
                 self.cache.lengths[b][layer] += T
+                if cfg.is_kivi:
+                    self._kivi_prefill()[(b, layer)] = T
 
     # ── decode ────────────────────────────────────────────────────────
     def append(self, layer: int, k: torch.Tensor, v: torch.Tensor, seq_begin: int = 0):
@@ -118,6 +125,9 @@ class DecodeEngine:
                 if pages + 1 > cfg.max_pages:
                     raise _lib.CacheFullError(_lib.ERR_CACHE_FULL, "append")
                 last = 0
+                pages += 1
+            if not self.kivi_window_ok(b, layer, pages - 1):
+                raise _lib.CacheFullError(_lib.ERR_CACHE_FULL, "append (KIVI fp16 K window)")
             if last + 1 == T:
                 may_fill = 1       # this append completes a page: run the page store
         sp = resolve_store_params(cfg, layer, _DT[k.dtype])
@@ -216,6 +226,21 @@ class DecodeEngine:
 
     def _pages(self, b, layer):
         return self._state().get((b, layer), (0, 0))[0]
+
+    def _kivi_prefill(self):
+        st = getattr(self.cache, "_kivi_pf", None)
+        if st is None:
+            st = {}
+            self.cache._kivi_pf = st
+        return st
+
+    def kivi_window_ok(self, b, layer, page) -> bool:
+        """KIVI base: a decode-appended row of `page` has a place in the fp16
+        K window (pages prefill_tokens // page_size + w, w < kivi_window_pages)."""
+        if not self.cfg.is_kivi:
+            return True
+        wp = page - self._kivi_prefill().get((b, layer), 0) // self.cfg.page_size
+        return 0 <= wp < self.cfg.kivi_window_pages
 
     def _last_page_valid(self, b, layer):
         return self._state().get((b, layer), (0, 0))[1]
@@ -396,6 +421,9 @@ class DecodeStepGraph:
                     if pages + 1 > min(self.cfg.max_pages, self.max_pages):
                         raise _lib.CacheFullError(_lib.ERR_CACHE_FULL, "decode step")
                     last = 0
+                    pages += 1
+                if not self.engine.kivi_window_ok(b, l, pages - 1):
+                    raise _lib.CacheFullError(_lib.ERR_CACHE_FULL, "decode step (KIVI fp16 K window)")
                 if last + 1 == T:
                     return 1
         return 0

@@ -164,7 +164,7 @@ class CAREKVLayer(nn.Module):
         if mode == "fp":
             K_att, V_att = k_post, v
         else:
-            K_att, V_att = self._quantize_dequantize(k_post), self._quantize_dequantize(v)
+            K_att, V_att = self._quantize_dequantize(k_post, "K"), self._quantize_dequantize(v, "V")
         if mode == "carekv_stored" and any_read_budget(cfg):
             O = self._stored_correction(eng, q_post, K_att, V_att, attention_mask, seq_begin)
             return self._out(O)
@@ -244,10 +244,16 @@ class CAREKVLayer(nn.Module):
                 out[b, :, t0:t1] = res.transpose(0, 1)
         return out
 
-    def _quantize_dequantize(self, x: Tensor) -> Tensor:
+    def _quantize_dequantize(self, x: Tensor, kind: str = "V") -> Tensor:
         """x [..., D] -> per-group quantize then dequantize with scales in x's
         dtype (layer.py:185-195): the K_hat / V_hat the reference's prefill
-        attends over (layer.py:298-299), before the cache's int8 scale step."""
+        attends over (layer.py:298-299), before the cache's int8 scale step.
+        KIVI-style base: per-channel K over the sequence axis, per-token V
+        (layer.py:706-712, kivi_helpers.py:35-59)."""
+        if self.cfg.is_kivi:
+            from .quantizer import quant_dequant_kivi_k, quant_dequant_kivi_v
+            return quant_dequant_kivi_k(x, self.cfg.base_bits) if kind == "K" else \
+                quant_dequant_kivi_v(x, self.cfg.base_bits)
         D = x.shape[-1]
         flat = x.reshape(-1, D).contiguous()
         codes, scale = quantize(flat, self.base_qcfg)

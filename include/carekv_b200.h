@@ -55,6 +55,14 @@ extern "C" {
 #define CAREKV_SCALE_BF16  2
 #define CAREKV_SCALE_F32   3
 
+/* base quantizer of an arena (CacheConfig.base_quantizer) */
+#define CAREKV_BASE_UNIFORM 0   /* per-group INT-b codes and scales ("uniform")          */
+#define CAREKV_BASE_KIVI    1   /* KIVI style ("kivi_style" / "kvquant_style"): prefill K
+                                 * codes with one scale per channel over the prefill,
+                                 * V codes with one scale per token; decode-appended K
+                                 * rows kept in fp16 (kivi_helpers.py:35-59,
+                                 * layer.py:1037-1085)                                  */
+
 /* Static shape of one cache arena (CacheConfig, cache.py:209-384). */
 typedef struct carekv_config {
     int32_t num_layers;
@@ -72,6 +80,11 @@ typedef struct carekv_config {
     int32_t scale_mode;         /* CAREKV_SCALE_*                             */
     int32_t k_slots_per_page;   /* K slot capacity per page (>= store budget)  */
     int32_t v_slots_per_page;   /* V slot capacity per page                    */
+    int32_t base_kind;          /* CAREKV_BASE_*; KIVI needs group_size == head_dim
+                                 * (one V scale per token) and scale_mode F32 (the
+                                 * scales' activation-dtype values)             */
+    int32_t kivi_window_pages;  /* KIVI: pages of fp16 K rows per (sequence, layer,
+                                 * kv head) for decode-appended tokens; 0 otherwise */
 } carekv_config_t;
 
 /* Device buffers of one arena holding `batch` sequences.  Shapes use
@@ -103,6 +116,11 @@ typedef struct carekv_cache {
     int32_t  *slot_counter;   /* [B][2] next K / V arena id per sequence                    */
     unsigned long long *read_counter; /* [L][H][2] K / V slots read, may be NULL           */
     int32_t  *error_flag;     /* [1] bit mask set by device-side checks                    */
+    /* KIVI base only (NULL otherwise): */
+    float    *k_chan_scale;   /* [B][L][H][D] per-channel K scale of the prefill (dtype value) */
+    uint16_t *k_window;       /* [B][L][H][W][T][D] fp16 K rows appended by decode: page
+                               * prefill_tokens / T + w of the sequence is window page w   */
+    int32_t  *prefill_tokens; /* [B][L][H] tokens written by the (single) prefill          */
 } carekv_cache_t;
 
 /* Per-call store policy, resolved by the host for one layer
@@ -155,9 +173,11 @@ int carekv_abi_version(void);
 const char *carekv_status_string(int status);
 
 /* Byte sizes of the arena buffers, in the order of carekv_cache_t's pointer
- * fields (23 entries, k_codes .. error_flag).  Replaces the sizing in
- * cache.py:430-536. */
-#define CAREKV_NUM_BUFFERS 23
+ * fields (26 entries, k_codes .. prefill_tokens; the last three are 0 for a
+ * uniform base).  Replaces the sizing in cache.py:430-536 (the KIVI fp16
+ * side buffer, cache.py:487-499, becomes packed codes, scales and a bounded
+ * fp16 window). */
+#define CAREKV_NUM_BUFFERS 26
 int carekv_cache_layout(const carekv_config_t *cfg, int32_t batch, size_t sizes[CAREKV_NUM_BUFFERS]);
 
 /* Reset an arena to empty: counters, valid rows and page counts zeroed,

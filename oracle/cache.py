@@ -14,13 +14,13 @@ import numpy as np
 from .numerics import round_to, F16, F32, BF16
 from .quant import (quantize, dequantize, pack_codes_2d, unpack_codes_2d,
                     packed_row_bytes, int8_scale_write, int8_scale_read,
-                    int8_scale_append)
+                    int8_scale_append, kivi_quant_dequant)
 from .store import StoreConfig, process_page, sketch_projection
 
 
 class OracleCache:
     def __init__(self, num_layers, num_kv_heads, head_dim, max_pages, store_cfg: StoreConfig,
-                 page_size=16, scale_quant="int8", scale_dtype=F16, layer_sensitivity=None):
+                 page_size=16, scale_quant="int8", scale_dtype=F16, layer_sensitivity=None, base="uniform"):
         self.L, self.H, self.D, self.P, self.T = num_layers, num_kv_heads, head_dim, max_pages, page_size
         self.cfg = store_cfg
         self.bits = store_cfg.base_bits
@@ -50,6 +50,12 @@ class OracleCache:
         self.next_v_slot = 0
         self.sens = list(layer_sensitivity) if layer_sensitivity else [1.0] * self.L
         self.sketch_P = sketch_projection(head_dim, store_cfg.k_channel_group, store_cfg.sketch_dim)
+        # KIVI-style base (kivi_style / kvquant_style): the reference keeps
+        # K_hat / V_hat in an fp16 side buffer (cache.py:487-499, 800-865)
+        self.base = base
+        if base == "kivi":
+            self.k_hat16 = np.zeros(shp + (self.T, head_dim), np.float32)
+            self.v_hat16 = np.zeros(shp + (self.T, head_dim), np.float32)
 
     # ── base writes ─────────────────────────────────────────────────
     def _write_scale(self, which, l, h, p, scale_in, dt):
@@ -73,6 +79,8 @@ class OracleCache:
 
     def prefill_write(self, l, h, K, V, dt, token_start_abs=0, sink_tokens=4):
         """_write_pages_for_kv_head, uniform base (layer.py:204-334)."""
+        if self.base == "kivi":
+            return self._prefill_write_kivi(l, h, K, V, dt, token_start_abs, sink_tokens)
         T_all, D = K.shape
         ps = self.T
         num_pages = math.ceil(T_all / ps)
@@ -100,6 +108,43 @@ class OracleCache:
             self.valid[l, h, pid] = nv
             res = process_page(cfg, Kp, Vp, Kc, Ks, Vc, Vs, nv, dt,
                                is_recent=is_recent, is_sink=is_sink, sketch_P=self.sketch_P)
+            self._commit_meta(l, h, pid, token_start_abs + t0, nv, res)
+            out.append(res)
+        return out
+
+    def _prefill_write_kivi(self, l, h, K, V, dt, token_start_abs, sink_tokens):
+        """_write_pages_for_kv_head, KIVI-style base (layer.py:230-297): K_hat
+        per channel over the whole prefill, V_hat per token, both in dt
+        (kivi_helpers.py:35-59); pages store fp16(K_hat) / fp16(V_hat) and the
+        store runs against them (K_hat_override, residual_store.py:272-274)."""
+        T_all, D = K.shape
+        ps = self.T
+        num_pages = math.ceil(T_all / ps)
+        cfg = self.cfg
+        cfg.sensitivity = self.sens[l]
+        K = round_to(np.asarray(K, np.float32), dt)
+        V = round_to(np.asarray(V, np.float32), dt)
+        K_hat = kivi_quant_dequant(K, self.bits, dt, axis=-2)
+        V_hat = kivi_quant_dequant(V, self.bits, dt, axis=-1)
+        out = []
+        for p in range(num_pages):
+            t0, t1 = p * ps, min((p + 1) * ps, T_all)
+            nv = t1 - t0
+            Kp = np.zeros((ps, D), np.float32)
+            Vp = np.zeros((ps, D), np.float32)
+            Khp = np.zeros((ps, D), np.float32)
+            Vhp = np.zeros((ps, D), np.float32)
+            Kp[:nv], Vp[:nv] = K[t0:t1], V[t0:t1]
+            Khp[:nv], Vhp[:nv] = K_hat[t0:t1], V_hat[t0:t1]
+            pid = int(self.next_page[l, h])
+            assert pid < self.P, "KV cache is full"
+            self.next_page[l, h] += 1
+            self.k_hat16[l, h, pid] = round_to(Khp, F16)
+            self.v_hat16[l, h, pid] = round_to(Vhp, F16)
+            self.valid[l, h, pid] = nv
+            res = process_page(cfg, Kp, Vp, None, None, None, None, nv, dt,
+                               is_recent=p >= num_pages - 4, is_sink=(token_start_abs + t0) < sink_tokens,
+                               K_hat_override=Khp, V_hat_override=Vhp, sketch_P=self.sketch_P)
             self._commit_meta(l, h, pid, token_start_abs + t0, nv, res)
             out.append(res)
         return out
@@ -142,6 +187,8 @@ class OracleCache:
             assert pid < self.P, "KV cache is full"
             self.next_page[l, h] += 1
             self.valid[l, h, pid] = 0
+        if self.base == "kivi":
+            return self._append_kivi(l, h, pid, k_row, v_row, dt, pos_abs)
         kc, ks = quantize(np.asarray(k_row, np.float32)[None], self.bits, self.g, dt)
         vc, vs = quantize(np.asarray(v_row, np.float32)[None], self.bits, self.g, dt)
         off = int(self.valid[l, h, pid])
@@ -176,6 +223,31 @@ class OracleCache:
             self._commit_meta(l, h, pid, ts, ps, res)
         return pid, off
 
+    def _append_kivi(self, l, h, pid, k_row, v_row, dt, pos_abs):
+        """KIVI decode append (layer.py:1037-1101): the row's K quantized per
+        channel over its one token, V per token, stored fp16; a page filled
+        by decode is re-stored with K_orig := K_hat (every residual 0)."""
+        ps = self.T
+        k = round_to(np.asarray(k_row, np.float32)[None], dt)
+        v = round_to(np.asarray(v_row, np.float32)[None], dt)
+        off = int(self.valid[l, h, pid])
+        assert off < ps, "page already full"
+        self.k_hat16[l, h, pid, off] = round_to(kivi_quant_dequant(k, self.bits, dt, axis=-2)[0], F16)
+        self.v_hat16[l, h, pid, off] = round_to(kivi_quant_dequant(v, self.bits, dt, axis=-1)[0], F16)
+        self.valid[l, h, pid] = off + 1
+        if off + 1 == ps:
+            Kh = round_to(self.k_hat16[l, h, pid], dt)
+            Vh = round_to(self.v_hat16[l, h, pid], dt)
+            cfg = self.cfg
+            cfg.sensitivity = self.sens[l]
+            if pos_abs is None:
+                pos_abs = int(self.valid[l, 0, :self.next_page[l, 0]].sum()) - 1
+            ts = pos_abs + 1 - ps
+            res = process_page(cfg, Kh, Vh, None, None, None, None, ps, dt, is_recent=True, is_sink=ts < 4,
+                               K_hat_override=Kh, V_hat_override=Vh, sketch_P=self.sketch_P)
+            self._commit_meta(l, h, pid, ts, ps, res)
+        return pid, off
+
     # ── reads ───────────────────────────────────────────────────────
     def page_ids(self, l, h):
         return list(range(int(self.next_page[l, h])))
@@ -191,6 +263,10 @@ class OracleCache:
             n = int(self.valid[l, h, p])
             lens.append(n)
             if n == 0:
+                continue
+            if self.base == "kivi":   # read_base_hat_concat (cache.py:845-865)
+                Ks_all.append(self.k_hat16[l, h, p, :n].copy())
+                Vs_all.append(self.v_hat16[l, h, p, :n].copy())
                 continue
             Kc = unpack_codes_2d(self.k_codes[l, h, p, :n], self.bits, self.D)
             Vc = unpack_codes_2d(self.v_codes[l, h, p, :n], self.bits, self.D)

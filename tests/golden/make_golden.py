@@ -339,23 +339,116 @@ def gen_kivi(out):
     print("kivi.npz", len(cases), "cases")
 
 
+# ───────────────────────────── KIVI-style base ─────────────────────────────
+KIVI_STORE_CASES = [
+    # name, dt, D, bits, T, store k, store v, steps
+    ("kivi_int2_d128_bf16", "bf16", 128, 2, 70, 1, 1, 20),
+    ("kivi_int2_d64_fp16", "fp16", 64, 2, 45, 2, 2, 20),
+    ("kivi_int3_d64_fp32", "fp32", 64, 3, 50, 1, 2, 20),
+    ("kivi_int4_d128_bf16", "bf16", 128, 4, 33, 2, 1, 20),
+]
+
+
+def dump_kivi(cache, arrays, key):
+    """The fp16 side buffers (cache.py:487-499), valid counts and slots."""
+    arrays[key + "_khat"] = as_np(cache.base_K_hat_fp16)
+    arrays[key + "_vhat"] = as_np(cache.base_V_hat_fp16)
+    arrays[key + "_valid"] = cache.valid_tokens.numpy().copy()
+    L, H, P = cache.valid_tokens.shape
+    metas = []
+    for l in range(L):
+        for h in range(H):
+            for p in range(cache.next_page[l][h]):
+                m = cache.meta_table[l][h][p]
+                if m is None:
+                    continue
+                metas.append(dict(l=l, h=h, p=p, k=list(m.k_residual_slots), v=list(m.v_residual_slots)))
+                arrays[f"{key}_kerr_{l}_{h}_{p}"] = as_np(m.k_error_norm)
+                arrays[f"{key}_verr_{l}_{h}_{p}"] = as_np(m.v_error_norm)
+    arrays[key + "_meta"] = np.array(json.dumps(metas))
+    nk = cache.num_stored_residual_slots()
+    arrays[key + "_kbuf"] = cache.k_residual_buf[:nk[0]].numpy().view(np.uint8).copy()
+    arrays[key + "_kbufs"] = as_np(cache.k_residual_scale[:nk[0], 0])
+    arrays[key + "_vbuf"] = cache.v_residual_buf[:nk[1]].numpy().view(np.uint8).copy()
+    arrays[key + "_vbufs"] = as_np(cache.v_residual_scale[:nk[1], 0])
+    arrays[key + "_npages"] = np.array(cache.next_page, np.int32)
+
+
+def gen_kivi_store(out):
+    """KIVI-style base (base_quantizer='kivi_style'): the prefill store
+    (layer.py:230-297), then decode appends through CAREKVLayer.decode_step
+    (layer.py:1037-1101) with their base attention outputs."""
+    import torch
+    from CARE_KV.care_kv.cache import CacheConfig, CAREKVCache
+    arrays, cases = {}, []
+    os.environ["CAREKV_STORE_POLICY"] = "residual_kind_aware"
+    os.environ["CAREKV_PREFILL_RESIDUAL_KIND"] = "both"
+    for ci, (name, dt, D, bits, T, sk, sv, steps) in enumerate(KIVI_STORE_CASES):
+        Hq, Hkv = 4, 2
+        cfg = CacheConfig(num_layers=1, num_heads=Hq, num_kv_heads=Hkv, head_dim=D, page_size=16,
+                          max_pages=8, base_bits=bits, group_size=32, k_channel_group=32, v_token_block=4,
+                          sketch_dim=32, packed_base=True, scale_quant="none", store_budget_mode="absolute",
+                          store_abs_k=sk, store_abs_v=sv, read_budget_ratio=0.0, base_quantizer="kivi_style")
+        layer = make_layer(cfg, Hq, Hkv, D, dt, 400 + ci)
+        cache = CAREKVCache(cfg)
+        g = torch.Generator().manual_seed(500 + ci)
+        K = torch.randn(Hkv, T, D, generator=g)
+        K[:, :, :4] *= 20.0
+        V = torch.randn(Hkv, T, D, generator=g)
+        Kt, Vt = K.to(tdt(dt)), V.to(tdt(dt))
+        for h in range(Hkv):
+            layer._write_pages_for_kv_head(cache, h, Kt[h], Vt[h], token_start_abs=0, sink_tokens=4)
+        key = f"k{ci}"
+        arrays[key + "_K"] = as_np(Kt)
+        arrays[key + "_V"] = as_np(Vt)
+        dump_kivi(cache, arrays, key)
+        dm = Hkv * D
+        hs = torch.randn(steps, dm, generator=g).to(tdt(dt))
+        outs, qs, ks, vs = [], [], [], []
+        rec = {}
+        orig = layer.attn.forward
+
+        def fwd(*a, **kw):
+            r = orig(*a, **kw)
+            rec["O"] = r
+            return r
+        layer.attn.forward = fwd
+        for s_ in range(steps):
+            h1 = hs[s_:s_ + 1]
+            qs.append(as_np((h1[0] @ layer.W_Q.T).reshape(Hq, D)))
+            ks.append(as_np((h1[0] @ layer.W_K.T).reshape(Hkv, D)))
+            vs.append(as_np((h1[0] @ layer.W_V.T).reshape(Hkv, D)))
+            layer.decode_step(cache, h1, position_embeddings=None)
+            outs.append(as_np(rec["O"]))
+        arrays[key + "_dq"] = np.stack(qs)
+        arrays[key + "_dk"] = np.stack(ks)
+        arrays[key + "_dv"] = np.stack(vs)
+        arrays[key + "_dO"] = np.stack(outs)
+        dump_kivi(cache, arrays, key + "d")
+        cases.append(dict(key=key, name=name, dt=dt, D=D, bits=bits, T=T, store_abs_k=sk, store_abs_v=sv,
+                          Hq=Hq, Hkv=Hkv, max_pages=8, steps=steps))
+    arrays["meta"] = np.array(json.dumps(cases))
+    np.savez_compressed(os.path.join(out, "kivi_store.npz"), **arrays)
+    print("kivi_store.npz", len(cases), "cases")
+
+
 # ───────────────────────────── layer ─────────────────────────────
 def gen_layer(out):
     """CAREKVLayer.prefill + decode_step of the reference (layer.py:643-1163)."""
     import torch
     sys.path.insert(0, HERE)
-    from layer_case import LAYER_CASES, layer_inputs, layer_cfg_kwargs
+    from layer_case import LAYER_CASES, KIVI_LAYER_CASES, layer_inputs, layer_cfg_kwargs
     from CARE_KV.care_kv.cache import CacheConfig, CAREKVCache
     from CARE_KV.care_kv.layer import CAREKVLayer
     env = dict(CAREKV_K_CORRECTION_MODE="exact", CAREKV_KSCORE_LIVE="1", CAREKV_SCORE_NORMALIZE="1",
                CAREKV_PREFILL_RESIDUAL_KIND="both", CAREKV_STORE_POLICY="residual_kind_aware")
     arrays, cases = {}, []
-    for ci, (name, Hq, Hkv, D, T, S, mode, seed) in enumerate(LAYER_CASES):
+    for ci, (name, Hq, Hkv, D, T, S, mode, seed, *base) in enumerate(LAYER_CASES + KIVI_LAYER_CASES):
         os.environ.update(env)
         os.environ["CAREKV_PREFILL_MODE"] = mode
         L = T + S
         W_Q, W_K, W_V, W_O, hid, cos, sin = [torch.from_numpy(x) for x in layer_inputs(Hq, Hkv, D, L, seed)]
-        cfg = CacheConfig(**layer_cfg_kwargs(Hq, Hkv, D, L))
+        cfg = CacheConfig(**layer_cfg_kwargs(Hq, Hkv, D, L, *base))
         layer = CAREKVLayer(cfg, 0, W_Q, W_K, W_V, W_O)
         cache = CAREKVCache(cfg)
         pre = layer.prefill(cache, hid[:T], position_embeddings=(cos[:, :T], sin[:, :T]))
@@ -365,7 +458,8 @@ def gen_layer(out):
         key = f"l{ci}"
         arrays[key + "_prefill"] = as_np(pre)
         arrays[key + "_decode"] = as_np(torch.cat(dec, dim=0))
-        cases.append(dict(key=key, name=name, Hq=Hq, Hkv=Hkv, D=D, T=T, steps=S, prefill_mode=mode, seed=seed))
+        cases.append(dict(key=key, name=name, Hq=Hq, Hkv=Hkv, D=D, T=T, steps=S, prefill_mode=mode, seed=seed,
+                          base=base[0] if base else "uniform"))
     for k in list(env) + ["CAREKV_PREFILL_MODE"]:
         os.environ.pop(k, None)
     arrays["meta"] = np.array(json.dumps(cases))
@@ -378,7 +472,7 @@ def main():
     ap.add_argument("--reference", default=os.environ.get("CAREKV_REFERENCE"),
                     help="root of the reference project checkout (or set CAREKV_REFERENCE)")
     ap.add_argument("--out", default=HERE)
-    ap.add_argument("--only", default="", help="comma list of quant,store,correction,layer,kivi")
+    ap.add_argument("--only", default="", help="comma list of quant,store,correction,layer,kivi,kivi_store")
     a = ap.parse_args()
     if not a.reference:
         ap.error("give --reference (or CAREKV_REFERENCE): the reference checkout the fixtures come from")
@@ -387,7 +481,7 @@ def main():
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     only = set(x for x in a.only.split(",") if x)
     for nm, fn in (("quant", gen_quant), ("store", gen_store), ("correction", gen_correction), ("layer", gen_layer),
-                   ("kivi", gen_kivi)):
+                   ("kivi", gen_kivi), ("kivi_store", gen_kivi_store)):
         if not only or nm in only:
             fn(a.out)
 

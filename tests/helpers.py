@@ -209,3 +209,42 @@ def classify_selection(got, want, info, q, tie_margin=1e-5):
     if saturated_attention(info, q):
         return "saturated"
     return "mismatch"
+
+
+def compare_kivi_state(gpu_cache, oc, b, layer, check_payloads=True):
+    """KIVI base: the GPU arena's (sequence b, layer) against the oracle's
+    fp16 side buffers (bit for bit, NaN where the reference has NaN), valid
+    counts and residual slots."""
+    import torch
+    valid = gpu_cache.view("valid")[b, layer].cpu().numpy()
+    assert np.array_equal(valid, oc.valid[layer]), "valid tokens"
+    npg = gpu_cache.view("num_pages")[b, layer].cpu().numpy()
+    assert np.array_equal(npg, oc.next_page[layer]), "page counts"
+    for h in range(oc.H):
+        Kg, Vg, lens = gpu_cache.read_base_hat_concat(layer, h, seq=b)
+        Ko, Vo, lens_o = oc.read_base_concat(layer, h)
+        assert lens == lens_o, ("valid lengths", h)
+        np.testing.assert_array_equal(Kg.float().cpu().numpy(), Ko, err_msg=f"K_hat kv head {h}")
+        np.testing.assert_array_equal(Vg.float().cpu().numpy(), Vo, err_msg=f"V_hat kv head {h}")
+    kdata, vdata = gpu_cache.view("k_slot_data"), gpu_cache.view("v_slot_data")
+    kgrp, vblk = gpu_cache.view("k_slot_group"), gpu_cache.view("v_slot_block")
+    for h in range(oc.H):
+        for p in range(int(npg[h])):
+            om = oc.meta[layer][h][p]
+            gm = gpu_cache.page_meta(layer, h, p, seq=b)
+            if om is None:
+                continue
+            assert gm.k_residual_slots == om["k_slots"], ("K slot ids", h, p, gm.k_residual_slots, om["k_slots"])
+            assert gm.v_residual_slots == om["v_slots"], ("V slot ids", h, p, gm.v_residual_slots, om["v_slots"])
+            np.testing.assert_allclose(gm.k_error_norm.float().cpu().numpy(), om["k_err"], rtol=1e-3, atol=1e-7)
+            np.testing.assert_allclose(gm.v_error_norm.float().cpu().numpy(), om["v_err"], rtol=1e-3, atol=1e-7)
+            if not check_payloads:
+                continue
+            if kdata is not None:
+                for j, cg in enumerate(kgrp[b, layer, h, p].cpu().numpy()):
+                    if cg >= 0:
+                        assert np.array_equal(kdata[b, layer, h, p, j].cpu().numpy(), oc.k_slots[om["k_slots"][cg]][0])
+            if vdata is not None:
+                for j, vb in enumerate(vblk[b, layer, h, p].cpu().numpy()):
+                    if vb >= 0:
+                        assert np.array_equal(vdata[b, layer, h, p, j].cpu().numpy(), oc.v_slots[om["v_slots"][vb]][0])

@@ -41,7 +41,7 @@ def test_layer_matches_reference(case):
     L = T + S
     W_Q, W_K, W_V, W_O, hid, cos, sin = [torch.from_numpy(x).to(dev) for x in layer_inputs(Hq, Hkv, D, L, case["seed"])]
     with env(CAREKV_PREFILL_MODE=case["prefill_mode"], **PAPER_BEST_ENV):
-        cfg = pkg.CacheConfig(**layer_cfg_kwargs(Hq, Hkv, D, L))
+        cfg = pkg.CacheConfig(**layer_cfg_kwargs(Hq, Hkv, D, L, case.get("base", "uniform")))
         cache = pkg.CAREKVCache(cfg, dev, batch=1)
         layer = pkg.CAREKVLayer(cfg, 0, W_Q, W_K, W_V, W_O, dev)
         pre = layer.prefill(cache, hid[:T], position_embeddings=(cos[:, :T], sin[:, :T]))

@@ -110,8 +110,10 @@ def test_adapter_env_config_and_patch():
     e = ad.env()
     assert e["CAREKV_STORE_ABS_K"] == "1" and e["CAREKV_READ_ABS_V"] == "3"
     assert e["CAREKV_READ_BUDGET_MODE"] == "absolute" and e["CAREKV_PREFILL_MODE"] == "carekv_stored"
+    # the KIVI-style base is built; rotation / calibrated bases are not
+    assert ad_mod.CAREKVAdapter(base_quantizer="kivi_style").base_quantizer == "kivi_style"
     with pytest.raises(NotImplementedError):
-        ad_mod.CAREKVAdapter(base_quantizer="kivi_style")
+        ad_mod.CAREKVAdapter(base_quantizer="rotatekv_style")
     keys = list(e)
     saved = {k: __import__("os").environ.get(k) for k in keys}
     try:

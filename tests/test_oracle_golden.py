@@ -172,3 +172,56 @@ def test_oracle_kivi_matches_reference(case):
     for axis, name in ((-2, "_k"), (-1, "_v")):
         got = kivi_quant_dequant(x, case["bits"], case["dtype"], axis)
         np.testing.assert_array_equal(got, KIVI[case["key"] + name], err_msg=f"{case['key']}{name}")
+
+
+def _check_kivi_cache(oc, z, key):
+    """fp16 side buffers bit for bit (NaN where the reference has NaN), valid
+    counts, slot ids, payloads and error norms."""
+    np.testing.assert_array_equal(oc.k_hat16, z[key + "_khat"], err_msg="K_hat side buffer")
+    np.testing.assert_array_equal(oc.v_hat16, z[key + "_vhat"], err_msg="V_hat side buffer")
+    assert np.array_equal(oc.valid, z[key + "_valid"]), "valid tokens"
+    assert np.array_equal(oc.next_page, z[key + "_npages"]), "page counts"
+    for m in json.loads(str(z[key + "_meta"])):
+        om = oc.meta[m["l"]][m["h"]][m["p"]]
+        assert om is not None
+        assert om["k_slots"] == m["k"], ("K slot ids", m)
+        assert om["v_slots"] == m["v"], ("V slot ids", m)
+        tag = f"{m['l']}_{m['h']}_{m['p']}"
+        np.testing.assert_allclose(om["k_err"], z[f"{key}_kerr_{tag}"], rtol=1e-3, atol=1e-7)
+        np.testing.assert_allclose(om["v_err"], z[f"{key}_verr_{tag}"], rtol=1e-3, atol=1e-7)
+    for kind, slots, nxt in (("k", oc.k_slots, oc.next_k_slot), ("v", oc.v_slots, oc.next_v_slot)):
+        buf = z[f"{key}_{kind}buf"]
+        assert nxt == buf.shape[0]
+        for sid in range(buf.shape[0]):
+            assert np.array_equal(slots[sid][0], buf[sid]), (kind, "payload", sid)
+            assert np.float32(slots[sid][1]) == z[f"{key}_{kind}bufs"][sid]
+
+
+@pytest.mark.parametrize("ci", range(4))
+def test_kivi_store_and_decode_golden(ci):
+    """KIVI-style base (base_quantizer='kivi_style'): per-channel K / per-token
+    V prefill store, decode appends and base decode attention against the
+    reference's own outputs."""
+    z, cases = _load("kivi_store.npz")
+    c = cases[ci]
+    key, dt = c["key"], c["dt"]
+    sc = StoreConfig(head_dim=c["D"], base_bits=c["bits"], group_size=32, store_abs_k=c["store_abs_k"],
+                     store_abs_v=c["store_abs_v"], store_budget_mode="absolute")
+    oc = OracleCache(1, c["Hkv"], c["D"], c["max_pages"], sc, scale_quant="none", base="kivi")
+    K, V = z[key + "_K"], z[key + "_V"]
+    for h in range(c["Hkv"]):
+        oc.prefill_write(0, h, K[h], V[h], dt)
+    _check_kivi_cache(oc, z, key)
+    rc = RouteConfig(head_dim=c["D"])
+    grp = c["Hq"] // c["Hkv"]
+    for s in range(c["steps"]):
+        pos = int(oc.valid[0, 0, :oc.next_page[0, 0]].sum())
+        for h in range(c["Hkv"]):
+            oc.append(0, h, z[key + "_dk"][s][h], z[key + "_dv"][s][h], dt, pos_abs=pos)
+        O_ref = z[key + "_dO"][s]
+        for h in range(c["Hkv"]):
+            O, _ = oracle.decode_attention_kvh(oc, 0, h, z[key + "_dq"][s][h * grp:(h + 1) * grp], rc,
+                                               correction=False)
+            tol = {"fp32": 1e-5, "fp16": 2e-3, "bf16": 8e-3}[dt]
+            np.testing.assert_allclose(oracle.round_to(O, dt), O_ref[h * grp:(h + 1) * grp], rtol=tol, atol=tol)
+    _check_kivi_cache(oc, z, key + "d")
