@@ -242,7 +242,7 @@ def run_gpu(args, rank, world):
                           max_pages=max_pages, base_bits=w["bits"], group_size=w["group_size"],
                           scale_quant="int8", packed_base=True, store_budget_mode="absolute",
                           store_abs_k=w["store_k"], store_abs_v=w["store_v"], read_budget_mode="ratio",
-                          read_budget_ratio=w["read_ratio"], route_policy="joint")
+                          read_budget_ratio=w["read_ratio"], route_policy="joint", correction_impl="vectorized")
     cache = pkg.CAREKVCache(cfg, dev, batch=B)
     eng = pkg.DecodeEngine(cache)
     g = torch.Generator(device=dev).manual_seed(1234 + seq0)
@@ -356,7 +356,7 @@ def run_prefill_store(batch):
                           max_pages=N // 16 + 8, base_bits=w["bits"], group_size=w["group_size"],
                           scale_quant="int8", packed_base=True, store_budget_mode="absolute",
                           store_abs_k=w["store_k"], store_abs_v=w["store_v"], read_budget_mode="ratio",
-                          read_budget_ratio=w["read_ratio"], route_policy="joint")
+                          read_budget_ratio=w["read_ratio"], route_policy="joint", correction_impl="vectorized")
     cache = pkg.CAREKVCache(cfg, dev, batch=batch)
     eng = pkg.DecodeEngine(cache)
     g = torch.Generator(device=dev).manual_seed(0)
@@ -424,7 +424,7 @@ def run_side(name, steps, warmup):
     kw = dict(num_layers=L, num_heads=Hq, num_kv_heads=H, head_dim=D, page_size=16, max_pages=N // 16 + 8,
               base_bits=sd["bits"], group_size=sd["group_size"], scale_quant="int8", packed_base=True,
               store_budget_mode="absolute", store_abs_k=1, store_abs_v=1, read_budget_mode="ratio",
-              read_budget_ratio=0.03, route_policy="joint")
+              read_budget_ratio=0.03, route_policy="joint", correction_impl="vectorized")
     if sd["base"] != "uniform":
         kw.update(base_quantizer=sd["base"], scale_quant="none", kivi_window_pages=2)
     cfg = pkg.CacheConfig(**kw)

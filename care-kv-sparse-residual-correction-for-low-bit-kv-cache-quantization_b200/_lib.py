@@ -60,7 +60,12 @@ class RouteParams(ctypes.Structure):
     _fields_ = [("kind", i32), ("joint", i32), ("score_normalize", i32), ("kscore_live", i32),
                 ("exact", i32), ("budget_mode", i32), ("read_k", i32), ("read_v", i32),
                 ("ratio_k", ctypes.c_double), ("ratio_v", ctypes.c_double), ("k_corr_scale", f32), ("sensitivity", f32),
-                ("lambda_k", f32), ("lambda_v", f32)]
+                ("lambda_k", f32), ("lambda_v", f32), ("legacy", i32), ("policy", i32), ("baseline_score", i32),
+                ("adaptive_score", i32), ("rel_threshold", f32), ("abs_threshold", f32), ("min_keep", i32)]
+
+
+POLICY = {"separate": 0, "joint": 1, "k_first": 2, "adaptive": 3}
+SCORE = {"carekv": 0, "magnitude_only": 1, "attention_only": 2, "oracle_proxy": 3}
 
 
 class Shard(ctypes.Structure):

@@ -129,9 +129,11 @@ class CacheConfig:
     correction_impl: str = "cached"
     pack_impl: str = "vectorized"
     budget_policy: str = "uniform"
-    # B200 build only: keep the fp16 K sketches (read only by the sketch
-    # proxy score; the combined_kvscore path never reads them).
-    store_sketch: bool = False
+    # B200 build only: keep the fp16 K sketches (read by the cached router and
+    # the vectorized router's sketch proxy score; combined_kvscore never reads
+    # them).  None: kept unless correction_impl is "vectorized" (the
+    # reference stores them always; its cached router needs them).
+    store_sketch: Optional[bool] = None
     # B200 build only, KIVI-style base: pages of fp16 K rows per (sequence,
     # layer, kv head) kept for decode-appended tokens (the reference keeps
     # them in its fp16 side buffer, cache.py:487-499)
@@ -160,6 +162,8 @@ class CacheConfig:
             raise ValueError(f"pack_impl={self.pack_impl}")
         if self.budget_policy not in {"uniform", "u_shaped", "sensitivity", "layer_head_impact"}:
             raise ValueError(f"budget_policy={self.budget_policy}")
+        if self.store_sketch is None:
+            self.store_sketch = self.correction_impl != "vectorized"
 
     def scale_torch_dtype(self):
         import torch
@@ -324,9 +328,12 @@ def _check_unbuilt_route_knobs() -> None:
 
 def resolve_route_params(cfg: CacheConfig, layer_id: int, kind: Optional[str] = None,
                          score_normalize: Optional[bool] = None,
-                         k_corr_scale: Optional[float] = None) -> "_lib.RouteParams":
+                         k_corr_scale: Optional[float] = None, legacy: bool = False) -> "_lib.RouteParams":
     """Budget resolution of residual_router.py:37-76 plus the env knobs of
-    vectorized_joint_correction (attention.py:576-957)."""
+    vectorized_joint_correction (attention.py:576-957), or, legacy=True, of
+    the cached router ResidualRouter.route (residual_router.py:88-452): sketch
+    K scores, the route policy (joint / separate / k_first / adaptive), the
+    baseline_score ablations and the adaptive_score thresholds."""
     _check_unbuilt_route_knobs()
     if kind is None:
         kind = os.environ.get("CAREKV_PREFILL_RESIDUAL_KIND", "both").lower()
@@ -357,7 +364,30 @@ def resolve_route_params(cfg: CacheConfig, layer_id: int, kind: Optional[str] = 
     p.sensitivity = float(cfg.layer_sensitivity[layer_id])
     p.lambda_k = float(os.environ.get("CAREKV_KSCORE_LAMBDA_K", "1") or 1)
     p.lambda_v = float(os.environ.get("CAREKV_KSCORE_LAMBDA_V", "1") or 1)
+    if legacy:
+        if cfg.baseline_score not in _lib.SCORE:
+            raise NotImplementedError(f"baseline_score={cfg.baseline_score!r}: built are {sorted(_lib.SCORE)}")
+        if not cfg.store_sketch:
+            raise ValueError("the cached router scores K slots from their sketches: CacheConfig(store_sketch=True)")
+        p.legacy = 1
+        p.kscore_live = 0
+        p.joint = 1 if cfg.route_policy == "joint" else 0
+        p.policy = _lib.POLICY[cfg.route_policy]
+        p.baseline_score = _lib.SCORE[cfg.baseline_score]
+        p.adaptive_score = 1 if cfg.read_budget_mode == "adaptive_score" else 0
+        p.rel_threshold = float(cfg.read_relative_threshold or 0.0)
+        p.abs_threshold = float(cfg.read_absolute_threshold or 0.0)
+        p.min_keep = int(cfg.read_min_keep or 0)
     return p
+
+
+def legacy_router(cfg: CacheConfig) -> bool:
+    """Does a correction of this configuration take the reference's cached
+    router?  The reference's prefill correction does unless correction_impl is
+    "vectorized" (layer.py:522-630).  (Its decode step always does,
+    attention.py:1025; this library's decode runs the vectorized router
+    unless CAREKV_DECODE_ROUTER=cached.)"""
+    return cfg.correction_impl != "vectorized"
 
 
 def any_read_budget(cfg: CacheConfig) -> bool:

@@ -84,6 +84,19 @@ int validate_shard(const carekv_config_t* c, const carekv_shard_t* sh) {
 
 int64_t act_bytes(int32_t dt) { return dt == CAREKV_F32 ? 4 : 2; }
 
+// The cached router: sketch K scores, a known policy and score; its
+// adaptive_score thresholds work on at most 32 selected slots per query
+// (absolute caps).
+int validate_legacy(const carekv_route_params_t* p) {
+  if (p->legacy == 0) return CAREKV_OK;
+  if (p->legacy != 1 || p->kscore_live) return CAREKV_ERR_INVALID_ARG;
+  if (p->policy < CAREKV_POLICY_SEPARATE || p->policy > CAREKV_POLICY_ADAPTIVE) return CAREKV_ERR_INVALID_ARG;
+  if (p->baseline_score < CAREKV_SCORE_CAREKV || p->baseline_score > CAREKV_SCORE_ORACLE_PROXY)
+    return CAREKV_ERR_INVALID_ARG;
+  if (p->adaptive_score && (p->budget_mode != 0 || p->read_k + p->read_v > 32)) return CAREKV_ERR_UNSUPPORTED;
+  return CAREKV_OK;
+}
+
 #define CHECK(x)                      \
   do {                                \
     const int _s = (x);               \
@@ -329,6 +342,7 @@ int carekv_decode_attention_shard(const carekv_config_t* cfg, const carekv_cache
     if (params->budget_mode == 0 && (params->read_k < 0 || params->read_v < 0)) return CAREKV_ERR_INVALID_ARG;
     if (!params->kscore_live && (!cache->k_sketch || cfg->sketch_dim <= 0 || !sketch_proj))
       return CAREKV_ERR_INVALID_ARG;
+    CHECK(validate_legacy(params));
   }
   if (seq_count == 0 || max_pages_used == 0) {
     if (seq_count == 0) return CAREKV_OK;
@@ -370,6 +384,7 @@ int carekv_prefill_correction(const carekv_config_t* cfg, const carekv_cache_t* 
   if (params->kind != CAREKV_KIND_NONE) {
     // any budget is served (selections beyond 32 entries apply in rounds)
     if (params->budget_mode == 0 && (params->read_k < 0 || params->read_v < 0)) return CAREKV_ERR_INVALID_ARG;
+    CHECK(validate_legacy(params));
   }
   if (n_pos == 0) return CAREKV_OK;
   return prefill_correction(*cfg, *cache, layer, seq, n_pos, max_pages_used, q, logits, row_max, attn, attn_sum,

@@ -174,6 +174,8 @@ struct RouteSmem {
   int cnt_k, cnt_v, ntot, any_k, nkp, nvs;
   float mshift;
   float zS;              // sum over the selected K pages' tokens of A (e^ds - 1)
+  float ent[QN];         // cached router, adaptive policy: attention entropy per query
+  double vsum[NW];
 };
 
 // Route + correct one (sequence, kv head) `bh` with the NW warps of the
@@ -563,7 +565,18 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           }
 #pragma unroll
           for (int o = 8; o > 0; o >>= 1) qd += __shfl_xor_sync(hm, qd, o);
-          if (t == 0) sc[i * NG + e] = mass * fabsf(qd) * bnd * pvd * rp.sensitivity;
+          if (t == 0) {
+            // residual_router.py:185-212 (the cached router's baseline_score
+            // ablations; the vectorized proxy is the "carekv" score)
+            float v;
+            switch (rp.legacy ? rp.baseline_score : CAREKV_SCORE_CAREKV) {
+              case CAREKV_SCORE_MAGNITUDE_ONLY: v = fabsf(qd); break;
+              case CAREKV_SCORE_ATTENTION_ONLY: v = mass; break;
+              case CAREKV_SCORE_ORACLE_PROXY: v = fabsf(qd) * mass; break;
+              default: v = mass * fabsf(qd) * bnd * pvd * rp.sensitivity;
+            }
+            sc[i * NG + e] = v;
+          }
         }
       }
     }
@@ -590,7 +603,14 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           float mass = 0.f;
           for (int t = t0; t < t1; ++t)
             mass += attw(Wb[i * sst + p * kPage + tok_pos(t, a.s_perm)], i);
-          sc[i * NG + KG + e] = __fmul_rn(__fmul_rn(mass, err), rp.sensitivity);
+          float v;
+          switch (rp.legacy ? rp.baseline_score : CAREKV_SCORE_CAREKV) {
+            case CAREKV_SCORE_MAGNITUDE_ONLY: v = err; break;
+            case CAREKV_SCORE_ATTENTION_ONLY: v = mass; break;
+            case CAREKV_SCORE_ORACLE_PROXY: v = __fmul_rn(mass, err); break;
+            default: v = __fmul_rn(__fmul_rn(mass, err), rp.sensitivity);
+          }
+          sc[i * NG + KG + e] = v;
         }
       } else {
         for (int i = 0; i < QN; ++i) sc[i * NG + KG + e] = -1.f;
@@ -610,7 +630,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   __syncthreads();
 
   // ── budgets (residual_router.py:37-76) ──
-  const int n_k = sm.cnt_k, n_v = sm.cnt_v;
+  const int n_k = sm.cnt_k, n_v = sm.cnt_v, ntot_all = sm.ntot;
   const bool want_k = kind_k && n_k > 0, want_v = kind_v && n_v > 0;
   int bk, bv;
   {
@@ -634,7 +654,11 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   const bool score_k = want_k && bk > 0, score_v = want_v && bv > 0;
 
   // ── 3a. normalisation; kinds that take no part are not candidates ──
-  const bool norm = rp.score_normalize && rp.kind == CAREKV_KIND_BOTH && score_k && score_v;
+  // the cached router normalises whenever kind is "both" and ranks every
+  // candidate of an enabled kind (residual_router.py:318-348); the
+  // vectorized router only kinds with a budget
+  const bool norm = rp.legacy ? (rp.score_normalize && rp.kind == CAREKV_KIND_BOTH)
+                              : (rp.score_normalize && rp.kind == CAREKV_KIND_BOTH && score_k && score_v);
   if (norm) {
     for (int i = 0; i < QN; ++i) {
       float ak = 0.f, av = 0.f;
@@ -656,7 +680,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
     __syncthreads();
   }
   for (int e = tid; e < NG; e += NT) {
-    const bool part = e < KG ? score_k : score_v;
+    const bool part = rp.legacy ? (e < KG ? want_k : want_v) : (e < KG ? score_k : score_v);
     for (int i = 0; i < QN; ++i) {
       float v = sc[i * NG + e];
       if (!part) v = -1.f;
@@ -895,8 +919,117 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   };
   if (tid < QN) sm.nsel[tid] = 0;
   __syncthreads();
+  // cached router, adaptive policy: attention entropy of each query over
+  // the valid tokens, -sum max(A, eps) log max(A, eps) (residual_router.py:369-376)
+  if (rp.legacy && rp.policy == CAREKV_POLICY_ADAPTIVE) {
+    for (int i = 0; i < QN; ++i) {
+      float ent = 0.f;
+      for (int x = tid; x < np * kPage; x += NT) {
+        const int p = x >> 4, t = x & (kPage - 1);
+        if (t < a.cache.valid[lhp * d.P + p]) {
+          const float av = fmaxf(attw(Wb[i * sst + p * kPage + tok_pos(t, a.s_perm)], i), kREps);
+          ent -= av * logf(av);
+        }
+      }
+      ent = warp_sum(ent);
+      if (lane == 0) sm.red[warp][i] = ent;
+    }
+    __syncthreads();
+    if (tid < QN) {
+      float e = 0.f;
+      for (int w = 0; w < NW; ++w) e += sm.red[w][tid];
+      sm.ent[tid] = e;
+    }
+    __syncthreads();
+  }
+  // Keep, of the selected entries of query i, those passing the
+  // adaptive_score thresholds per kind: score >= rel * the kind's top score
+  // and >= abs; a kind left with fewer than min_keep keeps its min_keep best
+  // (residual_router.py:393-433).  At most 32 entries (host-checked).
+  auto thresholds = [&](int i) {
+    if (warp == 0) {
+      const int n = sm.nsel[i];
+      const int e = lane < n ? sm.sel[i][lane] : 0x7fffffff;
+      const float sv = lane < n ? sc[i * NG + e] : -1.f;
+      const bool isk = lane < n && e < KG, isv = lane < n && e >= KG;
+      float topk = isk ? sv : -1.f, topv = isv ? sv : -1.f;
+      topk = warp_max(topk);
+      topv = warp_max(topv);
+      const float top = isk ? topk : topv;
+      const bool pass = (lane < n) && (rp.rel_threshold <= 0.f || sv >= rp.rel_threshold * top) &&
+                        (rp.abs_threshold <= 0.f || sv >= rp.abs_threshold);
+      int rank = 0;
+      for (int j = 0; j < n; ++j) {
+        const int ej = __shfl_sync(0xffffffffu, e, j);
+        const float sj = __shfl_sync(0xffffffffu, sv, j);
+        if ((ej < KG) == isk && (sj > sv || (sj == sv && ej < e))) ++rank;
+      }
+      const int npass = __popc(__ballot_sync(0xffffffffu, pass && isk)) * isk +
+                        __popc(__ballot_sync(0xffffffffu, pass && isv)) * isv;
+      const int nkind = __popc(__ballot_sync(0xffffffffu, isk)) * isk + __popc(__ballot_sync(0xffffffffu, isv)) * isv;
+      const bool keep = (lane < n) && (rp.min_keep > 0 && npass < rp.min_keep ? rank < min(rp.min_keep, nkind) : pass);
+      const unsigned km = __ballot_sync(0xffffffffu, keep);
+      const int pos = __popc(km & ((1u << lane) - 1u));
+      __syncwarp();
+      if (keep) {
+        sm.sel[i][pos] = e;
+        gsel_base[i * a.sel_stride + 1 + pos] = e;
+      }
+      __syncwarp();
+      if (lane == 0) sm.nsel[i] = __popc(km);
+    }
+    __syncthreads();
+  };
   for (int i = 0; i < QN; ++i) {
-    if (joint) {
+    if (rp.legacy) {
+      // ResidualRouter.route policies (residual_router.py:325-390)
+      if (rp.policy == CAREKV_POLICY_JOINT) {
+        const int mb = (bk > 0 && bv > 0) ? bk + bv : max(bk, bv);
+        pick(i, 0, NG, min(mb, n_k + n_v));
+      } else if (rp.policy == CAREKV_POLICY_K_FIRST) {
+        pick(i, 0, KG, bk);
+        const int rem = max(0, bk + bv - sm.nsel[i]);
+        if (rem > 0 && n_v > 0) {
+          // V candidates at or above the mean V score, best first
+          double vs = 0.0;
+          int vc = 0;
+          for (int e = KG + tid; e < NG; e += NT) {
+            const float v = sc[i * NG + e];
+            if (v >= 0.f) { vs += v; ++vc; }
+          }
+          for (int o = 16; o > 0; o >>= 1) {
+            vs += __shfl_xor_sync(0xffffffffu, vs, o);
+            vc += __shfl_xor_sync(0xffffffffu, vc, o);
+          }
+          if (lane == 0) { sm.vsum[warp] = vs; sm.scan[warp] = vc; }
+          __syncthreads();
+          double tv = 0.0;
+          int tc = 0;
+          for (int w = 0; w < NW; ++w) { tv += sm.vsum[w]; tc += sm.scan[w]; }
+          const double vmean = tc > 0 ? tv / tc : 0.0;
+          __syncthreads();
+          for (int e = KG + tid; e < NG; e += NT) {
+            const float v = sc[i * NG + e];
+            if (v >= 0.f && static_cast<double>(v) < vmean) sc[i * NG + e] = -1.f;
+          }
+          __syncthreads();
+          pick(i, KG, NG, rem);
+        }
+      } else if (rp.policy == CAREKV_POLICY_ADAPTIVE) {
+        const int tot = bk + bv;
+        if (tot > 0) {
+          const double vf = fmin(1.0, fmax(0.0, static_cast<double>(sm.ent[i]) / log(static_cast<double>(max(ntot_all, 2)))));
+          const int va = max(0, static_cast<int>(rint(tot * vf)));   // Python round: half to even
+          const int ka = max(0, tot - va);
+          pick(i, 0, KG, ka);
+          pick(i, KG, NG, va);
+        }
+      } else {
+        pick(i, 0, KG, bk);
+        pick(i, KG, NG, bv);
+      }
+      if (rp.adaptive_score) thresholds(i);
+    } else if (joint) {
       const int mb = (bk > 0 && bv > 0) ? bk + bv : max(bk, bv);
       pick(i, 0, NG, min(mb, n_k + n_v));
     } else {

@@ -11,13 +11,22 @@ whether a page can complete, so no call reads device memory back.
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import Optional, Sequence, Tuple
 
 import torch
 
 from . import _lib
 from .cache import CAREKVCache
-from .config import resolve_route_params, resolve_store_params
+from .config import legacy_router, resolve_route_params, resolve_store_params
+
+
+def decode_router(router: Optional[str] = None) -> str:
+    """The decode router: "vectorized" (default) or "cached"."""
+    r = (router or os.environ.get("CAREKV_DECODE_ROUTER", "vectorized")).lower()
+    if r not in ("vectorized", "cached"):
+        raise ValueError(f"decode router {r!r}: vectorized or cached")
+    return r
 
 _DT = {torch.float32: _lib.F32, torch.float16: _lib.F16, torch.bfloat16: _lib.BF16}
 
@@ -140,8 +149,12 @@ class DecodeEngine:
 
     def attend(self, layer: int, q: torch.Tensor, out: Optional[torch.Tensor] = None, seq_begin: int = 0,
                kind: Optional[str] = None, correction: bool = True, score_normalize=None, k_corr_scale=None,
-               pages: Optional[int] = None) -> torch.Tensor:
-        """Decode attention for [seq_count, Hq, D] queries against the cache."""
+               pages: Optional[int] = None, router: Optional[str] = None) -> torch.Tensor:
+        """Decode attention for [seq_count, Hq, D] queries against the cache.
+        router: "vectorized" (vectorized_joint_correction per kv head, the
+        default) or "cached" (the reference decode step's ResidualRouter.route
+        + apply_slot_corrections per query head); None reads
+        CAREKV_DECODE_ROUTER."""
         cfg = self.cfg
         n = q.shape[0]
         q = self._check_tensor(q, (n, self.kvh_total * self.qn, cfg.head_dim), "decode q")
@@ -150,7 +163,7 @@ class DecodeEngine:
         if pages is None:
             pages = max(1, max((self._pages(b, layer) for b in range(seq_begin, seq_begin + n)), default=1))
         rp = resolve_route_params(cfg, layer, kind=kind, score_normalize=score_normalize,
-                                  k_corr_scale=k_corr_scale)
+                                  k_corr_scale=k_corr_scale, legacy=decode_router(router) == "cached")
         if not correction:
             rp.kind = _lib.KIND_NONE
         nbytes = self.workspace_bytes(n, pages)
@@ -166,13 +179,16 @@ class DecodeEngine:
                         logits: Optional[torch.Tensor] = None, row_max: Optional[torch.Tensor] = None,
                         v_rows: Optional[torch.Tensor] = None, v_pnorm: Optional[torch.Tensor] = None,
                         out: Optional[torch.Tensor] = None, kind: Optional[str] = None, score_normalize=None,
-                        k_corr_scale=None) -> torch.Tensor:
+                        k_corr_scale=None, legacy: Optional[bool] = None) -> torch.Tensor:
         """Stored-slot correction of a prefill (layer.py:458-637): one route /
         correct pass per (prefill position, kv head) over the slots of
         sequence `seq`.  With P = the sequence's pages and QN = Hq / Hkv:
         q [T, Hq, D]; attn, logits [T, Hkv, QN, P*16] fp32; attn_sum, row_max
         [T, Hkv, QN] fp32; o_base, o_exact [T, Hkv, QN, D] fp32; v_rows
-        [Hkv, P*16, D] fp32; v_pnorm [Hkv, P] fp32.  Returns [T, Hq, D]."""
+        [Hkv, P*16, D] fp32; v_pnorm [Hkv, P] fp32.  Returns [T, Hq, D].
+        legacy: the cached router (ResidualRouter.route per query, the
+        reference's prefill correction unless correction_impl is
+        "vectorized", layer.py:522-630); None follows cfg.correction_impl."""
         cfg = self.cfg
         T = q.shape[0]
         H, QN, D = cfg.num_kv_heads, cfg.num_heads // cfg.num_kv_heads, cfg.head_dim
@@ -199,7 +215,10 @@ class DecodeEngine:
         v_pnorm = f32(v_pnorm, (H, P), "v_pnorm")
         if out is None:
             out = torch.empty_like(q)
-        rp = resolve_route_params(cfg, layer, kind=kind, score_normalize=score_normalize, k_corr_scale=k_corr_scale)
+        if legacy is None:
+            legacy = legacy_router(cfg)
+        rp = resolve_route_params(cfg, layer, kind=kind, score_normalize=score_normalize, k_corr_scale=k_corr_scale,
+                                  legacy=legacy)
         n = ctypes.c_size_t(0)
         _lib.check(_lib.lib().carekv_prefill_workspace_bytes(ctypes.byref(self.cache.ccfg), T, P, ctypes.byref(n)),
                    "carekv_prefill_workspace_bytes")
@@ -340,7 +359,7 @@ class DecodeStepGraph:
         self.store_params = [resolve_store_params(self.cfg, l, dt) for l in range(self.L)]
         self.route_params = []
         for l in range(self.L):
-            rp = resolve_route_params(self.cfg, l)
+            rp = resolve_route_params(self.cfg, l, legacy=decode_router() == "cached")
             if not correction:
                 rp.kind = _lib.KIND_NONE
             self.route_params.append(rp)

@@ -166,7 +166,29 @@ typedef struct carekv_route_params {
     float   sensitivity;
     float   lambda_k;
     float   lambda_v;
+    /* The cached router (correction_impl "python" / "cached"): when legacy is
+     * 1 the selection follows ResidualRouter.route (residual_router.py:88-452)
+     * and the correction apply_slot_corrections (attention.py:208-374): K
+     * slots scored from their sketches (kscore_live must be 0), score
+     * normalisation whenever kind is "both", the policies below, and the
+     * adaptive_score thresholds on the selected slots.  0: the vectorized
+     * router (attention.py:576-957). */
+    int32_t legacy;
+    int32_t policy;           /* legacy: CAREKV_POLICY_*                            */
+    int32_t baseline_score;   /* legacy: CAREKV_SCORE_* (baseline_score ablations)  */
+    int32_t adaptive_score;   /* legacy: 1 = read_budget_mode "adaptive_score"      */
+    float   rel_threshold;    /* read_relative_threshold                            */
+    float   abs_threshold;    /* read_absolute_threshold                            */
+    int32_t min_keep;         /* read_min_keep                                      */
 } carekv_route_params_t;
+#define CAREKV_POLICY_SEPARATE 0
+#define CAREKV_POLICY_JOINT    1
+#define CAREKV_POLICY_K_FIRST  2
+#define CAREKV_POLICY_ADAPTIVE 3
+#define CAREKV_SCORE_CAREKV         0   /* mass x |q.k sketch| x boundary x V diff x sens */
+#define CAREKV_SCORE_MAGNITUDE_ONLY 1
+#define CAREKV_SCORE_ATTENTION_ONLY 2
+#define CAREKV_SCORE_ORACLE_PROXY   3
 
 /* ABI version and a static string for a status code. */
 int carekv_abi_version(void);

@@ -432,6 +432,93 @@ def gen_kivi_store(out):
     print("kivi_store.npz", len(cases), "cases")
 
 
+# ───────────────────────────── legacy cached router ─────────────────────────────
+LEGACY_CASES = [
+    # name, D, Hkv, T, store (k, v), read mode, rk, rv, ratio, policy, normalize, kmode, kind, baseline,
+    # rel, abs, min_keep
+    ("joint_norm_exact", 64, 2, 150, (2, 2), "absolute", 2, 2, 0.03, "joint", True, "exact", "both", "carekv", 0, 0, 0),
+    ("separate_linear", 64, 2, 150, (2, 2), "absolute", 2, 3, 0.03, "separate", False, "linear", "both", "carekv",
+     0, 0, 0),
+    ("k_first_exact", 64, 2, 150, (2, 2), "absolute", 2, 3, 0.03, "k_first", True, "exact", "both", "carekv", 0, 0, 0),
+    ("adaptive_exact", 64, 2, 150, (2, 2), "absolute", 3, 3, 0.03, "adaptive", True, "exact", "both", "carekv",
+     0, 0, 0),
+    ("ratio_joint_d128", 128, 1, 260, (1, 1), "ratio", 0, 0, 0.05, "joint", True, "exact", "both", "carekv", 0, 0, 0),
+    ("adaptive_score", 64, 2, 150, (2, 2), "adaptive_score", 3, 3, 0.03, "separate", True, "exact", "both", "carekv",
+     0.3, 0.0, 1),
+    ("magnitude_only", 64, 2, 150, (2, 2), "absolute", 2, 2, 0.03, "joint", True, "exact", "both", "magnitude_only",
+     0, 0, 0),
+    ("attention_only", 64, 2, 150, (2, 2), "absolute", 2, 2, 0.03, "separate", False, "linear", "both",
+     "attention_only", 0, 0, 0),
+    ("oracle_proxy", 64, 2, 150, (2, 2), "absolute", 2, 2, 0.03, "joint", True, "exact", "both", "oracle_proxy",
+     0, 0, 0),
+    ("kind_v", 64, 2, 150, (2, 2), "absolute", 2, 2, 0.03, "joint", False, "exact", "v", "carekv", 0, 0, 0),
+    ("kind_k_joint_one_budget", 64, 2, 150, (2, 2), "absolute", 2, 0, 0.03, "joint", True, "exact", "k", "carekv",
+     0, 0, 0),
+]
+
+
+def gen_legacy(out):
+    """ResidualRouter.route + apply_slot_corrections through the reference's
+    per-query-head CAREKVAttention.forward (attention.py:979-1039) on a
+    prefilled cache with sketches, several queries per kv head."""
+    import torch
+    from CARE_KV.care_kv.cache import CacheConfig, CAREKVCache
+    from CARE_KV.care_kv.attention import CAREKVAttention
+    arrays, cases = {}, []
+    os.environ["CAREKV_STORE_POLICY"] = "residual_kind_aware"
+    os.environ["CAREKV_PREFILL_RESIDUAL_KIND"] = "both"
+    for ci, (name, D, Hkv, T, (sk, sv), rmode, rk, rv, ratio, policy, norm, kmode, kind, base, rel, ab,
+             mk) in enumerate(LEGACY_CASES):
+        os.environ["CAREKV_K_CORRECTION_MODE"] = kmode
+        Hq = Hkv * 2
+        cfg = CacheConfig(num_layers=1, num_heads=Hq, num_kv_heads=Hkv, head_dim=D, page_size=16, max_pages=24,
+                          base_bits=3, group_size=32, k_channel_group=32, v_token_block=4, sketch_dim=32,
+                          packed_base=True, scale_quant="int8", store_budget_mode="absolute", store_abs_k=sk,
+                          store_abs_v=sv, read_budget_mode=rmode, read_abs_k=rk, read_abs_v=rv,
+                          read_budget_ratio=ratio, route_policy=policy, baseline_score=base,
+                          read_relative_threshold=float(rel), read_absolute_threshold=float(ab), read_min_keep=mk)
+        layer = make_layer(cfg, Hq, Hkv, D, "fp32", 700 + ci)
+        cache = CAREKVCache(cfg)
+        g = torch.Generator().manual_seed(800 + ci)
+        K = torch.randn(Hkv, T, D, generator=g)
+        K[:, :, :4] *= 20.0
+        V = torch.randn(Hkv, T, D, generator=g)
+        for h in range(Hkv):
+            layer._write_pages_for_kv_head(cache, h, K[h], V[h], token_start_abs=0, sink_tokens=4)
+        att = CAREKVAttention(cfg, 0, torch.device("cpu"))
+        rec = {}
+        orig = att.router.route
+
+        def route(*a, **kw):
+            r = orig(*a, **kw)
+            rec["sel"] = r
+            return r
+        att.router.route = route
+        key = f"g{ci}"
+        arrays[key + "_K"] = as_np(K)
+        arrays[key + "_V"] = as_np(V)
+        Q = torch.randn(Hkv, 4, D, generator=g)
+        Q[:, 1] *= 3.0                   # sharper attention for the second query of each head
+        arrays[key + "_Q"] = as_np(Q)
+        outs, sels = [], []
+        for h in range(Hkv):
+            for j in range(4):
+                rec.clear()
+                o = att.forward(cache, h, Q[h, j], kind=kind, k_corr_scale=0.1, score_normalize=norm)
+                outs.append(as_np(o))
+                ksel, vsel = rec.get("sel", ([], []))
+                sels.append(dict(k=[list(map(int, x)) for x in ksel], v=[list(map(int, x)) for x in vsel]))
+        arrays[key + "_O"] = np.stack(outs)
+        arrays[key + "_sel"] = np.array(json.dumps(sels))
+        cases.append(dict(key=key, name=name, D=D, Hkv=Hkv, T=T, store_abs_k=sk, store_abs_v=sv, read_mode=rmode,
+                          read_abs_k=rk, read_abs_v=rv, ratio=ratio, policy=policy, normalize=norm, kmode=kmode,
+                          kind=kind, baseline=base, rel=rel, abs=ab, min_keep=mk, k_corr_scale=0.1))
+    os.environ["CAREKV_K_CORRECTION_MODE"] = "exact"
+    arrays["meta"] = np.array(json.dumps(cases))
+    np.savez_compressed(os.path.join(out, "legacy_router.npz"), **arrays)
+    print("legacy_router.npz", len(cases), "cases")
+
+
 # ───────────────────────────── layer ─────────────────────────────
 def gen_layer(out):
     """CAREKVLayer.prefill + decode_step of the reference (layer.py:643-1163)."""
@@ -472,7 +559,7 @@ def main():
     ap.add_argument("--reference", default=os.environ.get("CAREKV_REFERENCE"),
                     help="root of the reference project checkout (or set CAREKV_REFERENCE)")
     ap.add_argument("--out", default=HERE)
-    ap.add_argument("--only", default="", help="comma list of quant,store,correction,layer,kivi,kivi_store")
+    ap.add_argument("--only", default="", help="comma list of quant,store,correction,layer,kivi,kivi_store,legacy")
     a = ap.parse_args()
     if not a.reference:
         ap.error("give --reference (or CAREKV_REFERENCE): the reference checkout the fixtures come from")
@@ -481,7 +568,7 @@ def main():
     torch.set_num_threads(min(8, os.cpu_count() or 1))
     only = set(x for x in a.only.split(",") if x)
     for nm, fn in (("quant", gen_quant), ("store", gen_store), ("correction", gen_correction), ("layer", gen_layer),
-                   ("kivi", gen_kivi), ("kivi_store", gen_kivi_store)):
+                   ("kivi", gen_kivi), ("kivi_store", gen_kivi_store), ("legacy", gen_legacy)):
         if not only or nm in only:
             fn(a.out)
 

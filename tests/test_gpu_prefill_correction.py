@@ -85,7 +85,7 @@ def test_prefill_correction_matches_oracle(pkg, case):
         cfg = pkg.CacheConfig(num_layers=1, num_heads=Hq, num_kv_heads=Hkv, head_dim=D, page_size=16,
                               max_pages=T // 16 + 2, base_bits=bits, group_size=g, scale_quant="int8",
                               store_budget_mode="absolute", store_abs_k=sk, store_abs_v=sv, route_policy=policy,
-                              sketch_dim=32, store_sketch=not live, **read)
+                              sketch_dim=32, store_sketch=not live, correction_impl="vectorized", **read)
         dev = torch.device("cuda")
         cache = pkg.CAREKVCache(cfg, dev, batch=1)
         eng = pkg.DecodeEngine(cache)

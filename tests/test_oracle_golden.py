@@ -225,3 +225,44 @@ def test_kivi_store_and_decode_golden(ci):
             tol = {"fp32": 1e-5, "fp16": 2e-3, "bf16": 8e-3}[dt]
             np.testing.assert_allclose(oracle.round_to(O, dt), O_ref[h * grp:(h + 1) * grp], rtol=tol, atol=tol)
     _check_kivi_cache(oc, z, key + "d")
+
+
+def _legacy_setup(c, z):
+    from oracle.legacy_router import legacy_correction  # noqa: F401
+    sc = StoreConfig(head_dim=c["D"], base_bits=3, group_size=32, store_abs_k=c["store_abs_k"],
+                     store_abs_v=c["store_abs_v"], store_budget_mode="absolute", sketch_dim=32)
+    oc = OracleCache(1, c["Hkv"], c["D"], 24, sc, scale_quant="int8")
+    K, V = z[c["key"] + "_K"], z[c["key"] + "_V"]
+    for h in range(c["Hkv"]):
+        oc.prefill_write(0, h, K[h], V[h], "fp32")
+    rc = RouteConfig(head_dim=c["D"], kind=c["kind"], route_policy=c["policy"], score_normalize=c["normalize"],
+                     k_correction_mode=c["kmode"], read_budget_mode=c["read_mode"], read_abs_k=c["read_abs_k"],
+                     read_abs_v=c["read_abs_v"], read_budget_ratio=c["ratio"])
+    return oc, rc
+
+
+@pytest.mark.parametrize("ci", range(11))
+def test_legacy_router_golden(ci):
+    """The legacy cached router (ResidualRouter.route + apply_slot_corrections)
+    against the reference's per-query-head decode attention."""
+    from oracle.legacy_router import legacy_correction
+    z, cases = _load("legacy_router.npz")
+    c = cases[ci]
+    oc, rc = _legacy_setup(c, z)
+    sels = json.loads(str(z[c["key"] + "_sel"]))
+    Q = z[c["key"] + "_Q"]
+    n = 0
+    for h in range(c["Hkv"]):
+        K_hat, V_hat, _ = oc.read_base_concat(0, h)
+        for j in range(Q.shape[1]):
+            q = Q[h, j]
+            S, A, O = oracle.base_attention(K_hat, V_hat, q[None], c["D"])
+            d, info = legacy_correction(oc, 0, h, q, S[0], A[0], O[0], V_hat, rc, oc.sketch_P, kind=c["kind"],
+                                        score_normalize=c["normalize"], k_corr_scale=c["k_corr_scale"],
+                                        exact=c["kmode"] == "exact", baseline=c["baseline"], rel_thr=c["rel"],
+                                        abs_thr=c["abs"], min_keep=c["min_keep"])
+            want = sels[n]
+            assert sorted(map(list, info["k_sel"])) == sorted(want["k"]), (h, j, info["k_sel"], want["k"])
+            assert sorted(map(list, info["v_sel"])) == sorted(want["v"]), (h, j, info["v_sel"], want["v"])
+            np.testing.assert_allclose(O[0] + d, z[c["key"] + "_O"][n], rtol=1e-4, atol=1e-5, err_msg=f"{h} {j}")
+            n += 1
