@@ -19,6 +19,13 @@ cudaError_t launch_prefill_store(const carekv_config_t& cfg, const carekv_cache_
                                  const void* V, int T, int seq_begin, int seq_count,
                                  const carekv_store_params_t& prm, const float* sketch_proj, int in_H,
                                  cudaStream_t st);
+// the warp-per-page prefill store (store_warp.cu) and the configurations
+// and inputs it takes (else launch_prefill_store runs page_store_kernel)
+bool prefill_store_warp_supported(const carekv_config_t& cfg, const carekv_cache_t& cache, const void* K,
+                                  const void* V, const carekv_store_params_t& prm);
+cudaError_t launch_prefill_store_warp(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer,
+                                      const void* K, const void* V, int T, int seq_begin, int seq_count,
+                                      const carekv_store_params_t& prm, int in_H, cudaStream_t st);
 cudaError_t launch_append(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* k,
                           const void* v, int seq_begin, int seq_count, const carekv_store_params_t& prm,
                           const float* sketch_proj, int may_fill, int in_H, cudaStream_t st);
@@ -29,8 +36,8 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
                      const carekv_route_params_t& rp, void* ws, size_t ws_bytes, const float* sketch_proj,
                      int act_heads, cudaStream_t st);
 size_t workspace_bytes(const carekv_config_t& c, int seq_count, int p_used);
-void prepare_decode_streams();
-int decode_attention_chunks(int seq_count);   // batch chunks one decode attention call runs   // creates the chunk streams of the current device (not under capture)
+void prepare_decode_streams();               // creates the chunk streams of the current device (not under capture)
+int decode_attention_chunks(int seq_count);   // batch chunks one decode attention call runs
 size_t prefill_workspace_bytes(const carekv_config_t& c, int n_pos, int p_used);
 int prefill_correction(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, int seq, int n_pos,
                        int p_used, const void* q, const float* logits, const float* row_max, const float* A,

@@ -1,6 +1,9 @@
 // Route + correct kernel (K4 + K2) after every split-K pass: one CTA of
-// kRouteWarps warps per (sequence, kv head) runs route_body (route_body.cuh);
-// small CTAs with per-QN scratch keep 8 of them resident per SM.
+// kRouteWarps warps per (sequence, kv head, query head) runs route_body
+// (route_body.cuh) -- the query heads of a GQA group route independently
+// (per-query scores, budgets and top-k), so a group of QN heads takes QN
+// CTAs in parallel; small CTAs keep 8 of them resident per SM.  The prefill
+// correction keeps a group in one CTA.
 #include "common.cuh"
 #include "internal.h"
 #include "decode_args.h"
@@ -22,12 +25,15 @@ __global__ void __launch_bounds__(kRouteWarps * 32, 8) route_kernel2(DecodeArgs 
 template <int QN>
 cudaError_t launch_route(DecodeArgs& a, cudaStream_t st, int n_bh) {
   const int NG = a.p_used * (a.cfg.k_slots_per_page + a.cfg.v_slots_per_page);
-  const size_t sc_bytes = static_cast<size_t>(QN) * NG * sizeof(float);
-  const int in_smem = sc_bytes + sizeof(RouteSmem<QN, kRouteWarps>) <= 46 * 1024 ? 1 : 0;
-  if (a.attn != nullptr)
+  if (a.attn != nullptr) {
+    const size_t sc_bytes = static_cast<size_t>(QN) * NG * sizeof(float);
+    const int in_smem = sc_bytes + sizeof(RouteSmem<QN, kRouteWarps>) <= 46 * 1024 ? 1 : 0;
     route_kernel2<QN, true><<<n_bh, kRouteWarps * 32, in_smem ? sc_bytes : 0, st>>>(a, in_smem);
-  else
-    route_kernel2<QN, false><<<n_bh, kRouteWarps * 32, in_smem ? sc_bytes : 0, st>>>(a, in_smem);
+  } else {
+    const size_t sc_bytes = static_cast<size_t>(NG) * sizeof(float);
+    const int in_smem = sc_bytes + sizeof(RouteSmem<1, kRouteWarps>) <= 46 * 1024 ? 1 : 0;
+    route_kernel2<1, false><<<dim3(n_bh, QN), kRouteWarps * 32, in_smem ? sc_bytes : 0, st>>>(a, in_smem);
+  }
   return cudaGetLastError();
 }
 

@@ -1,6 +1,7 @@
-// Route + correct (kernels K4 + K2) for one (sequence, kv head), as a
-// device function of NW warps; route_kernel2 (route.cu) runs it with one CTA
-// of 8 warps per (sequence, kv head) after every split-K pass.
+// Route + correct (kernels K4 + K2) for QN query heads of one (sequence,
+// kv head), as a device function of NW warps; route_kernel2 (route.cu) runs
+// it with one CTA per (sequence, kv head, query head) after every split-K
+// pass, and with one CTA per (position, kv head) for the prefill correction.
 //
 //  1. merge the split-K partials into O_base, M and L;
 //  2. score every stored residual slot: K slots with combined_kvscore
@@ -197,6 +198,11 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   const int b = PF && a.seq_fixed >= 0 ? a.seq_fixed : a.seq_begin + s;
   const int D = d.D;
   const int Hq = a.act_heads;   // query heads per activation row
+  // this CTA's query heads: q0 .. q0 + QN - 1 of the kv head's group of QG
+  // (decode splits a group over gridDim.y CTAs, one query head each; the
+  // prefill correction keeps the group in one CTA)
+  const int QG = PF ? QN : QN * static_cast<int>(gridDim.y);
+  const int q0 = PF ? 0 : QN * static_cast<int>(blockIdx.y);
   const int64_t lhp = d.lhp(b, a.layer, h);
   const int np = min(a.cache.num_pages[lhp], a.p_used);
   const carekv_route_params_t& rp = a.rp;
@@ -204,18 +210,18 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   // ── 1. queries and the merged split-K partials ──
   for (int idx = tid; idx < QN * D; idx += NT) {
     const int i = idx / D, c = idx % D;
-    sm.Q[i][c] = load_act(a.q, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + c, a.dt);
+    sm.Q[i][c] = load_act(a.q, (static_cast<int64_t>(s) * Hq + h * QG + q0 + i) * D + c, a.dt);
   }
   // every (query, channel) thread loads all splits' m, l and its O entry at
   // once (one round trip) and merges them; channel 0 publishes M, L
   if (tid == 0) { sm.cnt_k = 0; sm.cnt_v = 0; sm.ntot = 0; sm.any_k = 0; }
   for (int idx = tid; idx < QN * D; idx += NT) {
     const int i = idx / D, c = idx % D;
-    const int64_t base = static_cast<int64_t>(bh) * a.n_splits * QN + i;
+    const int64_t base = static_cast<int64_t>(bh) * a.n_splits * QG + q0 + i;
     if (po_direct) {   // po holds the base output itself, pm the logit row maxima (prefill)
-      sm.O[i][c] = a.po[(static_cast<int64_t>(bh) * QN + i) * D + c];
+      sm.O[i][c] = a.po[(static_cast<int64_t>(bh) * QG + q0 + i) * D + c];
       if (c == 0) {
-        sm.M[i] = a.pm ? a.pm[static_cast<int64_t>(bh) * QN + i] : 0.f;
+        sm.M[i] = a.pm ? a.pm[static_cast<int64_t>(bh) * QG + q0 + i] : 0.f;
         sm.L[i] = 1.f;
         sm.invL[i] = 1.f;
         sm.mlb[i] = 0.f;
@@ -223,15 +229,15 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       continue;
     }
     float M = -INFINITY;
-    for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, a.pm[base + sp * QN]);
+    for (int sp = 0; sp < a.n_splits; ++sp) M = fmaxf(M, a.pm[base + sp * QG]);
     float L = 0.f, O = 0.f;
     if (M != -INFINITY) {
       for (int sp = 0; sp < a.n_splits; ++sp) {
-        const float m = a.pm[base + sp * QN];
+        const float m = a.pm[base + sp * QG];
         if (m == -INFINITY) continue;
         const float f = rex2((m - M) * kRL2e);
-        L += a.pl[base + sp * QN] * f;
-        O += a.po[(base + sp * QN) * D + c] * f;
+        L += a.pl[base + sp * QG] * f;
+        O += a.po[(base + sp * QG) * D + c] * f;
       }
       O = __fdiv_rn(O, L);
     }
@@ -267,10 +273,10 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   __syncthreads();
 
   auto write_base = [&]() {
-    if (tid < QN) a.sel_out[(static_cast<int64_t>(bh) * QN + tid) * a.sel_stride] = 0;
+    if (tid < QN) a.sel_out[(static_cast<int64_t>(bh) * QG + q0 + tid) * a.sel_stride] = 0;
     for (int idx = tid; idx < QN * D; idx += NT) {
       const int i = idx / D, c = idx % D;
-      store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + c, sm.O[i][c], a.dt);
+      store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QG + q0 + i) * D + c, sm.O[i][c], a.dt);
     }
   };
   if (np == 0 || rp.kind == CAREKV_KIND_NONE) {
@@ -281,10 +287,10 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   const int KG = a.p_used * d.SK;
   const int VG = a.p_used * d.SV;
   const int NG = KG + VG;
-  float* sc = scores_in_smem ? dyn : a.scores + static_cast<int64_t>(bh) * QN * NG;
-  const float* Sb = a.S + static_cast<int64_t>(bh) * QN * a.p_used * kPage;
+  float* sc = scores_in_smem ? dyn : a.scores + (static_cast<int64_t>(bh) * QG + q0) * NG;
+  const float* Sb = a.S + (static_cast<int64_t>(bh) * QG + q0) * a.p_used * kPage;
   // weights source: A itself when given (read through attw), else the logits
-  const float* Wb = A_in ? A_in + static_cast<int64_t>(bh) * QN * a.p_used * kPage : Sb;
+  const float* Wb = A_in ? A_in + (static_cast<int64_t>(bh) * QG + q0) * a.p_used * kPage : Sb;
   const int64_t sst = static_cast<int64_t>(a.p_used) * kPage;
   const bool kind_k = rp.kind == CAREKV_KIND_BOTH || rp.kind == CAREKV_KIND_K;
   const bool kind_v = rp.kind == CAREKV_KIND_BOTH || rp.kind == CAREKV_KIND_V;
@@ -339,7 +345,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         for (int j = 0; j < d.SK; ++j) {
           const int e = p * d.SK + j;
           const int grp = live ? a.cache.k_slot_group[pg * d.SK + j] : -1;
-          const float4* wrow = reinterpret_cast<const float4*>(a.kw + ((static_cast<int64_t>(bh) * QN + i) * KG + e) * kPage);
+          const float4* wrow = reinterpret_cast<const float4*>(a.kw + ((static_cast<int64_t>(bh) * QG + q0 + i) * KG + e) * kPage);
           // ||dS * A(1-A)|| with dS = q.R_K / sqrt(D): the 1/sqrt(D) is
           // applied to the root
           float ss = 0.f;
@@ -404,33 +410,52 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
     // ||dS * A(1-A)|| over the page's valid tokens * ||V_page||_F * sens.
     const int gid = lane >> 2, tig = lane & 3;
     int cnt = 0;
-    for (int e = warp; e < KG; e += NW) {
+    // Every load of a slot is issued at once: the arena rows exist for every
+    // page below max_pages, so none waits on the slot's group or the page's
+    // count.
+    struct SlotLd {
+      int grp, nv;
+      uint32_t w0, w1;
+      uint16_t rs;
+      float vn, s4[4];
+    };
+    auto slot_load = [&](int e, SlotLd& x) {
       const int p = e / d.SK, j = e % d.SK;
       const int64_t pg = lhp * d.P + p;
-      int grp = -1, nv = 0;
-      if (p < np) {
-        grp = a.cache.k_slot_group[pg * d.SK + j];
-        nv = a.cache.valid[pg];
+      const bool live = e < KG && p < np;
+      const int64_t si = live ? pg * d.SK + j : 0;
+      const int64_t pgl = live ? pg : 0;
+      x.grp = live ? a.cache.k_slot_group[si] : -1;
+      x.nv = live ? a.cache.valid[pgl] : 0;
+      const uint8_t* pay = a.cache.k_slot_data + si * d.kslot_bytes;
+      x.w0 = *reinterpret_cast<const uint32_t*>(pay + gid * 16 + 4 * tig);
+      x.w1 = *reinterpret_cast<const uint32_t*>(pay + (gid + 8) * 16 + 4 * tig);
+      x.rs = a.cache.k_slot_scale[si];
+      x.vn = v_pnorm ? (live ? v_pnorm[h * a.p_used + p] : 0.f) : a.cache.v_norm2[pgl];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x.s4[u] = 0.f;
+      if (gid < QN && live) {
+        const float* srow = Wb + gid * sst + p * kPage;
+        x.s4[0] = srow[tok_pos(2 * tig, a.s_perm)];
+        x.s4[1] = srow[tok_pos(2 * tig + 1, a.s_perm)];
+        x.s4[2] = srow[tok_pos(8 + 2 * tig, a.s_perm)];
+        x.s4[3] = srow[tok_pos(9 + 2 * tig, a.s_perm)];
       }
+    };
+    for (int e = warp; e < KG; e += NW) {
+      SlotLd cur;
+      slot_load(e, cur);
+      const int grp = cur.grp, nv = cur.nv;
       const bool ok = grp >= 0 && nv > 0;
       cnt += ok;
       if (!ok || !may_k) {
         if (lane < QN) sc[lane * NG + e] = -1.f;
         continue;
       }
-      const uint8_t* pay = a.cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes;
-      const uint32_t w0 = *reinterpret_cast<const uint32_t*>(pay + gid * 16 + 4 * tig);
-      const uint32_t w1 = *reinterpret_cast<const uint32_t*>(pay + (gid + 8) * 16 + 4 * tig);
-      const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
-      const float vc = v_pnorm ? v_pnorm[h * a.p_used + p] : sqrtf(a.cache.v_norm2[pg]);
-      float s4[4] = {0.f, 0.f, 0.f, 0.f};
-      if (gid < QN) {
-        const float* srow = Wb + gid * sst + p * kPage;
-        s4[0] = srow[tok_pos(2 * tig, a.s_perm)];
-        s4[1] = srow[tok_pos(2 * tig + 1, a.s_perm)];
-        s4[2] = srow[tok_pos(8 + 2 * tig, a.s_perm)];
-        s4[3] = srow[tok_pos(9 + 2 * tig, a.s_perm)];
-      }
+      const uint32_t w0 = cur.w0, w1 = cur.w1;
+      const float rs = f16_bits_to_f32(cur.rs);
+      const float vc = v_pnorm ? cur.vn : sqrtf(cur.vn);
+      const float s4[4] = {cur.s4[0], cur.s4[1], cur.s4[2], cur.s4[3]};
       float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int ks = 0; ks < 2; ++ks) {
@@ -701,7 +726,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   // running list); warp 0 merges the warps' lists the same way.  Excluded
   // entries hold a negative score and sort last.
   // Publish the first n of a sorted list (one element per lane) into sel[i].
-  int* const gsel_base = a.sel_out + static_cast<int64_t>(bh) * QN * a.sel_stride;
+  int* const gsel_base = a.sel_out + (static_cast<int64_t>(bh) * QG + q0) * a.sel_stride;
   auto publish = [&](int i, float mv, int mi, int k) {
     const int base = sm.nsel[i];
     int n = __popc(__ballot_sync(0xffffffffu, mv >= 0.f));
@@ -1039,7 +1064,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
   }
   if (tid < QN) gsel_base[tid * a.sel_stride] = sm.nsel[tid];
   if (scores_in_smem) {
-    float* g = a.scores + static_cast<int64_t>(bh) * QN * NG;
+    float* g = a.scores + (static_cast<int64_t>(bh) * QG + q0) * NG;
     for (int e = tid; e < QN * NG; e += NT) g[e] = sc[e];
   }
   __syncthreads();
@@ -1102,7 +1127,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       for (int j = 0; j < d.SK; ++j) {
         if (!((mask >> j) & 1)) continue;
         if (a.kw != nullptr) {
-          acc += a.kw[((static_cast<int64_t>(bh) * QN + i) * KG + p * d.SK + j) * kPage + tok_pos(t, a.s_perm)];
+          acc += a.kw[((static_cast<int64_t>(bh) * QG + q0 + i) * KG + p * d.SK + j) * kPage + tok_pos(t, a.s_perm)];
           continue;
         }
         const int grp = a.cache.k_slot_group[pg * d.SK + j];
@@ -1447,34 +1472,60 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         if (e < KG) atomicOr(&kbits[(e / d.SK) >> 5], 1u << ((e / d.SK) & 31));
       }
       __syncthreads();
+      // Lane l decodes channels 4l .. 4l+3 of every row (one scale group):
+      // a page's weights, then 4 rows' code windows and scales at a time.
+      // Per channel the pages and rows are summed in the same order as
+      // token-serial decoding.
       float o2[4] = {0.f, 0.f, 0.f, 0.f}, z2 = 0.f;
+      const int cb = 4 * lane;                 // first channel of the lane
+      const bool cl = cb < D;
+      const int b0 = cb * d.bits;              // its bit offset in a packed row
+      const int wsh = b0 & 31;
+      const bool two = wsh + 4 * d.bits > 32;  // the 4 codes straddle a 32-bit word
+      const uint32_t cmask = (1u << d.bits) - 1u, csign = 1u << (d.bits - 1);
       for (int p = warp; p < np; p += NW) {
         if ((kbits[p >> 5] >> (p & 31)) & 1u) continue;
         const int64_t pg = lhp * d.P + p;
         const int nv = a.cache.valid[pg];
         const float vm = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
-        for (int t = 0; t < nv; ++t) {
-          const float A = attw(Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)], i);
-          z2 += A;
-          const uint8_t* vr = a.cache.v_codes + (pg * kPage + t) * R;
-          const int64_t srow = (pg * kPage + t) * G;
+        // token weights on lanes 0..15 (every logit row exists up to p_used)
+        const float sv = Sb[i * sst + p * kPage + tok_pos(lane & 15, a.s_perm)];
+        const float At = (lane & 15) < nv ? attw(sv, i) : 0.f;
+        // rows four at a time, each group's code windows and scales loaded at once
+#pragma unroll 1
+        for (int t0 = 0; t0 < kPage; t0 += 4) {
+          if (t0 >= nv) break;
+          uint32_t wlo[4], whi[4];
+          float vs[4];
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const int c = lane + 32 * jj;
-            if (c < D) {
-              const int cv = unpack_code(vr, c, d.bits);
-              const float vh = d.kivi ? f16r(kivi_hat(cv, reinterpret_cast<const float*>(a.cache.v_scale)[srow], a.dt))
-                                      : f16r(__fmul_rn(static_cast<float>(cv),
-                                                       read_scale(a.cache.v_scale, srow + c / d.gsize, d.scale_mode, vm)));
-              o2[jj] = fmaf(A, vh, o2[jj]);
+          for (int u = 0; u < 4; ++u) {
+            const int64_t rw = pg * kPage + t0 + u;
+            const uint32_t* row = reinterpret_cast<const uint32_t*>(a.cache.v_codes + rw * R);
+            wlo[u] = cl ? row[b0 >> 5] : 0u;
+            whi[u] = cl && two ? row[(b0 >> 5) + 1] : 0u;
+            vs[u] = !cl ? 0.f
+                        : (d.kivi ? reinterpret_cast<const float*>(a.cache.v_scale)[rw * G]
+                                  : read_scale(a.cache.v_scale, rw * G + cb / d.gsize, d.scale_mode, vm));
+          }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (t0 + u >= nv) break;
+            const float A = __shfl_sync(0xffffffffu, At, t0 + u);
+            z2 += A;
+            const uint32_t win = __funnelshift_r(wlo[u], whi[u], wsh);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const uint32_t cu = (win >> (k * d.bits)) & cmask;
+              const int cv = static_cast<int>(cu) - static_cast<int>((cu & csign) << 1);
+              const float vh = d.kivi ? f16r(kivi_hat(cv, vs[u], a.dt)) : f16r(__fmul_rn(static_cast<float>(cv), vs[u]));
+              o2[k] = fmaf(A, vh, o2[k]);
             }
           }
         }
       }
+      if (cl) {
 #pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const int c = lane + 32 * jj;
-        if (c < D) sm.acc2[warp][c] = o2[jj];
+        for (int k = 0; k < 4; ++k) sm.acc2[warp][cb + k] = o2[k];
       }
       if (lane == 0) sm.z2[warp] = z2;
     }
@@ -1499,7 +1550,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       const float ob = sm.O[i][tid];
       // exact form: a_new @ V = (cbase * sum_t A V + num) / (cbase * sum_t A + z); sum_t A V and
       // sum_t A are O and 1 in decode, given by the caller in the prefill correction
-      const int64_t row = static_cast<int64_t>(bh) * QN + i;
+      const int64_t row = static_cast<int64_t>(bh) * QG + q0 + i;
       const float oe = o_exact ? o_exact[row * D + tid] : ob;
       const float as = (po_direct && a.pl) ? a.pl[row] : 1.f;
       float delta;
@@ -1511,7 +1562,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       } else {
         delta = exact ? (__fdiv_rn(fmaf(cbase, oe, n), fmaf(cbase, as, z)) - ob) : (n - z * ob);
       }
-      store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + tid, ob + delta, a.dt);
+      store_act(a.out, (static_cast<int64_t>(s) * Hq + h * QG + q0 + i) * D + tid, ob + delta, a.dt);
     }
     __syncthreads();
   }

@@ -838,9 +838,14 @@ cudaError_t launch_prefill_store(const carekv_config_t& cfg, const carekv_cache_
     cudaError_t e0 = cudaGetLastError();
     if (e0 != cudaSuccess) return e0;
   }
-  dim3 grid(n_new, cfg.num_kv_heads, seq_count);
-  page_store_kernel<0><<<grid, 256, 0, st>>>(cfg, cache, layer, K, V, T, seq_begin, prm, in_H, sketch_proj);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e;
+  if (prefill_store_warp_supported(cfg, cache, K, V, prm)) {
+    e = launch_prefill_store_warp(cfg, cache, layer, K, V, T, seq_begin, seq_count, prm, in_H, st);
+  } else {
+    dim3 grid(n_new, cfg.num_kv_heads, seq_count);
+    page_store_kernel<0><<<grid, 256, 0, st>>>(cfg, cache, layer, K, V, T, seq_begin, prm, in_H, sketch_proj);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) return e;
   slot_id_scan_kernel<0><<<seq_count, 1024, 0, st>>>(cfg, cache, layer, seq_begin, n_new);
   return cudaGetLastError();
