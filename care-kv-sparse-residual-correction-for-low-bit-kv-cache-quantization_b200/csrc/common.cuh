@@ -181,6 +181,33 @@ __device__ __forceinline__ int nibble_code(float x, float s) {
   t = fminf(fmaxf(t, -8.0f), 7.0f);
   return static_cast<int>(t);
 }
+// ───────────── quotients through a reciprocal (page store hot loop) ─────────────
+// RN(x / s) from r = RN(1 / s): q = RN(x r), the remainder x - q s exact by
+// FMA, then RN(q + (x - q s) r) -- Markstein's correction (P. Markstein,
+// IBM J. Res. Dev. 34(1), 1990; Muller et al., Handbook of Floating-Point
+// Arithmetic, the division theorem with a correctly rounded reciprocal),
+// exact while the remainder does not underflow.  The codes below use it
+// only where that holds: quantizer quotients |x / s| <= 16 with s an fp16
+// value or a bf16 value >= 1e-9 (the quantizer's scales), and 4-bit slot
+// quotients |R / s4| <= 8 with s4 >= 1e-8 / 7; checked against __fdiv_rn
+// over every fp16 (x, s) pair and every bf16 pair with s >= 1e-9.
+__device__ __forceinline__ float div_by_recip(float x, float s, float r) {
+  const float q = __fmul_rn(x, r);
+  return __fmaf_rn(__fmaf_rn(-q, s, x), r, q);
+}
+// quant_code(x, scale) with rcp = __frcp_rn(scale)
+__device__ __forceinline__ int quant_code_r(float x, float scale, float rcp, int qmax, int dt) {
+  float t = rnd(div_by_recip(x, scale, rcp), dt);
+  if (t != t) return 0;  // 0/0 on an all-zero fp16 group (rcp = inf): NaN -> 0 as quant_code
+  t = rintf(t);
+  t = fminf(fmaxf(t, static_cast<float>(-qmax - 1)), static_cast<float>(qmax));
+  return static_cast<int>(t);
+}
+// nibble_code(x, s) with rcp = __frcp_rn(s)
+__device__ __forceinline__ int nibble_code_r(float x, float s, float rcp) {
+  const float t = rintf(div_by_recip(x, s, rcp));
+  return static_cast<int>(fminf(fmaxf(t, -8.0f), 7.0f));
+}
 __device__ __forceinline__ float unpack_nibble(const uint8_t* payload, int i, float scale) {
   int v = (payload[i >> 1] >> (4 * (i & 1))) & 15;
   if (v > 7) v -= 16;

@@ -16,7 +16,9 @@
 // CTA barrier: warps run their pages independently.
 //
 // Arithmetic per element is the store kernel's (common.cuh: group_scale,
-// quant_code, dequant, int8_scale_code, nibble_code), so codes, scales,
+// quant_code, dequant, int8_scale_code, nibble_code; the quotients of the
+// codes through a correctly rounded reciprocal, quant_code_r /
+// nibble_code_r, which give the same IEEE quotients), so codes, scales,
 // masters and payloads are bit-identical to it; the error norms and the
 // V_hat norm accumulate in a different fp32 order (per-lane partial sums,
 // then a butterfly), as the store kernel's order differs from the
@@ -39,8 +41,13 @@ __device__ __forceinline__ float2 unpack2(uint32_t w) {
 // two dt-representable floats -> 2-byte pair (exact)
 template <int DT>
 __device__ __forceinline__ uint32_t pack2(float a, float b) {
-  if (DT == CAREKV_BF16)
-    return (__float_as_uint(a) >> 16) | (__float_as_uint(b) & 0xffff0000u);
+  if (DT == CAREKV_BF16) {
+    // upper halves of both (one PRMT); as inline asm the compiler keeps the
+    // packed word rather than the two floats alive until their next use
+    uint32_t w;
+    asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(w) : "r"(__float_as_uint(a)), "r"(__float_as_uint(b)));
+    return w;
+  }
   const __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
@@ -70,13 +77,14 @@ struct PairSmem {
 };
 
 // GSEL: quantization group = D/4 (0: two groups per lane), D/2 (1: one
-// group per lane) or D (2: one group per lane pair).  KIND 0: the K warp of
-// a page, 1: its V warp.
-template <int D, int BITS, int GSEL, int DT, int KIND>
+// group per lane) or D (2: one group per lane pair).  kind 0: the K warp of
+// a page, 1: its V warp -- one code path for both, so the two warps of a
+// page run the same instructions.
+template <int D, int BITS, int GSEL, int DT>
 __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer,
-                                           const void* __restrict__ Xin, int T, int seq_begin, int n_seq,
+                                           const void* __restrict__ Xin, int T, int seq_begin,
                                            const carekv_store_params_t& prm, int in_H, int64_t gw, int pair,
-                                           PairSmem& ps) {
+                                           int kind, PairSmem& ps) {
   constexpr int NE = D / 2;            // elements per lane
   constexpr int NW = NE / 2;           // packed 2-byte pairs per lane
   constexpr int GPL = GSEL == 0 ? 2 : 1;
@@ -99,7 +107,7 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
   const int64_t lhp = d.lhp(seq_begin + s, layer, h);
   const int p = cache.num_pages[lhp] + pi;
   if (p >= d.P) {
-    if (lane == 0 && KIND == 0) atomicOr(cache.error_flag, kErrPageOverflow);
+    if (lane == 0 && kind == 0) atomicOr(cache.error_flag, kErrPageOverflow);
     return;   // both warps of the pair leave before their barrier
   }
   const int64_t pg = lhp * d.P + p;
@@ -122,21 +130,27 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
   }
 
   // ── group scales (quantizer.py:31-64; max is order-free) ──
+  // |x| of fp16 / bf16 values orders like the integer bits & 0x7fff, so the
+  // group maximum is taken on the packed pairs (16-bit lane-wise max)
   float m[GPL];
 #pragma unroll
-  for (int j = 0; j < GPL; ++j) m[j] = 0.f;
+  for (int j = 0; j < GPL; ++j) {
+    uint32_t mu = 0u;
 #pragma unroll
-  for (int w = 0; w < NW; ++w) {
-    const float2 f = unpack2<DT>(x[w]);
-    m[(2 * w) / GL] = fmaxf(m[(2 * w) / GL], fmaxf(fabsf(f.x), fabsf(f.y)));
+    for (int w = j * (NW / GPL); w < (j + 1) * (NW / GPL); ++w) mu = __vmaxu2(mu, x[w] & 0x7fff7fffu);
+    mu = max(mu & 0xffffu, mu >> 16);
+    m[j] = DT == CAREKV_BF16 ? __uint_as_float(mu << 16) : __half2float(__ushort_as_half(static_cast<unsigned short>(mu)));
   }
   if (GSEL == 2) m[0] = fmaxf(m[0], __shfl_xor_sync(0xffffffffu, m[0], 1));
-  float sc[GPL], rs[GPL];
+  float sc[GPL], rcp[GPL], rs[GPL];
 #pragma unroll
-  for (int j = 0; j < GPL; ++j) sc[j] = group_scale(m[j], qmax, dt);
+  for (int j = 0; j < GPL; ++j) {
+    sc[j] = group_scale(m[j], qmax, dt);
+    rcp[j] = __frcp_rn(sc[j]);
+  }
   // page scales (cache.py:592-606): int8 codes against the page master, or
   // the raw scale; rs = the scale as read back (fp16 value)
-  void* sdst = KIND == 0 ? cache.k_scale : cache.v_scale;
+  void* sdst = kind ? cache.v_scale : cache.k_scale;
   const int64_t srow = (pg * kPage + r) * G + (GSEL == 0 ? 2 * hf : (GSEL == 1 ? hf : 0));
   const bool writer = GSEL != 2 || hf == 0;
   if (d.scale_mode == CAREKV_SCALE_INT8) {
@@ -146,7 +160,7 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
     mx = fmaxf(warp_max(mx), clamp_lo(dt));
     const uint16_t mb = f32_to_f16_bits(__fdiv_rn(mx, 127.0f));
     const float master = f16_bits_to_f32(mb);
-    if (lane == 0) (KIND == 0 ? cache.k_master : cache.v_master)[pg] = mb;
+    if (lane == 0) (kind ? cache.v_master : cache.k_master)[pg] = mb;
     uint32_t c8w = 0u;
 #pragma unroll
     for (int j = 0; j < GPL; ++j) {
@@ -172,12 +186,13 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
 #pragma unroll
   for (int i = 0; i < NPW; ++i) pk[i] = 0u;
   float vn = 0.f;
+  const bool vnorm = kind && live;
 #pragma unroll
   for (int w = 0; w < NW; ++w) {
     const float2 f = unpack2<DT>(x[w]);
     const int j = (2 * w) / GL;
-    const int c0 = quant_code(f.x, sc[j], qmax, dt);
-    const int c1 = quant_code(f.y, sc[j], qmax, dt);
+    const int c0 = quant_code_r(f.x, sc[j], rcp[j], qmax, dt);
+    const int c1 = quant_code_r(f.y, sc[j], rcp[j], qmax, dt);
     // codes 2w, 2w+1 at bits BITS*e of the half row's little-endian stream
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
@@ -189,7 +204,7 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
     const float r0 = rnd(__fsub_rn(f.x, dequant(c0, sc[j], dt)), dt);
     const float r1 = rnd(__fsub_rn(f.y, dequant(c1, sc[j], dt)), dt);
     x[w] = pack2<DT>(r0, r1);
-    if (KIND == 1 && live) {
+    if (vnorm) {
       // V rows as stored: code * the scale as read back, in fp16
       const float v0 = f16r(__fmul_rn(static_cast<float>(c0), rs[j]));
       const float v1 = f16r(__fmul_rn(static_cast<float>(c1), rs[j]));
@@ -197,14 +212,13 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
       vn = fmaf(v1, v1, vn);
     }
   }
-  store_bytes<HB>((KIND == 0 ? cache.k_codes : cache.v_codes) + (pg * kPage + r) * R + hf * HB, pk);
+  store_bytes<HB>((kind ? cache.v_codes : cache.k_codes) + (pg * kPage + r) * R + hf * HB, pk);
 
   // ── candidates (residual_store.py:290-330): mean row error norm and the
   // 4-bit scale max(|R|, 1e-8) / 7 (residual_store.py:127-136) ──
   const int ncand = C + d.NV;
-  if (KIND == 0) {
+  if (kind == 0) {
     // K channel groups of 32: CPL per lane, shared by the 16 lanes of a half
-    float e[CPL], mx[CPL];
 #pragma unroll
     for (int j = 0; j < CPL; ++j) {
       float ss = 0.f, mj = 0.f;
@@ -221,16 +235,10 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
         ej += __shfl_xor_sync(0xffffffffu, ej, o);
         mj = fmaxf(mj, __shfl_xor_sync(0xffffffffu, mj, o));
       }
-      e[j] = ej;
-      mx[j] = mj;
-    }
-    // candidate x = hf * CPL + j is on lane hf (row 0) after the butterfly
-#pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-      if (lane < 2 && r == 0) {
-        const int cand = hf * CPL + j;
-        ps.e[cand] = nv > 0 ? __fdiv_rn(e[j], static_cast<float>(nv)) : 0.f;
-        ps.s4[cand] = __fdiv_rn(fmaxf(mx[j], 1e-8f), 7.0f);
+      // candidate hf * CPL + j: written by lane hf (row 0)
+      if (lane < 2) {
+        ps.e[lane * CPL + j] = nv > 0 ? __fdiv_rn(ej, static_cast<float>(nv)) : 0.f;
+        ps.s4[lane * CPL + j] = __fdiv_rn(fmaxf(mj, 1e-8f), 7.0f);
       }
     }
   } else {
@@ -292,99 +300,113 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
   }
   keep_k = min(keep_k, d.SK);
   keep_v = min(keep_v, d.SV);
-  const unsigned lt = (1u << lane) - 1u;
-  if (KIND == 0) {
-    const bool kept = elig && isk && rank < keep_k;
-    const unsigned mk = __ballot_sync(0xffffffffu, kept);
-    const int nk = __popc(mk);
-    if (kept) {
-      const int64_t sidx = pg * d.SK + __popc(mk & lt);
-      cache.k_slot_group[sidx] = static_cast<int8_t>(lane);
-      cache.k_slot_scale[sidx] = f32_to_f16_bits(ps.s4[lane]);
-      cache.k_slot_id[sidx] = rank;  // local rank; the scan adds the arena base
-    }
-    if (lane >= nk && lane < d.SK) {
-      cache.k_slot_group[pg * d.SK + lane] = -1;
-      cache.k_slot_id[pg * d.SK + lane] = -1;
-    }
-    if (isk) cache.k_err[pg * C + lane] = f32_to_f16_bits(e);
-    // payloads: value i = t*32 + c of the group (byte i/2, low nibble = even i)
-    unsigned km = mk;
+  // this warp's kind: K channel groups or V token blocks
+  const bool mine = kind ? isv : isk;
+  const int cap = kind ? d.SV : d.SK, c0k = kind ? C : 0;
+  const bool kept = elig && mine && rank < (kind ? keep_v : keep_k);
+  const unsigned km = __ballot_sync(0xffffffffu, kept);
+  const int nk = __popc(km);
+  int8_t* const sgrp = kind ? cache.v_slot_block : cache.k_slot_group;
+  uint16_t* const sscl = kind ? cache.v_slot_scale : cache.k_slot_scale;
+  int32_t* const sid = kind ? cache.v_slot_id : cache.k_slot_id;
+  if (kept) {
+    const int64_t sidx = pg * cap + __popc(km & ((1u << lane) - 1u));
+    sgrp[sidx] = static_cast<int8_t>(lane - c0k);
+    sscl[sidx] = f32_to_f16_bits(ps.s4[lane]);
+    sid[sidx] = rank;  // local rank; the scan adds the arena base
+  }
+  if (lane >= nk && lane < cap) {
+    sgrp[pg * cap + lane] = -1;
+    sid[pg * cap + lane] = -1;
+  }
+  if (mine) (kind ? cache.v_err + pg * d.NV : cache.k_err + pg * C)[lane - c0k] = f32_to_f16_bits(e);
+
+  // ── payloads of the kept slots, their nibbles spread over all 32 lanes ──
+  if (kind == 0) {
+    // K group g: value i = t*32 + c (byte i/2, low nibble = even i); lane
+    // (r, hf) codes channels hf*16 .. hf*16+15 of row r, fetched from the
+    // lane of row r that holds group g
+    unsigned mm = km;
     for (int j = 0; j < nk; ++j) {
-      const int g = __ffs(km) - 1;
-      km &= km - 1;
-      if (hf == g / CPL) {
-        const float s4 = ps.s4[g];
-        const int jj = g % CPL;
-        uint32_t pw[4] = {0u, 0u, 0u, 0u};
+      const int g = __ffs(mm) - 1;
+      mm &= mm - 1;
+      const float s4 = ps.s4[g], r4 = __frcp_rn(s4);
+      const int jj = g % CPL, src = 2 * r + g / CPL;
+      uint32_t pw[2] = {0u, 0u};
 #pragma unroll
-        for (int w = 0; w < 16; ++w) {
-          uint32_t xw = x[w];
+      for (int k = 0; k < 8; ++k) {
+        uint32_t a0 = x[k], a1 = x[8 + k];
 #pragma unroll
-          for (int q = 1; q < CPL; ++q)
-            if (q == jj) xw = x[16 * q + w];
-          const float2 f = unpack2<DT>(xw);
-          const uint32_t by = (static_cast<uint32_t>(nibble_code(f.x, s4)) & 15u) |
-                              ((static_cast<uint32_t>(nibble_code(f.y, s4)) & 15u) << 4);
-          pw[w >> 2] |= by << (8 * (w & 3));
-        }
-        uint8_t* dst = cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes + r * 16;
-        *reinterpret_cast<uint4*>(dst) = make_uint4(pw[0], pw[1], pw[2], pw[3]);
+        for (int q = 1; q < CPL; ++q)
+          if (q == jj) { a0 = x[16 * q + k]; a1 = x[16 * q + 8 + k]; }
+        const uint32_t v0 = __shfl_sync(0xffffffffu, a0, src), v1 = __shfl_sync(0xffffffffu, a1, src);
+        const float2 f = unpack2<DT>(hf ? v1 : v0);
+        const uint32_t by = (static_cast<uint32_t>(nibble_code_r(f.x, s4, r4)) & 15u) |
+                            ((static_cast<uint32_t>(nibble_code_r(f.y, s4, r4)) & 15u) << 4);
+        pw[k >> 2] |= by << (8 * (k & 3));
       }
+      *reinterpret_cast<uint2*>(cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes + r * 16 + hf * 8) =
+          make_uint2(pw[0], pw[1]);
     }
   } else {
-    const bool kept = elig && isv && rank < keep_v;
-    const unsigned mv = __ballot_sync(0xffffffffu, kept);
-    const int nvk = __popc(mv);
-    if (kept) {
-      const int64_t sidx = pg * d.SV + __popc(mv & lt);
-      cache.v_slot_block[sidx] = static_cast<int8_t>(lane - C);
-      cache.v_slot_scale[sidx] = f32_to_f16_bits(ps.s4[lane]);
-      cache.v_slot_id[sidx] = rank;
-    }
-    if (lane >= nvk && lane < d.SV) {
-      cache.v_slot_block[pg * d.SV + lane] = -1;
-      cache.v_slot_id[pg * d.SV + lane] = -1;
-    }
-    if (isv) cache.v_err[pg * d.NV + lane - C] = f32_to_f16_bits(e);
-    // payloads: value i = (t - t0)*D + c of the block
-    unsigned vm = mv;
-    for (int j = 0; j < nvk; ++j) {
-      const int xc = __ffs(vm) - 1;
-      vm &= vm - 1;
+    // V block b: value i = (t - tb)*D + c; byte k of the block is word k of
+    // its lanes 2tb, 2tb+1, ... in order
+    unsigned mm = km;
+    for (int j = 0; j < nk; ++j) {
+      const int xc = __ffs(mm) - 1;
+      mm &= mm - 1;
+      const float s4 = ps.s4[xc], r4 = __frcp_rn(s4);
       const int tb = (xc - C) * d.vtb;
-      if (r >= tb && r < tb + d.vtb) {
-        const float s4 = ps.s4[xc];
+      uint8_t* const dst = cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes;
+      if (d.vtb == 4) {
+        // 8 source lanes x NW words = 32 lanes x WPL bytes
+        constexpr int WPL = NW / 4;
+        const int src = 2 * tb + (lane >> 2), part = lane & 3;
+        uint32_t y[WPL];
+#pragma unroll
+        for (int w = 0; w < NW; ++w) {
+          const uint32_t v = __shfl_sync(0xffffffffu, x[w], src);
+          if (w / WPL == part) y[w % WPL] = v;
+        }
+        uint32_t pw[WPL / 4];
+#pragma unroll
+        for (int i = 0; i < WPL / 4; ++i) pw[i] = 0u;
+#pragma unroll
+        for (int k = 0; k < WPL; ++k) {
+          const float2 f = unpack2<DT>(y[k]);
+          const uint32_t by = (static_cast<uint32_t>(nibble_code_r(f.x, s4, r4)) & 15u) |
+                              ((static_cast<uint32_t>(nibble_code_r(f.y, s4, r4)) & 15u) << 4);
+          pw[k >> 2] |= by << (8 * (k & 3));
+        }
+        store_bytes<WPL>(dst + lane * WPL, pw);
+      } else if (r >= tb && r < tb + d.vtb) {
         uint32_t pw[NW / 4];
 #pragma unroll
         for (int i = 0; i < NW / 4; ++i) pw[i] = 0u;
 #pragma unroll
         for (int w = 0; w < NW; ++w) {
           const float2 f = unpack2<DT>(x[w]);
-          const uint32_t by = (static_cast<uint32_t>(nibble_code(f.x, s4)) & 15u) |
-                              ((static_cast<uint32_t>(nibble_code(f.y, s4)) & 15u) << 4);
+          const uint32_t by = (static_cast<uint32_t>(nibble_code_r(f.x, s4, r4)) & 15u) |
+                              ((static_cast<uint32_t>(nibble_code_r(f.y, s4, r4)) & 15u) << 4);
           pw[w >> 2] |= by << (8 * (w & 3));
         }
-        uint8_t* dst = cache.v_slot_data + (pg * d.SV + j) * d.vslot_bytes + ((r - tb) * D + hf * NE) / 2;
-        store_bytes<NW>(dst, pw);
+        store_bytes<NW>(dst + ((r - tb) * D + hf * NE) / 2, pw);
       }
     }
   }
 }
 
 template <int D, int BITS, int GSEL, int DT>
-__global__ void __launch_bounds__(kWarps * 32) page_store_warp(carekv_config_t cfg, carekv_cache_t cache, int layer,
+__global__ void __launch_bounds__(kWarps * 32, 3) page_store_warp(carekv_config_t cfg, carekv_cache_t cache, int layer,
                                                                const void* __restrict__ Kin,
                                                                const void* __restrict__ Vin, int T, int seq_begin,
                                                                int n_seq, carekv_store_params_t prm, int in_H) {
   __shared__ PairSmem ps[kWarps / 2];
-  const int warp = threadIdx.x >> 5, pair = warp >> 1;
+  const int warp = threadIdx.x >> 5, pair = warp >> 1, kind = warp & 1;
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * (kWarps / 2) + pair;   // page of this warp pair
   if (gw >= static_cast<int64_t>(n_seq) * cfg.num_kv_heads * ((T + kPage - 1) / kPage)) return;
-  if (warp & 1)
-    store_half<D, BITS, GSEL, DT, 1>(cfg, cache, layer, Vin, T, seq_begin, n_seq, prm, in_H, gw, pair, ps[pair]);
-  else
-    store_half<D, BITS, GSEL, DT, 0>(cfg, cache, layer, Kin, T, seq_begin, n_seq, prm, in_H, gw, pair, ps[pair]);
+  store_half<D, BITS, GSEL, DT>(cfg, cache, layer, kind ? Vin : Kin, T, seq_begin, prm, in_H, gw, pair, kind,
+                                ps[pair]);
 }
 
 template <int D, int BITS, int GSEL>
