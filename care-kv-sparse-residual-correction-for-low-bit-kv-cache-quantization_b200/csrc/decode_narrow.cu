@@ -224,7 +224,9 @@ __device__ __forceinline__ uint32_t v_field4(const VSrc4& v, const Keys& K, uint
 // GC, SKC: scale groups per row and K slots per page fixed at compile time
 // (every stage offset then folds into the instructions), or 0 = read from
 // the configuration.
-template <int QN, int D, int BITS, int GC, int SKC>
+// KSLOT: q . R_K of the stored K slots is written (a.kw != nullptr; the
+// stage then also holds the pages' slot payloads).
+template <int QN, int D, int BITS, int GC, int SKC, bool KSLOT>
 __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   static_assert(BITS == 3 || BITS == 4, "narrow pass: INT3 or INT4 rows");
   constexpr int R = D * BITS / 8;
@@ -253,7 +255,7 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
   const int pb = pa + qv + (warp < rv ? 1 : 0);
   const int Hq = a.act_heads;   // query heads per activation row
   const int G = GC > 0 ? GC : d.G, SK = SKC > 0 ? SKC : d.SK;
-  const bool kslot = a.kw != nullptr;
+  constexpr bool kslot = KSLOT;
   const Geo g = geo(D, G, SK, kslot, BITS);
   const int64_t page0 = lhp * d.P;
   const int KG = a.p_used * SK;
@@ -540,6 +542,8 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
 
   bool failed = false;
   int fail_chunk = n_chunks;
+  int slot = 0;        // c % kNS
+  uint32_t phase = 0;  // (c / kNS) & 1
   for (int c = 0; c < n_chunks; ++c) {
     const int pbase = pa + c * kCP;
     const int mi = (pbase - pa) & (kWin - 1);
@@ -571,13 +575,13 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
       }
       __syncwarp();
     }
-    if (!mbar_wait(&bar[c % kNS], (c / kNS) & 1)) {
+    if (!mbar_wait(&bar[slot], phase)) {
       failed = true;
       fail_chunk = c;
       if (lane == 0) atomicOr(a.cache.error_flag, 4);
       break;
     }
-    const uint8_t* st = wsm + (c % kNS) * g.stage;
+    const uint8_t* st = wsm + slot * g.stage;
     // a full stage (two pages) runs as one straight-line block; the odd
     // last page of a range takes the one-page form
     auto stage = [&](auto npc) {
@@ -639,6 +643,10 @@ __global__ void __launch_bounds__(kWarps * 32, 4) decode_narrow(DecodeArgs a) {
       fence_proxy_async();
       issue(c + kNS);
     }
+    if (++slot == kNS) {
+      slot = 0;
+      phase ^= 1u;
+    }
   }
   if (failed && lane == 0) {
     // let the copies already issued land (bounded) before the staging area
@@ -697,18 +705,24 @@ size_t narrow_smem_bytes(const carekv_config_t& c, bool kslot) {
   return static_cast<size_t>(narrow::geo(c.head_dim, G, c.k_slots_per_page, kslot, c.base_bits).total);
 }
 
-template <int QN, int D, int BITS, int GC, int SKC>
-static cudaError_t launch_narrow_kernel(DecodeArgs& a, cudaStream_t st, int n_bh) {
-  const int smem = static_cast<int>(narrow_smem_bytes(a.cfg, a.kw != nullptr));
+template <int QN, int D, int BITS, int GC, int SKC, bool KSLOT>
+static cudaError_t launch_narrow_ks(DecodeArgs& a, cudaStream_t st, int n_bh) {
+  const int smem = static_cast<int>(narrow_smem_bytes(a.cfg, KSLOT));
   static int attr_bytes = 0;  // per process; the attribute is per function, not per device
   if (smem > attr_bytes) {
-    cudaError_t e = cudaFuncSetAttribute(narrow::decode_narrow<QN, D, BITS, GC, SKC>,
+    cudaError_t e = cudaFuncSetAttribute(narrow::decode_narrow<QN, D, BITS, GC, SKC, KSLOT>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     attr_bytes = smem;
   }
-  narrow::decode_narrow<QN, D, BITS, GC, SKC><<<n_bh * a.n_splits, narrow::kWarps * 32, smem, st>>>(a);
+  narrow::decode_narrow<QN, D, BITS, GC, SKC, KSLOT><<<n_bh * a.n_splits, narrow::kWarps * 32, smem, st>>>(a);
   return cudaGetLastError();
+}
+
+template <int QN, int D, int BITS, int GC, int SKC>
+static cudaError_t launch_narrow_kernel(DecodeArgs& a, cudaStream_t st, int n_bh) {
+  return a.kw != nullptr ? launch_narrow_ks<QN, D, BITS, GC, SKC, true>(a, st, n_bh)
+                         : launch_narrow_ks<QN, D, BITS, GC, SKC, false>(a, st, n_bh);
 }
 
 // 32-channel scale groups with one or two K slots per page (store budgets

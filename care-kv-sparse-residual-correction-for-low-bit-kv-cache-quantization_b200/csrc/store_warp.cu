@@ -16,10 +16,14 @@
 // CTA barrier: warps run their pages independently.
 //
 // Arithmetic per element is the store kernel's (common.cuh: group_scale,
-// quant_code, dequant, int8_scale_code, nibble_code; the quotients of the
-// codes through a correctly rounded reciprocal, quant_code_r /
-// nibble_code_r, which give the same IEEE quotients), so codes, scales,
-// masters and payloads are bit-identical to it; the error norms and the
+// quant_code, dequant, int8_scale_code, nibble_code), in forms that give
+// the same values: code quotients through a correctly rounded reciprocal
+// (div_by_recip, the IEEE quotient on these operands), X_hat = code * s and
+// R = X - X_hat as one rounding in fp16 / bf16 pair arithmetic (the fp32
+// product and difference are exact before the store kernel rounds them to
+// the dtype).  Codes, scales, masters and payloads are therefore
+// bit-identical to it for finite inputs (a NaN input row gets the clamped
+// code instead of 0); the error norms and the
 // V_hat norm accumulate in a different fp32 order (per-lane partial sums,
 // then a butterfly), as the store kernel's order differs from the
 // reference's own.
@@ -38,18 +42,28 @@ __device__ __forceinline__ float2 unpack2(uint32_t w) {
   const __half2 h = *reinterpret_cast<const __half2*>(&w);
   return __half22float2(h);
 }
-// two dt-representable floats -> 2-byte pair (exact)
+// (lo, hi) -> dt pair with round to nearest even (lo in the low half)
 template <int DT>
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-  if (DT == CAREKV_BF16) {
-    // upper halves of both (one PRMT); as inline asm the compiler keeps the
-    // packed word rather than the two floats alive until their next use
-    uint32_t w;
-    asm("prmt.b32 %0, %1, %2, 0x7632;" : "=r"(w) : "r"(__float_as_uint(a)), "r"(__float_as_uint(b)));
-    return w;
-  }
-  const __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
+__device__ __forceinline__ uint32_t cvt_pair(float lo, float hi) {
+  uint32_t d;
+  if (DT == CAREKV_BF16) asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  else asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+// lane-wise a * b and a - b of dt pairs, one rounding to nearest even each
+template <int DT>
+__device__ __forceinline__ uint32_t mul_pair(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if (DT == CAREKV_BF16) asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+template <int DT>
+__device__ __forceinline__ uint32_t sub_pair(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if (DT == CAREKV_BF16) asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
 }
 
 // Store n bytes (n = 4, 8, 12, 16, 24 or 32) of w[] at dst, in the widest
@@ -146,7 +160,10 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
 #pragma unroll
   for (int j = 0; j < GPL; ++j) {
     sc[j] = group_scale(m[j], qmax, dt);
-    rcp[j] = __frcp_rn(sc[j]);
+    // a zero scale (an all-zero fp16 group, where the clamp bound underflows)
+    // takes reciprocal 0: its x are all 0 and so are its codes, as the
+    // reference's 0/0 -> NaN -> int8 0
+    rcp[j] = sc[j] > 0.f ? __frcp_rn(sc[j]) : 0.f;
   }
   // page scales (cache.py:592-606): int8 codes against the page master, or
   // the raw scale; rs = the scale as read back (fp16 value)
@@ -187,29 +204,41 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
   for (int i = 0; i < NPW; ++i) pk[i] = 0u;
   float vn = 0.f;
   const bool vnorm = kind && live;
+  // the group scales as dt pairs (exact: they are dt values), the read-back
+  // V scales as fp16 pairs
+  uint32_t s2[GPL], rs2[GPL];
+#pragma unroll
+  for (int j = 0; j < GPL; ++j) {
+    s2[j] = cvt_pair<DT>(sc[j], sc[j]);
+    rs2[j] = cvt_pair<CAREKV_F16>(rs[j], rs[j]);
+  }
+  const float lo = static_cast<float>(-qmax - 1), hi = static_cast<float>(qmax);
 #pragma unroll
   for (int w = 0; w < NW; ++w) {
     const float2 f = unpack2<DT>(x[w]);
     const int j = (2 * w) / GL;
-    const int c0 = quant_code_r(f.x, sc[j], rcp[j], qmax, dt);
-    const int c1 = quant_code_r(f.y, sc[j], rcp[j], qmax, dt);
-    // codes 2w, 2w+1 at bits BITS*e of the half row's little-endian stream
+    // code = clamp(rint(dt(x / s))) (quant_code; the quotient as div_by_recip)
+    const float2 qd = unpack2<DT>(cvt_pair<DT>(div_by_recip(f.x, sc[j], rcp[j]), div_by_recip(f.y, sc[j], rcp[j])));
+    const float t0 = fminf(fmaxf(rintf(qd.x), lo), hi), t1 = fminf(fmaxf(rintf(qd.y), lo), hi);
+    // codes 2w, 2w+1 at bits BITS*e of the half row's little-endian stream;
+    // t + 1.5*2^23 holds t in two's complement in its low mantissa bits
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const uint32_t cu = static_cast<uint32_t>(u ? c1 : c0) & ((1u << BITS) - 1u);
+      const uint32_t cu = __float_as_uint((u ? t1 : t0) + 12582912.0f) & ((1u << BITS) - 1u);
       const int bit = BITS * (2 * w + u);
       pk[bit / 32] |= cu << (bit % 32);
       if (bit % 32 > 32 - BITS) pk[bit / 32 + 1] |= cu >> (32 - bit % 32);
     }
-    const float r0 = rnd(__fsub_rn(f.x, dequant(c0, sc[j], dt)), dt);
-    const float r1 = rnd(__fsub_rn(f.y, dequant(c1, sc[j], dt)), dt);
-    x[w] = pack2<DT>(r0, r1);
+    // X_hat = dt(code * s) and R = dt(X - X_hat), both one rounding in the
+    // dt pair arithmetic, equal to the fp32-then-dt rounding of dequant and
+    // the residual (code * s and X - X_hat are exact in fp32 here)
+    const uint32_t c2 = cvt_pair<DT>(t0, t1);
+    x[w] = sub_pair<DT>(x[w], mul_pair<DT>(c2, s2[j]));
     if (vnorm) {
       // V rows as stored: code * the scale as read back, in fp16
-      const float v0 = f16r(__fmul_rn(static_cast<float>(c0), rs[j]));
-      const float v1 = f16r(__fmul_rn(static_cast<float>(c1), rs[j]));
-      vn = fmaf(v0, v0, vn);
-      vn = fmaf(v1, v1, vn);
+      const float2 v = unpack2<CAREKV_F16>(mul_pair<CAREKV_F16>(cvt_pair<CAREKV_F16>(t0, t1), rs2[j]));
+      vn = fmaf(v.x, v.x, vn);
+      vn = fmaf(v.y, v.y, vn);
     }
   }
   store_bytes<HB>((kind ? cache.v_codes : cache.k_codes) + (pg * kPage + r) * R + hf * HB, pk);
