@@ -197,9 +197,10 @@ static inline int64_t sel_stride(const carekv_config_t& c, int p_used) {
 }
 
 // Split-K pass chosen for a layout.  NARROW: INT3 or INT4 / int8 scales with at most
-// 4 query heads per kv head (decode_narrow.cu, 4 CTAs per SM, also computes
-// q . R_K of the stored K slots); WIDE: the same layout with 8 query heads
-// (decode_fast.cu, 2 CTAs per SM); GENERIC: every other layout.
+// 4 query heads per kv head (decode_narrow.cu, 4 CTAs per SM); WIDE: INT3 with
+// 8 query heads (decode_fast.cu, 2 CTAs per SM); both also compute q . R_K of
+// the stored K slots.  GENERIC: every other layout (the router computes the
+// slot dots itself).
 enum class Pass { GENERIC, WIDE, NARROW };
 inline Pass choose_pass(const carekv_config_t& c) {
   const int D = c.head_dim;
@@ -222,7 +223,8 @@ inline int chunk_size(int seq_count) {
 }
 
 // Workspace regions, each 256-byte aligned: selection readback, scores,
-// logits, split partials m / l / O, and (narrow pass) q . R_K per K slot.
+// logits, split partials m / l / O, and (narrow and wide passes) q . R_K
+// per K slot.
 // The split plan is the one of a chunk (chunk_size sequences).
 struct WsLayout {
   int64_t sel, scores, S, pm, pl, po, kw, total;
@@ -241,7 +243,7 @@ inline WsLayout ws_layout(const carekv_config_t& c, int seq_count, int p_used) {
   w.pl = o;     o = align256(o + n_bh * sp.n_splits * qn * 4);
   w.po = o;     o = align256(o + n_bh * sp.n_splits * qn * static_cast<int64_t>(c.head_dim) * 4);
   w.kw = o;
-  if (pass == Pass::NARROW) o = align256(o + n_bh * qn * static_cast<int64_t>(p_used) * c.k_slots_per_page * kPage * 4);
+  if (pass != Pass::GENERIC) o = align256(o + n_bh * qn * static_cast<int64_t>(p_used) * c.k_slots_per_page * kPage * 4);
   w.total = o;
   return w;
 }
@@ -261,7 +263,7 @@ static cudaError_t launch_qn(DecodeArgs& a, cudaStream_t st, int n_bh) {
   dim3 g1(n_bh, a.n_splits);
   cudaError_t e;
   const Pass pass = a.force_generic ? Pass::GENERIC : choose_pass(a.cfg);
-  if (pass != Pass::NARROW) a.kw = nullptr;
+  if (pass == Pass::GENERIC) a.kw = nullptr;
   if (pass == Pass::NARROW) {
     if constexpr (QN <= 4) {
       e = a.cfg.head_dim == 64 ? launch_decode_narrow<QN, 64>(a, st, n_bh)
@@ -405,11 +407,12 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
   a.pm = reinterpret_cast<float*>(w + wl.pm);
   a.pl = reinterpret_cast<float*>(w + wl.pl);
   a.po = reinterpret_cast<float*>(w + wl.po);
-  // q . R_K is precomputed by the narrow pass whenever live combined_kvscore
-  // scoring may read it: K slots stored and K residuals part of the route
+  // q . R_K is precomputed by the narrow and wide passes whenever live
+  // combined_kvscore scoring may read it: K slots stored and K residuals
+  // part of the route
   const bool live_k = rp.kind != CAREKV_KIND_NONE && rp.kind != CAREKV_KIND_V && rp.kscore_live &&
                       cfg.k_slots_per_page > 0;
-  a.kw = (choose_pass(cfg) == Pass::NARROW && live_k) ? reinterpret_cast<float*>(w + wl.kw) : nullptr;
+  a.kw = (choose_pass(cfg) != Pass::GENERIC && live_k) ? reinterpret_cast<float*>(w + wl.kw) : nullptr;
   a.s_perm = 0;
   a.dq_keys[0] = i3_key2(0, 0);
   a.dq_keys[1] = i3_key2(3, 3);

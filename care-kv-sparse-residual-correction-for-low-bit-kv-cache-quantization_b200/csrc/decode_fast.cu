@@ -19,6 +19,9 @@
 //    keep ~22 bits: the logits match an fp32 dot product to accumulation-
 //    order rounding.  The channel order inside each MMA is permuted so that
 //    every thread decodes whole packed words it loads itself.
+//  * q . R_K of every stored K slot (for the router's combined_kvscore) on
+//    the same Q rows: the slot's 4-bit codes are the B operand as exact
+//    fp16 integers, the slot scale applied to the fp32 result.
 #include "common.cuh"
 #include "internal.h"
 #include "decode_args.h"
@@ -109,6 +112,10 @@ __global__ void __launch_bounds__(kWarps * 32, 2) decode_partial_int3(DecodeArgs
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t bars[kWarps][kNS];
   __shared__ float sm_m[kWarps][8], sm_l[kWarps][8];
+  // A fragments of the slot dots per 32-channel group and k-step: rows gid =
+  // q_hi, gid+8 = q_lo of query gid; k-step ks covers channels
+  // 8*tig + 4*ks + {0..3} of the group (the nibble order of a payload word)
+  __shared__ __align__(16) uint32_t qfr[D / 32][2][32][4];
 
   const Dims d = make_dims(a.cfg);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -164,6 +171,31 @@ __global__ void __launch_bounds__(kWarps * 32, 2) decode_partial_int3(DecodeArgs
   for (int j = 0; j < NT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
   float m_run = -INFINITY, l_part = 0.f;
   float* Srow = a.S + (static_cast<int64_t>(bh) * QN + gid) * a.p_used * kPage;
+  const bool kslot = a.kw != nullptr;
+  if (kslot) {
+    for (int x = threadIdx.x; x < (D / 32) * 2 * 32; x += blockDim.x) {
+      const int g = x / 64, ks = (x / 32) % 2, ln = x % 32;
+      const int qg = ln >> 2, tg = ln & 3;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+      if (qg < QN)
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          v[e] = load_act(a.q, (static_cast<int64_t>(s) * Hq + h * QN + qg) * D + g * 32 + 8 * tg + 4 * ks + e, a.dt);
+      float hi[4], lo[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        hi[e] = __half2float(__float2half_rn(v[e]));
+        lo[e] = v[e] - hi[e];
+      }
+      qfr[g][ks][ln][0] = pack_h2(hi[0], hi[1]);
+      qfr[g][ks][ln][1] = pack_h2(lo[0], lo[1]);
+      qfr[g][ks][ln][2] = pack_h2(hi[2], hi[3]);
+      qfr[g][ks][ln][3] = pack_h2(lo[2], lo[3]);
+    }
+    __syncthreads();
+  }
+  const int KG = a.p_used * d.SK;
+  float* Wrow = kslot ? a.kw + (static_cast<int64_t>(bh) * QN + gid) * KG * kPage : nullptr;
 
   const int n_chunks = (pb - pa + kCP - 1) / kCP;
   const int64_t page0 = lhp * d.P;
@@ -235,6 +267,32 @@ __global__ void __launch_bounds__(kWarps * 32, 2) decode_partial_int3(DecodeArgs
             *reinterpret_cast<float2*>(Srow + p * kPage + t) = make_float2(sv[nt][0], sv[nt][1]);
           } else if (t < nv) {
             Srow[p * kPage + t] = sv[nt][0];
+          }
+        }
+      }
+      // ── q . R_K of the page's stored K slots: tokens 2tig, 2tig+1 (c0)
+      // and 8+2tig, 9+2tig (c1) of query gid, times the slot scale ──
+      if (kslot && nv > 0) {
+        for (int j = 0; j < d.SK; ++j) {
+          const int grp = a.cache.k_slot_group[pg * d.SK + j];
+          if (grp < 0 || grp >= D / 32) continue;
+          const uint8_t* pay = a.cache.k_slot_data + (pg * d.SK + j) * d.kslot_bytes;
+          const uint32_t w0 = *reinterpret_cast<const uint32_t*>(pay + gid * 16 + 4 * tig);
+          const uint32_t w1 = *reinterpret_cast<const uint32_t*>(pay + (gid + 8) * 16 + 4 * tig);
+          const float rs = f16_bits_to_f32(a.cache.k_slot_scale[pg * d.SK + j]);
+          float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int ks = 0; ks < 2; ++ks) {
+            const uint4 af = *reinterpret_cast<const uint4*>(&qfr[grp][ks][lane][0]);
+            mma_f16(c0, af.x, af.y, af.z, af.w, nib_pair(w0, 2 * ks), nib_pair(w0, 2 * ks + 1));
+            mma_f16(c1, af.x, af.y, af.z, af.w, nib_pair(w1, 2 * ks), nib_pair(w1, 2 * ks + 1));
+          }
+          if (gid < QN) {
+            float* wr = Wrow + (static_cast<int64_t>(p) * d.SK + j) * kPage;
+            *reinterpret_cast<float2*>(wr + 2 * tig) =
+                make_float2(__fmul_rn(c0[0] + c0[2], rs), __fmul_rn(c0[1] + c0[3], rs));
+            *reinterpret_cast<float2*>(wr + 8 + 2 * tig) =
+                make_float2(__fmul_rn(c1[0] + c1[2], rs), __fmul_rn(c1[1] + c1[3], rs));
           }
         }
       }
