@@ -57,6 +57,15 @@ int validate_cache(const carekv_config_t* c, const carekv_cache_t* k) {
   if (c->base_kind == CAREKV_BASE_KIVI && (!k->k_chan_scale || !k->prefill_tokens ||
                                            (c->kivi_window_pages > 0 && !k->k_window)))
     return CAREKV_ERR_INVALID_ARG;
+  // the kernels stage rows, scales and slot payloads with 16-byte and bulk
+  // copies: every buffer starts on a 16-byte boundary (cudaMalloc gives 256)
+  const void* bufs[] = {k->k_codes, k->v_codes, k->k_scale, k->v_scale, k->k_master, k->v_master, k->valid,
+                        k->num_pages, k->v_norm2, k->k_slot_group, k->k_slot_data, k->k_slot_scale, k->k_slot_id,
+                        k->v_slot_block, k->v_slot_data, k->v_slot_scale, k->v_slot_id, k->k_err, k->v_err,
+                        k->k_sketch, k->slot_counter, k->read_counter, k->error_flag, k->k_chan_scale,
+                        k->k_window, k->prefill_tokens};
+  for (const void* b : bufs)
+    if ((reinterpret_cast<uintptr_t>(b) & 15) != 0) return CAREKV_ERR_INVALID_ARG;
   return CAREKV_OK;
 }
 

@@ -1,11 +1,12 @@
 // Decode attention over the packed cache (kernels K3, K4 and K2).
 //
-// decode_partial_kernel  (K3)  split-K pass: each CTA streams a range of
-//   pages of one (sequence, kv head), dequantizes K and V rows to their fp16
-//   values, computes the logits of the kv head's query group, keeps an online
-//   softmax and the weighted V sum, writes the logits to the workspace (the
-//   router needs the normalised weights of every token) and one (m, l, O)
-//   partial per CTA.
+// K3 split-K pass (decode_narrow.cu, decode_fast.cu, decode_generic.cu):
+//   each CTA streams a range of pages of one (sequence, kv head),
+//   dequantizes K and V rows to their fp16 values, computes the logits of
+//   the kv head's query group, keeps an online softmax and the weighted V
+//   sum, writes the logits (the router needs the normalised weights of every
+//   token) and q . R_K of the stored K slots to the workspace, and one
+//   (m, l, O) partial per CTA; this file plans and launches it.
 // route_kernel  (K4 + K2)  per (sequence, kv head): merges the partials into
 //   O_base, scores every stored residual slot (combined_kvscore or the sketch
 //   proxy), normalises per query, selects the joint / separate top-k and
@@ -23,135 +24,6 @@
 #include <cstdlib>
 
 namespace carekv {
-
-// ─────────────────────────── K3: split-K pass ───────────────────────────
-template <int QN, int DPL>
-__global__ void __launch_bounds__(128) decode_partial_kernel(DecodeArgs a) {
-  const Dims d = make_dims(a.cfg);
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int bh = blockIdx.x, split = blockIdx.y;
-  const int s = bh / d.H, h = bh % d.H, b = a.seq_begin + s;
-  const int D = d.D;
-  const int64_t lhp = d.lhp(b, a.layer, h);
-  const int np = min(a.cache.num_pages[lhp], a.p_used);
-  const int p0 = split * a.pps, p1 = min(np, p0 + a.pps);
-  const int Hq = a.act_heads;   // query heads per activation row
-
-  float q[QN][DPL];
-#pragma unroll
-  for (int i = 0; i < QN; ++i)
-#pragma unroll
-    for (int j = 0; j < DPL; ++j)
-      q[i][j] = load_act(a.q, (static_cast<int64_t>(s) * Hq + h * QN + i) * D + lane + 32 * j, a.dt);
-
-  float m[QN], l[QN], o[QN][DPL];
-#pragma unroll
-  for (int i = 0; i < QN; ++i) {
-    m[i] = -INFINITY;
-    l[i] = 0.f;
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) o[i][j] = 0.f;
-  }
-  float* Srow = a.S + static_cast<int64_t>(bh) * QN * a.p_used * kPage;
-  const int64_t sstride = static_cast<int64_t>(a.p_used) * kPage;
-  // KIVI base: the prefill's per-channel K scales of this lane's channels,
-  // and where the fp16 window of decode-appended K rows starts
-  float kcs[DPL];
-  int pf = 0;
-  if (d.kivi) {
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) kcs[j] = a.cache.k_chan_scale[lhp * D + lane + 32 * j];
-    pf = a.cache.prefill_tokens[lhp];
-  }
-
-  for (int p = p0 + warp; p < p1; p += 4) {
-    const int64_t pg = lhp * d.P + p;
-    const int nv = a.cache.valid[pg];
-    float mk = 0.f, mv = 0.f;
-    if (d.scale_mode == CAREKV_SCALE_INT8) {
-      mk = f16_bits_to_f32(a.cache.k_master[pg]);
-      mv = f16_bits_to_f32(a.cache.v_master[pg]);
-    }
-    for (int t = 0; t < nv; ++t) {
-      const uint8_t* kr = a.cache.k_codes + (pg * kPage + t) * d.R;
-      const uint8_t* vr = a.cache.v_codes + (pg * kPage + t) * d.R;
-      const int64_t srow = (pg * kPage + t) * d.G;
-      float kh[DPL], vh[DPL];
-      if (d.kivi) {
-        // K_hat: packed prefill rows (per-channel scale) or the fp16 window
-        // row of a decode-appended token; V_hat: per-token scale.  Both as
-        // the reference's fp16 side buffer holds them (cache.py:800-821)
-        const bool packed_row = p * kPage + t < pf;
-        const uint16_t* wrow = packed_row ? nullptr : a.cache.k_window + ((lhp * d.W + (p - pf / kPage)) * kPage + t) * D;
-        const float vs = reinterpret_cast<const float*>(a.cache.v_scale)[srow];
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) {
-          const int c = lane + 32 * j;
-          kh[j] = packed_row ? f16r(kivi_hat(unpack_code(kr, c, d.bits), kcs[j], a.dt)) : f16_bits_to_f32(wrow[c]);
-          vh[j] = f16r(kivi_hat(unpack_code(vr, c, d.bits), vs, a.dt));
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) {
-          const int c = lane + 32 * j;
-          const int g = c / d.gsize;
-          const float sk = read_scale(a.cache.k_scale, srow + g, d.scale_mode, mk);
-          const float sv = read_scale(a.cache.v_scale, srow + g, d.scale_mode, mv);
-          kh[j] = f16r(__fmul_rn(static_cast<float>(unpack_code(kr, c, d.bits)), sk));
-          vh[j] = f16r(__fmul_rn(static_cast<float>(unpack_code(vr, c, d.bits)), sv));
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < QN; ++i) {
-        float acc = 0.f;
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) acc = fmaf(kh[j], q[i][j], acc);
-        const float sc = __fmul_rn(warp_sum(acc), a.sf);
-        if (lane == 0) Srow[i * sstride + p * kPage + t] = sc;
-        const float mn = fmaxf(m[i], sc);
-        const float corr = expf(m[i] - mn);  // m = -inf on the first token -> 0
-        const float e = expf(sc - mn);
-        l[i] = l[i] * corr + e;
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) o[i][j] = fmaf(o[i][j], corr, e * vh[j]);
-        m[i] = mn;
-      }
-    }
-  }
-
-  // merge the 4 warps
-  __shared__ float sm_m[4][QN], sm_l[4][QN];
-  __shared__ float sm_o[4][QN][DPL * 32];
-  if (lane == 0) {
-#pragma unroll
-    for (int i = 0; i < QN; ++i) { sm_m[warp][i] = m[i]; sm_l[warp][i] = l[i]; }
-  }
-#pragma unroll
-  for (int i = 0; i < QN; ++i)
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) sm_o[warp][i][lane + 32 * j] = o[i][j];
-  __syncthreads();
-  const int64_t part = static_cast<int64_t>(bh) * a.n_splits + split;
-  for (int idx = threadIdx.x; idx < QN * D; idx += blockDim.x) {
-    const int i = idx / D, c = idx % D;
-    float M = -INFINITY;
-    for (int w = 0; w < 4; ++w) M = fmaxf(M, sm_m[w][i]);
-    float L = 0.f, O = 0.f;
-    if (M != -INFINITY) {
-      for (int w = 0; w < 4; ++w) {
-        const float f = sm_m[w][i] == -INFINITY ? 0.f : expf(sm_m[w][i] - M);
-        L += sm_l[w][i] * f;
-        O += sm_o[w][i][c] * f;
-      }
-    }
-    a.po[(part * QN + i) * D + c] = O;
-    if (c == 0) {
-      a.pm[part * QN + i] = M;
-      a.pl[part * QN + i] = L;
-    }
-  }
-}
-
 
 // ─────────────────────────── host launch ───────────────────────────
 struct SplitPlan {
@@ -199,8 +71,8 @@ static inline int64_t sel_stride(const carekv_config_t& c, int p_used) {
 // Split-K pass chosen for a layout.  NARROW: INT3 or INT4 / int8 scales with at most
 // 4 query heads per kv head (decode_narrow.cu, 4 CTAs per SM); WIDE: INT3 with
 // 8 query heads (decode_fast.cu, 2 CTAs per SM); both also compute q . R_K of
-// the stored K slots.  GENERIC: every other layout (the router computes the
-// slot dots itself).
+// the stored K slots.  GENERIC: every other layout (decode_generic.cu, which
+// computes them too).
 enum class Pass { GENERIC, WIDE, NARROW };
 inline Pass choose_pass(const carekv_config_t& c) {
   const int D = c.head_dim;
@@ -243,7 +115,7 @@ inline WsLayout ws_layout(const carekv_config_t& c, int seq_count, int p_used) {
   w.pl = o;     o = align256(o + n_bh * sp.n_splits * qn * 4);
   w.po = o;     o = align256(o + n_bh * sp.n_splits * qn * static_cast<int64_t>(c.head_dim) * 4);
   w.kw = o;
-  if (pass != Pass::GENERIC) o = align256(o + n_bh * qn * static_cast<int64_t>(p_used) * c.k_slots_per_page * kPage * 4);
+  o = align256(o + n_bh * qn * static_cast<int64_t>(p_used) * c.k_slots_per_page * kPage * 4);
   w.total = o;
   return w;
 }
@@ -260,10 +132,8 @@ size_t prefill_workspace_bytes(const carekv_config_t& c, int n_pos, int p_used) 
 
 template <int QN>
 static cudaError_t launch_qn(DecodeArgs& a, cudaStream_t st, int n_bh) {
-  dim3 g1(n_bh, a.n_splits);
   cudaError_t e;
   const Pass pass = a.force_generic ? Pass::GENERIC : choose_pass(a.cfg);
-  if (pass == Pass::GENERIC) a.kw = nullptr;
   if (pass == Pass::NARROW) {
     if constexpr (QN <= 4) {
       e = a.cfg.head_dim == 64 ? launch_decode_narrow<QN, 64>(a, st, n_bh)
@@ -275,9 +145,7 @@ static cudaError_t launch_qn(DecodeArgs& a, cudaStream_t st, int n_bh) {
     e = a.cfg.head_dim == 64 ? launch_decode_partial_int3<QN, 64>(a, st, n_bh)
                              : launch_decode_partial_int3<QN, 128>(a, st, n_bh);
   } else {
-    if (a.cfg.head_dim == 64) decode_partial_kernel<QN, 2><<<g1, 128, 0, st>>>(a);
-    else decode_partial_kernel<QN, 4><<<g1, 128, 0, st>>>(a);
-    e = cudaGetLastError();
+    e = launch_decode_generic<QN>(a, st, n_bh);
   }
   if (e != cudaSuccess) return e;
   return launch_route<QN>(a, st, n_bh);
@@ -407,12 +275,12 @@ int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, in
   a.pm = reinterpret_cast<float*>(w + wl.pm);
   a.pl = reinterpret_cast<float*>(w + wl.pl);
   a.po = reinterpret_cast<float*>(w + wl.po);
-  // q . R_K is precomputed by the narrow and wide passes whenever live
+  // q . R_K is precomputed by the split-K pass whenever live
   // combined_kvscore scoring may read it: K slots stored and K residuals
   // part of the route
   const bool live_k = rp.kind != CAREKV_KIND_NONE && rp.kind != CAREKV_KIND_V && rp.kscore_live &&
                       cfg.k_slots_per_page > 0;
-  a.kw = (choose_pass(cfg) != Pass::GENERIC && live_k) ? reinterpret_cast<float*>(w + wl.kw) : nullptr;
+  a.kw = live_k ? reinterpret_cast<float*>(w + wl.kw) : nullptr;
   a.s_perm = 0;
   a.dq_keys[0] = i3_key2(0, 0);
   a.dq_keys[1] = i3_key2(3, 3);

@@ -31,6 +31,9 @@ cudaError_t launch_append(const carekv_config_t& cfg, const carekv_cache_t& cach
                           const float* sketch_proj, int may_fill, int in_H, cudaStream_t st);
 cudaError_t launch_kivi_k(const void* x, void* out, int64_t n, int T, int D, int bits, int dt, cudaStream_t st);
 cudaError_t launch_kivi_v(const void* x, void* out, int64_t rows, int D, int bits, int dt, cudaStream_t st);
+struct DecodeArgs;
+template <int QN>
+cudaError_t launch_decode_generic(DecodeArgs& a, cudaStream_t st, int n_bh);
 int decode_attention(const carekv_config_t& cfg, const carekv_cache_t& cache, int layer, const void* q,
                      void* out, int dtype, int seq_begin, int seq_count, int p_used,
                      const carekv_route_params_t& rp, void* ws, size_t ws_bytes, const float* sketch_proj,

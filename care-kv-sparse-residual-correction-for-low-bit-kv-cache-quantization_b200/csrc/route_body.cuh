@@ -1461,9 +1461,10 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
     }
     if (ill) {
       // direct form: A V and A of every valid token outside the selected K
-      // pages (a page bitmap in the staging area, free after the rounds)
-      uint32_t* kbits = reinterpret_cast<uint32_t*>(sm.stg);
+      // pages (a page bitmap at the end of the staging area, free after the
+      // rounds)
       const int nwords = (a.p_used + 31) >> 5;
+      uint32_t* kbits = reinterpret_cast<uint32_t*>(sm.stg + kRStg) - nwords;
       __syncthreads();
       for (int x = tid; x < nwords; x += NT) kbits[x] = 0u;
       __syncthreads();
@@ -1472,10 +1473,10 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         if (e < KG) atomicOr(&kbits[(e / d.SK) >> 5], 1u << ((e / d.SK) & 31));
       }
       __syncthreads();
-      // Lane l decodes channels 4l .. 4l+3 of every row (one scale group):
-      // a page's weights, then 4 rows' code windows and scales at a time.
-      // Per channel the pages and rows are summed in the same order as
-      // token-serial decoding.
+      // Lane l decodes channels 4l .. 4l+3 of every row (one scale group).
+      // Warp w takes the pages p = w (mod NW) in ascending order, so per
+      // channel the pages and rows are summed in the same order whichever way
+      // the rows arrive.
       float o2[4] = {0.f, 0.f, 0.f, 0.f}, z2 = 0.f;
       const int cb = 4 * lane;                 // first channel of the lane
       const bool cl = cb < D;
@@ -1483,15 +1484,9 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       const int wsh = b0 & 31;
       const bool two = wsh + 4 * d.bits > 32;  // the 4 codes straddle a 32-bit word
       const uint32_t cmask = (1u << d.bits) - 1u, csign = 1u << (d.bits - 1);
-      for (int p = warp; p < np; p += NW) {
-        if ((kbits[p >> 5] >> (p & 31)) & 1u) continue;
-        const int64_t pg = lhp * d.P + p;
-        const int nv = a.cache.valid[pg];
-        const float vm = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
-        // token weights on lanes 0..15 (every logit row exists up to p_used)
-        const float sv = Sb[i * sst + p * kPage + tok_pos(lane & 15, a.s_perm)];
-        const float At = (lane & 15) < nv ? attw(sv, i) : 0.f;
-        // rows four at a time, each group's code windows and scales loaded at once
+      // rows of one page, four at a time (their code windows and scales
+      // fetched together): rowp(t) -> packed row, scl(t) -> its scale
+      auto acc_rows = [&](int nv, float At, auto&& rowp, auto&& scl) {
 #pragma unroll 1
         for (int t0 = 0; t0 < kPage; t0 += 4) {
           if (t0 >= nv) break;
@@ -1499,13 +1494,10 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           float vs[4];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const int64_t rw = pg * kPage + t0 + u;
-            const uint32_t* row = reinterpret_cast<const uint32_t*>(a.cache.v_codes + rw * R);
+            const uint32_t* row = reinterpret_cast<const uint32_t*>(rowp(t0 + u));
             wlo[u] = cl ? row[b0 >> 5] : 0u;
             whi[u] = cl && two ? row[(b0 >> 5) + 1] : 0u;
-            vs[u] = !cl ? 0.f
-                        : (d.kivi ? reinterpret_cast<const float*>(a.cache.v_scale)[rw * G]
-                                  : read_scale(a.cache.v_scale, rw * G + cb / d.gsize, d.scale_mode, vm));
+            vs[u] = cl ? scl(t0 + u) : 0.f;
           }
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
@@ -1522,12 +1514,84 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
             }
           }
         }
+      };
+      // staged: batches of pages copied into shared memory by warp 0's
+      // lanes (packed V rows, V scales, logits; one round trip per batch),
+      // a multiple of NW pages per batch to keep each warp's page order
+      const int pbytes = k_codes_b + k_sc_b + kPage * 4;
+      const int cap = min(32, (kRStg - nwords * 4) / pbytes) / NW * NW;
+      if (bulk && cap > 0) {
+        for (int p0 = 0; p0 < np; p0 += cap) {
+          const int p1 = min(np, p0 + cap);
+          __syncthreads();   // every warp is done with the previous batch
+          if (warp == 0) {
+            const int p = p0 + lane;
+            const bool take = p < p1 && !((kbits[p >> 5] >> (p & 31)) & 1u);
+            const unsigned tm = __ballot_sync(0xffffffffu, take);
+            const int64_t pg = lhp * d.P + p;
+            if (lane < cap) {
+              sm.kp_nv[lane] = take ? a.cache.valid[pg] : 0;
+              sm.kp_vm[lane] = take && d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
+            }
+            if (lane == 0) mbar_expect_tx(&sm.stg_bar, static_cast<uint32_t>(__popc(tm) * pbytes));
+            __syncwarp();
+            if (take) {
+              uint8_t* dst = sm.stg + lane * pbytes;
+              fence_proxy_async();
+              bulk_g2s(dst, a.cache.v_codes + pg * k_codes_b, k_codes_b, &sm.stg_bar);
+              bulk_g2s(dst + k_codes_b, reinterpret_cast<const uint8_t*>(a.cache.v_scale) + pg * k_sc_b, k_sc_b, &sm.stg_bar);
+              bulk_g2s(dst + k_codes_b + k_sc_b, Wb + i * sst + p * kPage, kPage * 4, &sm.stg_bar);
+            }
+          }
+          stg_failed = __syncthreads_or(!mbar_wait(&sm.stg_bar, n_batches & 1)) != 0;
+          if (stg_failed) break;
+          ++n_batches;
+          for (int x = warp; x < p1 - p0; x += NW) {
+            const int nv = sm.kp_nv[x];   // 0 for the selected pages
+            if (nv == 0) continue;
+            const uint8_t* base = sm.stg + x * pbytes;
+            const float* lg = reinterpret_cast<const float*>(base + k_codes_b + k_sc_b);
+            const float vm = sm.kp_vm[x];
+            const float At = (lane & 15) < nv ? attw(lg[tok_pos(lane & 15, a.s_perm)], i) : 0.f;
+            acc_rows(nv, At, [&](int t) { return base + t * R; },
+                     [&](int t) -> float {
+                       return d.kivi ? reinterpret_cast<const float*>(base + k_codes_b)[t * G]
+                                     : read_scale(base + k_codes_b, t * G + cb / d.gsize, d.scale_mode, vm);
+                     });
+          }
+        }
+      } else {
+        for (int p = warp; p < np; p += NW) {
+          if ((kbits[p >> 5] >> (p & 31)) & 1u) continue;
+          const int64_t pg = lhp * d.P + p;
+          const int nv = a.cache.valid[pg];
+          const float vm = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
+          // token weights on lanes 0..15 (every logit row exists up to p_used)
+          const float sv = Sb[i * sst + p * kPage + tok_pos(lane & 15, a.s_perm)];
+          const float At = (lane & 15) < nv ? attw(sv, i) : 0.f;
+          acc_rows(nv, At, [&](int t) { return a.cache.v_codes + (pg * kPage + t) * R; },
+                   [&](int t) -> float {
+                     const int64_t rw = pg * kPage + t;
+                     return d.kivi ? reinterpret_cast<const float*>(a.cache.v_scale)[rw * G]
+                                   : read_scale(a.cache.v_scale, rw * G + cb / d.gsize, d.scale_mode, vm);
+                   });
+        }
       }
       if (cl) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) sm.acc2[warp][cb + k] = o2[k];
       }
       if (lane == 0) sm.z2[warp] = z2;
+      if (stg_failed) {
+        // a staged batch did not land in time: as for the rounds above
+        if (tid == 0) {
+          atomicOr(a.cache.error_flag, 4);
+          (void)mbar_wait(&sm.stg_bar, n_batches & 1);
+        }
+        __syncthreads();
+        write_base();
+        return;
+      }
     }
     // fold the word layout's row groups onto lanes 0 .. WPR-1
     for (int o = WPR; o < 32; o <<= 1)
