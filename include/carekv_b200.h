@@ -90,7 +90,9 @@ typedef struct carekv_config {
 /* Device buffers of one arena holding `batch` sequences.  Shapes use
  * B=batch, L=num_layers, H=num_kv_heads, P=max_pages, T=page_size,
  * R=packed row bytes, G=head_dim/group_size, C=head_dim/k_channel_group,
- * NV=page_size/v_token_block, SK/SV=slot capacities. */
+ * NV=page_size/v_token_block, SK/SV=slot capacities.  Every buffer starts on
+ * a 16-byte boundary (cudaMalloc gives 256); a misaligned one is rejected
+ * with CAREKV_ERR_INVALID_ARG. */
 typedef struct carekv_cache {
     int32_t   batch;
     uint8_t  *k_codes;        /* [B][L][H][P][T][R] packed rows (quantizer.py row format) */

@@ -97,6 +97,21 @@ def test_null_cache_is_rejected_without_touching_the_gpu():
     assert lib.carekv_quantize(None, None, None, 4, 128, 3, 32, 0, None) == 1
 
 
+def test_misaligned_cache_buffer_is_rejected_without_touching_the_gpu():
+    # every buffer must start on a 16-byte boundary (the kernels stage rows
+    # and slots with 16-byte and bulk copies); the check runs before any
+    # CUDA call, so fake addresses are enough
+    pkg, lib = _lib()
+    c = _cfg(pkg).c_config()
+    cache = pkg._lib.Cache()
+    cache.batch = 1
+    names = [n for n, _ in pkg._lib.Cache._fields_ if n != "batch"]
+    for i, n in enumerate(names):
+        setattr(cache, n, 0x10000 * (i + 1))
+    cache.v_scale = 0x10000 * 100 + 8   # 8-byte aligned only: rejected before any launch or copy
+    assert lib.carekv_cache_init(ctypes.byref(c), ctypes.byref(cache), None) == 1
+
+
 def test_cache_config_validation_mirrors_reference():
     pkg = load_pkg()
     with pytest.raises(ValueError, match="scale_dtype"):
