@@ -136,6 +136,52 @@ __device__ __forceinline__ void acc_nib_word(uint32_t u, float c, float (&acc)[8
   }
 }
 
+// Direct exact form: o2 += A_t V_hat_t and z2 += A_t over the valid rows of
+// one page for the lane's channels cb .. cb+3 (lane l: cb = 4l), the rows
+// and scales of the page at `rows` / `scales` (shared or global memory,
+// indexed as the arena does: row t at t*R, scale of (t, group) at t*G +
+// group), the page's token weights on lanes 0..15 of At.  Rows are fetched
+// four at a time.
+struct DirectLane {
+  int cb, b0, wsh;
+  bool cl, two;
+  uint32_t cmask, csign;
+};
+__device__ __forceinline__ void direct_rows(const Dims& d, int dt, const DirectLane& dl, const uint8_t* rows,
+                                            const void* scales, float vm, int nv, float At, float (&o2)[4],
+                                            float& z2) {
+#pragma unroll 1
+  for (int t0 = 0; t0 < kPage; t0 += 4) {
+    if (t0 >= nv) break;
+    uint32_t wlo[4], whi[4];
+    float vs[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int t = t0 + u;
+      const uint32_t* row = reinterpret_cast<const uint32_t*>(rows + t * d.R);
+      wlo[u] = dl.cl ? row[dl.b0 >> 5] : 0u;
+      whi[u] = dl.cl && dl.two ? row[(dl.b0 >> 5) + 1] : 0u;
+      vs[u] = !dl.cl ? 0.f
+                     : (d.kivi ? reinterpret_cast<const float*>(scales)[t * d.G]
+                               : read_scale(scales, t * d.G + dl.cb / d.gsize, d.scale_mode, vm));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (t0 + u >= nv) break;
+      const float A = __shfl_sync(0xffffffffu, At, t0 + u);
+      z2 += A;
+      const uint32_t win = __funnelshift_r(wlo[u], whi[u], dl.wsh);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t cu = (win >> (k * d.bits)) & dl.cmask;
+        const int cv = static_cast<int>(cu) - static_cast<int>((cu & dl.csign) << 1);
+        const float vh = d.kivi ? f16r(kivi_hat(cv, vs[u], dt)) : f16r(__fmul_rn(static_cast<float>(cv), vs[u]));
+        o2[k] = fmaf(A, vh, o2[k]);
+      }
+    }
+  }
+}
+
 // Scratch of one routing CTA: QN queries, NW warps.
 template <int QN, int NW>
 struct RouteSmem {
@@ -1478,51 +1524,26 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       // channel the pages and rows are summed in the same order whichever way
       // the rows arrive.
       float o2[4] = {0.f, 0.f, 0.f, 0.f}, z2 = 0.f;
-      const int cb = 4 * lane;                 // first channel of the lane
-      const bool cl = cb < D;
-      const int b0 = cb * d.bits;              // its bit offset in a packed row
-      const int wsh = b0 & 31;
-      const bool two = wsh + 4 * d.bits > 32;  // the 4 codes straddle a 32-bit word
-      const uint32_t cmask = (1u << d.bits) - 1u, csign = 1u << (d.bits - 1);
-      // rows of one page, four at a time (their code windows and scales
-      // fetched together): rowp(t) -> packed row, scl(t) -> its scale
-      auto acc_rows = [&](int nv, float At, auto&& rowp, auto&& scl) {
-#pragma unroll 1
-        for (int t0 = 0; t0 < kPage; t0 += 4) {
-          if (t0 >= nv) break;
-          uint32_t wlo[4], whi[4];
-          float vs[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const uint32_t* row = reinterpret_cast<const uint32_t*>(rowp(t0 + u));
-            wlo[u] = cl ? row[b0 >> 5] : 0u;
-            whi[u] = cl && two ? row[(b0 >> 5) + 1] : 0u;
-            vs[u] = cl ? scl(t0 + u) : 0.f;
-          }
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            if (t0 + u >= nv) break;
-            const float A = __shfl_sync(0xffffffffu, At, t0 + u);
-            z2 += A;
-            const uint32_t win = __funnelshift_r(wlo[u], whi[u], wsh);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const uint32_t cu = (win >> (k * d.bits)) & cmask;
-              const int cv = static_cast<int>(cu) - static_cast<int>((cu & csign) << 1);
-              const float vh = d.kivi ? f16r(kivi_hat(cv, vs[u], a.dt)) : f16r(__fmul_rn(static_cast<float>(cv), vs[u]));
-              o2[k] = fmaf(A, vh, o2[k]);
-            }
-          }
-        }
-      };
+      DirectLane dl;
+      dl.cb = 4 * lane;                         // first channel of the lane
+      dl.cl = dl.cb < D;
+      dl.b0 = dl.cb * d.bits;                   // its bit offset in a packed row
+      dl.wsh = dl.b0 & 31;
+      dl.two = dl.wsh + 4 * d.bits > 32;        // the 4 codes straddle a 32-bit word
+      dl.cmask = (1u << d.bits) - 1u;
+      dl.csign = 1u << (d.bits - 1);
+      const int cb = dl.cb;
+      const bool cl = dl.cl;
       // staged: batches of pages copied into shared memory by warp 0's
       // lanes (packed V rows, V scales, logits; one round trip per batch),
       // a multiple of NW pages per batch to keep each warp's page order
       const int pbytes = k_codes_b + k_sc_b + kPage * 4;
       const int cap = min(32, (kRStg - nwords * 4) / pbytes) / NW * NW;
-      if (bulk && cap > 0) {
-        for (int p0 = 0; p0 < np; p0 += cap) {
-          const int p1 = min(np, p0 + cap);
+      const bool staged = bulk && cap > 0;
+      const int step = staged ? cap : NW;   // unstaged: warp w reads page p0 + w from global memory
+      for (int p0 = 0; p0 < np; p0 += step) {
+        const int p1 = min(np, p0 + step);
+        if (staged) {
           __syncthreads();   // every warp is done with the previous batch
           if (warp == 0) {
             const int p = p0 + lane;
@@ -1546,35 +1567,32 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           stg_failed = __syncthreads_or(!mbar_wait(&sm.stg_bar, n_batches & 1)) != 0;
           if (stg_failed) break;
           ++n_batches;
-          for (int x = warp; x < p1 - p0; x += NW) {
-            const int nv = sm.kp_nv[x];   // 0 for the selected pages
-            if (nv == 0) continue;
-            const uint8_t* base = sm.stg + x * pbytes;
-            const float* lg = reinterpret_cast<const float*>(base + k_codes_b + k_sc_b);
-            const float vm = sm.kp_vm[x];
-            const float At = (lane & 15) < nv ? attw(lg[tok_pos(lane & 15, a.s_perm)], i) : 0.f;
-            acc_rows(nv, At, [&](int t) { return base + t * R; },
-                     [&](int t) -> float {
-                       return d.kivi ? reinterpret_cast<const float*>(base + k_codes_b)[t * G]
-                                     : read_scale(base + k_codes_b, t * G + cb / d.gsize, d.scale_mode, vm);
-                     });
-          }
         }
-      } else {
-        for (int p = warp; p < np; p += NW) {
-          if ((kbits[p >> 5] >> (p & 31)) & 1u) continue;
-          const int64_t pg = lhp * d.P + p;
-          const int nv = a.cache.valid[pg];
-          const float vm = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
-          // token weights on lanes 0..15 (every logit row exists up to p_used)
-          const float sv = Sb[i * sst + p * kPage + tok_pos(lane & 15, a.s_perm)];
+        for (int x = warp; x < p1 - p0; x += NW) {
+          const int p = p0 + x;
+          const uint8_t* rows;
+          const uint8_t* scl;
+          int nv;
+          float vm, sv;
+          if (staged) {
+            nv = sm.kp_nv[x];   // 0 for the selected pages
+            if (nv == 0) continue;
+            rows = sm.stg + x * pbytes;
+            scl = rows + k_codes_b;
+            vm = sm.kp_vm[x];
+            sv = reinterpret_cast<const float*>(rows + k_codes_b + k_sc_b)[tok_pos(lane & 15, a.s_perm)];
+          } else {
+            if ((kbits[p >> 5] >> (p & 31)) & 1u) continue;
+            const int64_t pg = lhp * d.P + p;
+            nv = a.cache.valid[pg];
+            vm = d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
+            rows = a.cache.v_codes + pg * k_codes_b;
+            scl = reinterpret_cast<const uint8_t*>(a.cache.v_scale) + pg * k_sc_b;
+            // every logit row exists up to p_used
+            sv = Sb[i * sst + p * kPage + tok_pos(lane & 15, a.s_perm)];
+          }
           const float At = (lane & 15) < nv ? attw(sv, i) : 0.f;
-          acc_rows(nv, At, [&](int t) { return a.cache.v_codes + (pg * kPage + t) * R; },
-                   [&](int t) -> float {
-                     const int64_t rw = pg * kPage + t;
-                     return d.kivi ? reinterpret_cast<const float*>(a.cache.v_scale)[rw * G]
-                                   : read_scale(a.cache.v_scale, rw * G + cb / d.gsize, d.scale_mode, vm);
-                   });
+          direct_rows(d, a.dt, dl, rows, scl, vm, nv, At, o2, z2);
         }
       }
       if (cl) {
