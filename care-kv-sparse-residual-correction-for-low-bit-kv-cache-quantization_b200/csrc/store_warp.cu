@@ -42,6 +42,14 @@ __device__ __forceinline__ float2 unpack2(uint32_t w) {
   const __half2 h = *reinterpret_cast<const __half2*>(&w);
   return __half22float2(h);
 }
+// The larger magnitude of a lane-wise 16-bit max of |x| bits (x & 0x7fff
+// per half: magnitudes of finite fp16 / bf16 values order like their bits)
+template <int DT>
+__device__ __forceinline__ float abs_pair_max(uint32_t mu) {
+  mu = max(mu & 0xffffu, mu >> 16);
+  return DT == CAREKV_BF16 ? __uint_as_float(mu << 16) : __half2float(__ushort_as_half(static_cast<unsigned short>(mu)));
+}
+
 // (lo, hi) -> dt pair with round to nearest even (lo in the low half)
 template <int DT>
 __device__ __forceinline__ uint32_t cvt_pair(float lo, float hi) {
@@ -152,8 +160,7 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
     uint32_t mu = 0u;
 #pragma unroll
     for (int w = j * (NW / GPL); w < (j + 1) * (NW / GPL); ++w) mu = __vmaxu2(mu, x[w] & 0x7fff7fffu);
-    mu = max(mu & 0xffffu, mu >> 16);
-    m[j] = DT == CAREKV_BF16 ? __uint_as_float(mu << 16) : __half2float(__ushort_as_half(static_cast<unsigned short>(mu)));
+    m[j] = abs_pair_max<DT>(mu);
   }
   if (GSEL == 2) m[0] = fmaxf(m[0], __shfl_xor_sync(0xffffffffu, m[0], 1));
   float sc[GPL], rcp[GPL], rs[GPL];
@@ -219,7 +226,14 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
     const int j = (2 * w) / GL;
     // code = clamp(rint(dt(x / s))) (quant_code; the quotient as div_by_recip)
     const float2 qd = unpack2<DT>(cvt_pair<DT>(div_by_recip(f.x, sc[j], rcp[j]), div_by_recip(f.y, sc[j], rcp[j])));
-    const float t0 = fminf(fmaxf(rintf(qd.x), lo), hi), t1 = fminf(fmaxf(rintf(qd.y), lo), hi);
+    float t0 = rintf(qd.x), t1 = rintf(qd.y);
+    if constexpr (DT != CAREKV_BF16) {
+      // fp16 scales may be subnormal, their quotients above qmax; a bf16
+      // scale is normal (>= clamp / qmax) and within 2^-8 of max / qmax, so
+      // |x / s| <= qmax (1 + 2^-8) rounds inside [-qmax, qmax]
+      t0 = fminf(fmaxf(t0, lo), hi);
+      t1 = fminf(fmaxf(t1, lo), hi);
+    }
     // codes 2w, 2w+1 at bits BITS*e of the half row's little-endian stream;
     // t + 1.5*2^23 holds t in two's complement in its low mantissa bits
 #pragma unroll
@@ -250,14 +264,16 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
     // K channel groups of 32: CPL per lane, shared by the 16 lanes of a half
 #pragma unroll
     for (int j = 0; j < CPL; ++j) {
-      float ss = 0.f, mj = 0.f;
+      float ss = 0.f;
+      uint32_t mu = 0u;
 #pragma unroll
       for (int w = 16 * j; w < 16 * j + 16; ++w) {
         const float2 f = unpack2<DT>(x[w]);
         ss = fmaf(f.x, f.x, ss);
         ss = fmaf(f.y, f.y, ss);
-        mj = fmaxf(mj, fmaxf(fabsf(f.x), fabsf(f.y)));
+        mu = __vmaxu2(mu, x[w] & 0x7fff7fffu);
       }
+      float mj = abs_pair_max<DT>(mu);
       float ej = live ? sqrtf(ss) : 0.f;
 #pragma unroll
       for (int o = 2; o < 32; o <<= 1) {
@@ -272,14 +288,16 @@ __device__ __forceinline__ void store_half(const carekv_config_t& cfg, const car
     }
   } else {
     // V token blocks of vtb rows: lanes 2*vtb*b .. 2*vtb*(b+1)-1
-    float ss = 0.f, mv = 0.f;
+    float ss = 0.f;
+    uint32_t mu = 0u;
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
       const float2 f = unpack2<DT>(x[w]);
       ss = fmaf(f.x, f.x, ss);
       ss = fmaf(f.y, f.y, ss);
-      mv = fmaxf(mv, fmaxf(fabsf(f.x), fabsf(f.y)));
+      mu = __vmaxu2(mu, x[w] & 0x7fff7fffu);
     }
+    float mv = abs_pair_max<DT>(mu);
     ss += __shfl_xor_sync(0xffffffffu, ss, 1);
     mv = fmaxf(mv, __shfl_xor_sync(0xffffffffu, mv, 1));
     float ev = live ? sqrtf(ss) : 0.f;
