@@ -1,8 +1,9 @@
 """The router's CTA size follows its grid: 4 warps when the (sequence, kv
 head, query head) grid fills the GPU, 8 or 16 when it is small (route.cu).
-Most GPU tests run small batches (16-warp CTAs); this one also runs a batch
-of 640 routing CTAs (4-warp CTAs) and checks, for sampled sequences, the
-oracle and the same sequences routed alone in a small batch."""
+Most GPU tests run small batches (16-warp CTAs); this one also runs batches
+of 640 (4-warp CTAs) and 384 (8-warp CTAs) routing CTAs and checks, for
+sampled sequences, the oracle and the same sequences routed alone in a
+small batch."""
 
 import numpy as np
 import pytest
@@ -25,9 +26,10 @@ def pkg():
     return load_pkg()
 
 
-def test_large_and_small_route_grids_agree(pkg):
-    B, H, D, T = 20, 32, 128, 200          # 640 routing CTAs: the 4-warp form
-    sample = [0, 7, 19]                    # routed alone: 96 CTAs, the 16-warp form
+@pytest.mark.parametrize("B", [20, 12], ids=["640_ctas_4_warps", "384_ctas_8_warps"])
+def test_large_and_small_route_grids_agree(pkg, B):
+    H, D, T = 32, 128, 200
+    sample = [0, 7, B - 1]                 # routed alone: 96 CTAs, the 16-warp form
     rng = np.random.default_rng(20260)
     K = rng.standard_normal((B, H, T, D)).astype(np.float32)
     K[..., :4] *= 20.0
