@@ -361,6 +361,9 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       // kept block does not wait for the block index
       uint2 ve4 = make_uint2(0u, 0u);
       if (live && d.NV == 4) ve4 = *reinterpret_cast<const uint2*>(a.cache.v_err + pg * 4);
+      // the first V slot's block, loaded before any score store (the scores
+      // may live in global memory, and a later load would wait for them)
+      const int vb0 = live && d.SV > 0 ? a.cache.v_slot_block[pg * d.SV] : -1;
       ntok += nv;
       for (int i = 0; i < QN; ++i) {
         const float4* srow = reinterpret_cast<const float4*>(Wb + i * sst + p * kPage);
@@ -418,7 +421,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
         }
         for (int j = 0; j < d.SV; ++j) {
           const int e = p * d.SV + j;
-          const int vb = live ? a.cache.v_slot_block[pg * d.SV + j] : -1;
+          const int vb = live ? (j == 0 ? vb0 : a.cache.v_slot_block[pg * d.SV + j]) : -1;
           const int t0 = vb * d.vtb, t1 = min(t0 + d.vtb, nv);
           const bool ok = vb >= 0 && t1 > t0;
           if (i == 0) cntv += ok;
@@ -943,25 +946,46 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       float tau = sm.gv[0];
       for (int w = 1; w < NW; ++w) tau = fminf(tau, sm.gv[w]);
       if (tau >= 0.f) {
-        for (int e = lo + tid; e < hi; e += NT) {
-          const float x = row[e];
-          if (x >= tau) {
-            const int slot = atomicAdd(&sm.gcount, 1);
-            if (slot < 64) {
-              sm.gv[32 + slot] = x;
-              sm.gi[32 + slot] = e;
-            }
+        // candidates: one slot reservation per warp and pass (ballot), -0
+        // folded onto +0 so that float order is the key order
+        for (int e0 = lo; e0 < hi; e0 += NT) {
+          const int e = e0 + tid;
+          const float x = e < hi ? row[e] : -1.f;
+          const bool c = x >= tau;
+          const unsigned bc = __ballot_sync(0xffffffffu, c);
+          int slot0 = 0;
+          if (lane == 0 && bc) slot0 = atomicAdd(&sm.gcount, __popc(bc));
+          slot0 = __shfl_sync(0xffffffffu, slot0, 0);
+          const int slot = slot0 + __popc(bc & ((1u << lane) - 1u));
+          if (c && slot < 64) {
+            sm.gv[32 + slot] = __fadd_rn(x, 0.0f);
+            sm.gi[32 + slot] = e;
           }
         }
         __syncthreads();
         const int nc = sm.gcount;
         if (nc <= 64) {
-          if (warp == 0) {
-            uint64_t k0 = rkey(lane < nc ? sm.gv[32 + lane] : -2.f, lane < nc ? sm.gi[32 + lane] : 0x7fffffff);
-            uint64_t k1 = rkey(lane + 32 < nc ? sm.gv[64 + lane] : -2.f, lane + 32 < nc ? sm.gi[64 + lane] : 0x7fffffff);
-            rsort64(k0, k1, lane);
-            publish(i, rkey_score(k0), rkey_index(k0), k);
+          // rank of every candidate under (score desc, index asc): the
+          // candidates ahead of it; ranks below k are published in rank order
+          // (all candidates score >= tau >= 0)
+          const int base = sm.nsel[i];
+          const int n = min(nc, k);
+          if (tid < nc) {
+            const float x = sm.gv[32 + tid];
+            const int ix = sm.gi[32 + tid];
+            int r = 0;
+            for (int j = 0; j < nc; ++j) {
+              const float y = sm.gv[32 + j];
+              r += (y > x || (y == x && sm.gi[32 + j] < ix)) ? 1 : 0;
+            }
+            if (r < n) {
+              gsel_base[i * a.sel_stride + 1 + base + r] = ix;
+              if (base + r < kRSel) sm.sel[i][base + r] = ix;
+              if (ix < KG) sm.any_k = 1;
+            }
           }
+          __syncthreads();
+          if (tid == 0) sm.nsel[i] = base + n;
           __syncthreads();
           return;
         }
@@ -1203,10 +1227,15 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       for (int o = 16; o > 0; o >>= 1) m |= __shfl_xor_sync(0xffffffffu, m, o);
       return m;
     };
+    // statistics of the exact pass over the selected K pages' valid tokens,
+    // per thread: the largest ds, sum of A (e^ds - 1), the token count
+    float ex_mx = -INFINITY, ex_zs = 0.f;
+    int ex_cov = 0;
     // tables of the round [r0, r1): selected K pages (the first selection of
     // a page leads it) and V slots with the per-item scalars (one round
-    // trip), then wK per (selected K page, token)
-    auto load_round = [&](int r0, int r1, bool count_reads) {
+    // trip), then wK per (selected K page, token), with the exact pass's
+    // statistics when `stats` (the logit and q.R_K loads in one round trip)
+    auto load_round = [&](int r0, int r1, bool count_reads, bool stats) {
       if (warp == 0) {
         const int nsel = r1 - r0;
         if (multi) {
@@ -1263,7 +1292,19 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       __syncthreads();
       for (int x = tid; x < sm.nkp * kPage; x += NT) {
         const int u = x / kPage, t = x % kPage;
-        sm.ds[u][t] = wk_of(sm.kp_page[u], sm.kp_mask[u], t);
+        const int p = sm.kp_page[u], nv = sm.kp_nv[u];
+        // the logit is loaded before wK is summed
+        const float sv = (stats && !PF && t < nv) ? Sb[i * sst + p * kPage + tok_pos(t, a.s_perm)] : 0.f;
+        const float wk = wk_of(p, sm.kp_mask[u], t);
+        sm.ds[u][t] = wk;
+        if (stats) {
+          if (t == 0) ex_cov += nv;
+          if (t < nv) {
+            const float dsv = __fdiv_rn(wk, a.sqrt_d);
+            ex_mx = fmaxf(ex_mx, dsv);
+            if (!PF) ex_zs += attw(sv, i) * expm1f(dsv);
+          }
+        }
       }
       __syncthreads();
     };
@@ -1284,33 +1325,37 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
     float mshift = 0.f;
     bool ill = false;
     if (exact) {
-      float mx = -INFINITY, zs = 0.f;
-      int covered = 0, nkp_all = 0;
+      int nkp_all = 0;
+      ex_mx = -INFINITY;
+      ex_zs = 0.f;
+      ex_cov = 0;
       for (int q0 = 0; q0 < n_all;) {
         const int q1 = round_end(q0);
-        load_round(q0, q1, !multi);
-        if (warp == 0) {
-          for (int u = 0; u < sm.nkp; ++u) {
-            const int nv = sm.kp_nv[u];
-            covered += nv;
-            if (lane < nv) {
-              const float dsv = __fdiv_rn(sm.ds[u][lane], a.sqrt_d);
-              mx = fmaxf(mx, dsv);
-              if (!PF) zs += attw(Sb[i * sst + sm.kp_page[u] * kPage + tok_pos(lane, a.s_perm)], i) * expm1f(dsv);
-            }
-          }
-        }
+        load_round(q0, q1, !multi, true);
         nkp_all += sm.nkp;
         q0 = q1;
         __syncthreads();
       }
-      if (warp == 0) {
-        mx = warp_max(mx);
-        zs = warp_sum(zs);
-        if (lane == 0) {
-          sm.mshift = (nkp_all == 0) ? 0.f : (covered >= ntot ? mx : fmaxf(mx, 0.f));
-          sm.ill = !PF && nkp_all > 0 && covered < ntot && 1.f + zs < kIllNorm;
+      // CTA-wide: max and sum over the warps (the sum only decides the
+      // conditioning test), token count
+      const float wmx = warp_max(ex_mx), wzs = warp_sum(ex_zs);
+      const int wcov = __reduce_add_sync(0xffffffffu, ex_cov);
+      if (lane == 0) {
+        sm.gv[warp] = wmx;
+        sm.gv[NW + warp] = wzs;
+        sm.gi[warp] = wcov;
+      }
+      __syncthreads();
+      if (tid == 0) {
+        float mx = sm.gv[0], zs = sm.gv[NW];
+        int covered = sm.gi[0];
+        for (int w = 1; w < NW; ++w) {
+          mx = fmaxf(mx, sm.gv[w]);
+          zs += sm.gv[NW + w];
+          covered += sm.gi[w];
         }
+        sm.mshift = (nkp_all == 0) ? 0.f : (covered >= ntot ? mx : fmaxf(mx, 0.f));
+        sm.ill = !PF && nkp_all > 0 && covered < ntot && 1.f + zs < kIllNorm;
       }
       __syncthreads();
       mshift = sm.mshift;
@@ -1323,7 +1368,7 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
     for (int r0 = 0; r0 < n_all;) {
       const int r1 = round_end(r0);
       if (r0 > 0) __syncthreads();   // every warp is done with the previous round's tables
-      if (multi || !exact) load_round(r0, r1, true);   // a single round is loaded by the exact pass
+      if (multi || !exact) load_round(r0, r1, true, false);   // a single round is loaded by the exact pass
       const int nkp = sm.nkp, nvs = sm.nvs, nit = nkp + nvs;
       // batch plan: item -> staging offset, batch boundaries
       if (tid == 0) {
