@@ -1370,21 +1370,40 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       if (r0 > 0) __syncthreads();   // every warp is done with the previous round's tables
       if (multi || !exact) load_round(r0, r1, true, false);   // a single round is loaded by the exact pass
       const int nkp = sm.nkp, nvs = sm.nvs, nit = nkp + nvs;
-      // batch plan: item -> staging offset, batch boundaries
-      if (tid == 0) {
-        int off = 0, nb = 0;
-        sm.bnd[0] = 0;
-        for (int it = 0; it < nit; ++it) {
-          const int sz = it < nkp ? k_item_b : v_item_b;
-          if (off + sz > kRStg) {
-            sm.bnd[++nb] = it;
-            off = 0;
-          }
-          sm.ioff[it] = off;
-          off += sz;
+      // batch plan: item -> staging offset, batch boundaries.  A round holds
+      // at most kRSel = 32 items: warp 0 scans their sizes, and when they fit
+      // one batch the offsets are the exclusive prefix sums; else lane 0
+      // packs them greedily in order
+      if (warp == 0) {
+        const int sz = lane < nit ? (lane < nkp ? k_item_b : v_item_b) : 0;
+        int incl = sz;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
         }
-        sm.bnd[++nb] = nit;
-        sm.nb = nb;
+        if (__shfl_sync(0xffffffffu, incl, 31) <= kRStg) {
+          if (lane < nit) sm.ioff[lane] = incl - sz;
+          if (lane == 0) {
+            sm.bnd[0] = 0;
+            sm.bnd[1] = nit;
+            sm.nb = 1;
+          }
+        } else if (lane == 0) {
+          int off = 0, nb = 0;
+          sm.bnd[0] = 0;
+          for (int it = 0; it < nit; ++it) {
+            const int isz = it < nkp ? k_item_b : v_item_b;
+            if (off + isz > kRStg) {
+              sm.bnd[++nb] = it;
+              off = 0;
+            }
+            sm.ioff[it] = off;
+            off += isz;
+          }
+          sm.bnd[++nb] = nit;
+          sm.nb = nb;
+        }
       }
       __syncthreads();
       const int nb = sm.nb;
