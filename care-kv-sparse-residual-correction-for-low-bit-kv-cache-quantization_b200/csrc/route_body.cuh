@@ -137,27 +137,32 @@ __device__ __forceinline__ void acc_nib_word(uint32_t u, float c, float (&acc)[8
 }
 
 // Direct exact form: o2 += A_t V_hat_t and z2 += A_t over the valid rows of
-// one page for the lane's channels cb .. cb+3 (lane l: cb = 4l), the rows
-// and scales of the page at `rows` / `scales` (shared or global memory,
-// indexed as the arena does: row t at t*R, scale of (t, group) at t*G +
-// group), the page's token weights on lanes 0..15 of At.  Rows are fetched
-// four at a time.
+// one page for the lane's channels cb .. cb+3, the rows and scales of the
+// page at `rows` / `scales` (shared or global memory, indexed as the arena
+// does: row t at t*R, scale of (t, group) at t*G + group), the page's token
+// weights on lanes 0..15 of At.  Lane l holds channels 4l of every row; with
+// D = 64 the two half-warps take alternate rows instead (lane l: channels
+// 4 (l mod 16) of the rows of parity l / 16; the caller adds the halves).
+// Rows are fetched four at a time per warp.
 struct DirectLane {
   int cb, b0, wsh;
+  int rs, half;   // rows side by side in the warp (1 or 2), the lane's row parity
   bool cl, two;
   uint32_t cmask, csign;
 };
-__device__ __forceinline__ void direct_rows(const Dims& d, int dt, const DirectLane& dl, const uint8_t* rows,
-                                            const void* scales, float vm, int nv, float At, float (&o2)[4],
-                                            float& z2) {
+template <int RS>
+__device__ __forceinline__ void direct_rows_rs(const Dims& d, int dt, const DirectLane& dl, const uint8_t* rows,
+                                               const void* scales, float vm, int nv, float At, float (&o2)[4],
+                                               float& z2) {
+  constexpr int NU = 4 / RS;   // rows of the lane per step of 4
 #pragma unroll 1
   for (int t0 = 0; t0 < kPage; t0 += 4) {
     if (t0 >= nv) break;
-    uint32_t wlo[4], whi[4];
-    float vs[4];
+    uint32_t wlo[NU], whi[NU];
+    float vs[NU];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int t = t0 + u;
+    for (int u = 0; u < NU; ++u) {
+      const int t = t0 + u * RS + dl.half;
       const uint32_t* row = reinterpret_cast<const uint32_t*>(rows + t * d.R);
       wlo[u] = dl.cl ? row[dl.b0 >> 5] : 0u;
       whi[u] = dl.cl && dl.two ? row[(dl.b0 >> 5) + 1] : 0u;
@@ -166,20 +171,31 @@ __device__ __forceinline__ void direct_rows(const Dims& d, int dt, const DirectL
                                : read_scale(scales, t * d.G + dl.cb / d.gsize, d.scale_mode, vm));
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      if (t0 + u >= nv) break;
-      const float A = __shfl_sync(0xffffffffu, At, t0 + u);
-      z2 += A;
-      const uint32_t win = __funnelshift_r(wlo[u], whi[u], dl.wsh);
+    for (int u = 0; u < NU; ++u) {
+      // the warp's first row of the step is valid (uniform); the lane's row
+      // may lie past the page's rows
+      if (t0 + u * RS >= nv) break;
+      const int t = t0 + u * RS + dl.half;
+      const float A = __shfl_sync(0xffffffffu, At, t);
+      if (t < nv) {
+        z2 += A;
+        const uint32_t win = __funnelshift_r(wlo[u], whi[u], dl.wsh);
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const uint32_t cu = (win >> (k * d.bits)) & dl.cmask;
-        const int cv = static_cast<int>(cu) - static_cast<int>((cu & dl.csign) << 1);
-        const float vh = d.kivi ? f16r(kivi_hat(cv, vs[u], dt)) : f16r(__fmul_rn(static_cast<float>(cv), vs[u]));
-        o2[k] = fmaf(A, vh, o2[k]);
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t cu = (win >> (k * d.bits)) & dl.cmask;
+          const int cv = static_cast<int>(cu) - static_cast<int>((cu & dl.csign) << 1);
+          const float vh = d.kivi ? f16r(kivi_hat(cv, vs[u], dt)) : f16r(__fmul_rn(static_cast<float>(cv), vs[u]));
+          o2[k] = fmaf(A, vh, o2[k]);
+        }
       }
     }
   }
+}
+__device__ __forceinline__ void direct_rows(const Dims& d, int dt, const DirectLane& dl, const uint8_t* rows,
+                                            const void* scales, float vm, int nv, float At, float (&o2)[4],
+                                            float& z2) {
+  if (dl.rs == 2) direct_rows_rs<2>(d, dt, dl, rows, scales, vm, nv, At, o2, z2);
+  else direct_rows_rs<1>(d, dt, dl, rows, scales, vm, nv, At, o2, z2);
 }
 
 // Scratch of one routing CTA: QN queries, NW warps.
@@ -1589,7 +1605,9 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
       // the rows arrive.
       float o2[4] = {0.f, 0.f, 0.f, 0.f}, z2 = 0.f;
       DirectLane dl;
-      dl.cb = 4 * lane;                         // first channel of the lane
+      dl.rs = D == 64 ? 2 : 1;                  // D = 64: half-warps on alternate rows
+      dl.half = dl.rs == 2 ? lane >> 4 : 0;
+      dl.cb = 4 * (dl.rs == 2 ? (lane & 15) : lane);   // first channel of the lane
       dl.cl = dl.cb < D;
       dl.b0 = dl.cb * d.bits;                   // its bit offset in a packed row
       dl.wsh = dl.b0 & 31;
@@ -1659,7 +1677,12 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
           direct_rows(d, a.dt, dl, rows, scl, vm, nv, At, o2, z2);
         }
       }
-      if (cl) {
+      if (dl.rs == 2) {   // the odd rows' sums (lanes 16..31) onto lanes 0..15
+#pragma unroll
+        for (int k = 0; k < 4; ++k) o2[k] += __shfl_down_sync(0xffffffffu, o2[k], 16);
+        z2 += __shfl_down_sync(0xffffffffu, z2, 16);
+      }
+      if (cl && dl.half == 0) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) sm.acc2[warp][cb + k] = o2[k];
       }
