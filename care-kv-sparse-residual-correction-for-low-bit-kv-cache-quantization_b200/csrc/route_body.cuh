@@ -1632,10 +1632,6 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
             const bool take = p < p1 && !((kbits[p >> 5] >> (p & 31)) & 1u);
             const unsigned tm = __ballot_sync(0xffffffffu, take);
             const int64_t pg = lhp * d.P + p;
-            if (lane < cap) {
-              sm.kp_nv[lane] = take ? a.cache.valid[pg] : 0;
-              sm.kp_vm[lane] = take && d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
-            }
             if (lane == 0) mbar_expect_tx(&sm.stg_bar, static_cast<uint32_t>(__popc(tm) * pbytes));
             __syncwarp();
             if (take) {
@@ -1644,6 +1640,11 @@ __device__ __forceinline__ void route_body(const DecodeArgs& a, int bh, RouteSme
               bulk_g2s(dst, a.cache.v_codes + pg * k_codes_b, k_codes_b, &sm.stg_bar);
               bulk_g2s(dst + k_codes_b, reinterpret_cast<const uint8_t*>(a.cache.v_scale) + pg * k_sc_b, k_sc_b, &sm.stg_bar);
               bulk_g2s(dst + k_codes_b + k_sc_b, Wb + i * sst + p * kPage, kPage * 4, &sm.stg_bar);
+            }
+            // the pages' row counts and masters while the copies are in flight
+            if (lane < cap) {
+              sm.kp_nv[lane] = take ? a.cache.valid[pg] : 0;
+              sm.kp_vm[lane] = take && d.scale_mode == CAREKV_SCALE_INT8 ? f16_bits_to_f32(a.cache.v_master[pg]) : 0.f;
             }
           }
           stg_failed = __syncthreads_or(!mbar_wait(&sm.stg_bar, n_batches & 1)) != 0;
